@@ -1,0 +1,111 @@
+/* qlin: B200 (sm_100a) fused dequantize-and-GEMM linears for quantized diffusion-model weights.
+ *
+ * C ABI of libqlin.so.  Plain pointers and sizes only; every pointer named "device" is CUDA device
+ * memory on the current device, and `stream` is a cudaStream_t (NULL = legacy default stream).
+ *
+ * Ownership: the caller allocates every input, output and workspace.  The library never
+ * allocates, keeps no per-call state and launches only on `stream` (stream-ordered, re-entrant).
+ * Errors: functions return QLIN_OK or a positive qlin_status; qlin_last_error() gives a message
+ * for the calling thread.  QLIN_EDECLINE means "unsupported input, use the stock path" and
+ * mirrors the reference's `mps.linear(layer, x) -> None` decline
+ * (docs/research/2026-10-03-gguf-on-metal.md:117 in roblennon/mac-kernels-public).
+ *
+ * Dtype codes: 0 f32, 1 f16, 2 bf16, 3 int8, 4 uint8, 5 int32, 6 float8_e4m3fn.
+ * Shapes: X [m, k] row-major with row pitch ldx elements; Y [m, n] row-major with pitch ldy.
+ * Y = X . W^T (+ bias) with W [n, k].
+ */
+#ifndef QLIN_H_
+#define QLIN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum qlin_status {
+  QLIN_OK = 0,
+  QLIN_EDECLINE = 1, /* unsupported dtype / format / alignment: caller takes the stock path   */
+  QLIN_EINVAL = 2,   /* inconsistent arguments (sizes, null pointers, workspace too small)    */
+  QLIN_ECUDA = 3,    /* a CUDA runtime call failed; see qlin_last_error()                     */
+  QLIN_ETIMEOUT = 4  /* a kernel gave up a bounded wait (reported by qlin_device_status)      */
+};
+
+enum qlin_dtype { QLIN_F32 = 0, QLIN_F16 = 1, QLIN_BF16 = 2, QLIN_I8 = 3, QLIN_U8 = 4, QLIN_I32 = 5, QLIN_E4M3 = 6 };
+
+/* ggml type ids accepted by the GGUF entry points. */
+enum qlin_gguf_type { QLIN_Q4_0 = 2, QLIN_Q8_0 = 8, QLIN_Q4_K = 12, QLIN_Q6_K = 14, QLIN_IQ4_NL = 20 };
+
+const char* qlin_version(void);
+const char* qlin_last_error(void);
+
+/* Reads the device-side status word of the current device (synchronizes the device).  Returns
+ * 0 when no kernel timed out, else QLIN_ETIMEOUT and *where = (block << 8) | site.  reset != 0
+ * clears it. */
+int qlin_device_status(int reset, uint32_t* where);
+
+/* ------------------------------------------------------------------------------------------
+ * INT8 ConvRot weight-only linear.
+ * Replaces comfy-kitchen `int8_linear(x, qdata, scale, bias, out_dtype, convrot, convrot_groupsize)`
+ * (call sites bench/bench_ck01_int8.py:57, bench/bench_lora_fused_rank.py:39; contract
+ * docs/upstream/comfy-kitchen-mps-backend.md:44-56 in the reference).
+ *   q      int8 [n, k] row-major, stored already rotated (W_rot = W . H^T per group)
+ *   scale  per-output-channel scale [n] (dtype f32 or f16)
+ *   bias   [n] (f16 / f32 / bf16) or NULL
+ *   convrot_group  0 (no rotation) or the Hadamard block size: 32 / 128 (Sylvester) or 64 / 256
+ *                  (the reference's H4 Kronecker construction, modal/weight_error_app.py:90-98)
+ * x dtype f16 / bf16 / f32; y dtype f16 / bf16 / f32.  Requires k % 16 == 0 (and % group).
+ * ------------------------------------------------------------------------------------------ */
+size_t qlin_int8_linear_workspace(int64_t m, int64_t n, int64_t k);
+int qlin_int8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q, int64_t n,
+                     const void* scale, int scale_dtype, const void* bias, int bias_dtype, int convrot_group,
+                     void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * GGUF block-format linear (Q4_0, Q8_0, Q4_K, Q6_K, IQ4_NL).
+ * Replaces comfy-kitchen `gguf_linear(x, weight, qtype, shape, bias, out_dtype)` and its decode
+ * helpers `_decode` / `gguf_row_exp_<type>` (bench/bench_gguf_linear.py:120-127; design
+ * docs/research/2026-10-03-gguf-on-metal.md:83-97 in the reference).
+ *
+ * qlin_gguf_repack turns raw ggml blocks [n rows of k/QK blocks] into the resident stage layout
+ * (one time per weight) and writes the per-row exponents e (row_exp, length padded_n = n rounded
+ * up to 128).  The linear decodes each value in fp32 exactly as gguf-py 0.19.0, multiplies it by
+ * 2^-e and rounds once to fp16 for the tensor cores; the epilogue restores 2^e, adds bias in fp32
+ * and rounds once to the output dtype.  Requires k to be a whole number of blocks per row.
+ * ------------------------------------------------------------------------------------------ */
+int qlin_gguf_repacked_bytes(int qtype, int64_t n, int64_t k, size_t* bytes, int64_t* padded_n);
+int qlin_gguf_repack(const void* raw, int qtype, int64_t n, int64_t k, void* packed, size_t packed_bytes,
+                     int32_t* row_exp, int64_t row_exp_len, void* stream);
+size_t qlin_gguf_linear_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, int64_t ldx);
+int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                     const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
+                     int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Decode-only, bit-exact with gguf-py 0.19.0 (f32 out; f16 / bf16 out = that value rounded once).
+ * Blocks are indexed by flat element, so rows may straddle blocks.  Replaces comfy-kitchen
+ * `dequantize_gguf(weight, qtype, shape, out_dtype)` (docs/upstream/comfy-kitchen-mps-followups.md:43). */
+int qlin_gguf_dequantize(const void* raw, int qtype, int64_t n, int64_t k, void* out, int out_dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Activation prologues (exposed for tests and for callers that reuse one prologue across
+ * several linears sharing an input).
+ *   qlin_prologue_f16: optional block-Hadamard rotation, then per-row power-of-two scaling
+ *     (row max mapped into [2^14, 2^15)) and one rounding to fp16.  out [m, ldo] fp16,
+ *     row_exp[m] = f (the row was multiplied by 2^-f).
+ *   qlin_quantize_rows_int8: optional rotation, then quantize_int8_rowwise semantics
+ *     (modal/weight_error_app.py:109-115): scale = max(absmax/127, 1e-30) in fp32, quotient
+ *     formed in x's dtype, round half-to-even, clamp [-128, 127].  out int8 [m, ldo], scale[m] f32.
+ *     perm != 0 writes each group of 8 columns in the order 0,2,4,6,1,3,5,7 (the operand order of
+ *     the packed-weight kernels).
+ * ------------------------------------------------------------------------------------------ */
+int qlin_prologue_f16(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, int rotate_group, void* out,
+                      int64_t ldo, int32_t* row_exp, void* stream);
+int qlin_quantize_rows_int8(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, int rotate_group,
+                            int perm, int8_t* out, int64_t ldo, float* scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLIN_H_ */

@@ -1,0 +1,319 @@
+// The C ABI (include/qlin.h): argument checks, workspace carving, prologue + GEMM sequencing.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/qlin.h"
+#include "qlin_internal.h"
+#include "qlin_ptx.cuh"
+
+namespace qlin {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Workspace carving: consecutive 256-byte aligned regions.
+struct Carver {
+  uint8_t* base;
+  size_t cap, off = 0;
+  void* take(size_t bytes) {
+    void* p = base ? base + off : nullptr;
+    off = align256(off + bytes);
+    return p;
+  }
+};
+
+static bool is_float_dtype(int d) { return d == QLIN_F32 || d == QLIN_F16 || d == QLIN_BF16; }
+static int bias_kind_of(const void* bias, int dt) {
+  if (bias == nullptr) return 0;
+  return dt == QLIN_F16 ? 1 : dt == QLIN_F32 ? 2 : dt == QLIN_BF16 ? 3 : -1;
+}
+static int out_kind_of(int dt) { return dt == QLIN_F32 ? 0 : dt == QLIN_F16 ? 1 : dt == QLIN_BF16 ? 2 : -1; }
+
+static int check_cuda(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return QLIN_ECUDA;
+  }
+  return QLIN_OK;
+}
+
+static int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// Activation operand for the f16 family: fp16 [m, kp] + row exponents, produced by the prologue
+// unless x is already a suitable fp16 tensor and no rotation is requested.
+struct F16Operand {
+  const void* x;
+  long long ldx;
+  const int32_t* row_exp;
+};
+
+static size_t f16_operand_bytes(int64_t m, int64_t k) {
+  return align256((size_t)m * round_up(k, 64) * 2) + align256((size_t)m * 4);
+}
+
+static int make_f16_operand(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, int group, Carver& ws,
+                            cudaStream_t stream, F16Operand* out) {
+  const bool direct = x_dtype == QLIN_F16 && group == 0 && ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  if (direct) {
+    out->x = x;
+    out->ldx = ldx;
+    out->row_exp = nullptr;
+    return QLIN_OK;
+  }
+  const int64_t kp = round_up(k, 64);
+  void* xr = ws.take((size_t)m * kp * 2);
+  int32_t* rexp = reinterpret_cast<int32_t*>(ws.take((size_t)m * 4));
+  if (ws.off > ws.cap) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  if (launch_prologue(x, x_dtype, ldx, (int)m, (int)k, (int)kp, group, 0, xr, rexp, nullptr, 0, stream) != 0) {
+    set_error("unsupported rotation group %d", group);
+    return QLIN_EDECLINE;
+  }
+  int rc = check_cuda("prologue launch");
+  if (rc) return rc;
+  out->x = xr;
+  out->ldx = kp;
+  out->row_exp = rexp;
+  return QLIN_OK;
+}
+
+static bool valid_group(int g) { return g == 0 || g == 32 || g == 64 || g == 128 || g == 256; }
+
+}  // namespace qlin
+
+using namespace qlin;
+
+extern "C" {
+
+const char* qlin_version(void) { return "qlin 0.1 (sm_100a, tcgen05)"; }
+
+const char* qlin_last_error(void) { return g_err; }
+
+int qlin_device_status(int reset, uint32_t* where) {
+  void* p = device_status_ptr();
+  if (p == nullptr) {
+    set_error("device status word unavailable");
+    return QLIN_ECUDA;
+  }
+  DeviceStatus st{};
+  if (cudaMemcpy(&st, p, sizeof(st), cudaMemcpyDeviceToHost) != cudaSuccess) return check_cuda("status read");
+  if (where) *where = st.where;
+  if (reset) {
+    DeviceStatus z{};
+    if (cudaMemcpy(p, &z, sizeof(z), cudaMemcpyHostToDevice) != cudaSuccess) return check_cuda("status reset");
+  }
+  return st.timed_out ? QLIN_ETIMEOUT : QLIN_OK;
+}
+
+// ------------------------------------------------------------------------------------------ INT8
+size_t qlin_int8_linear_workspace(int64_t m, int64_t n, int64_t k) {
+  return f16_operand_bytes(m, k) + align256(f16_gemm_partial_bytes((int)m, (int)n, (int)k, 0, 0));
+}
+
+int qlin_int8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q, int64_t n,
+                     const void* scale, int scale_dtype, const void* bias, int bias_dtype, int convrot_group, void* y,
+                     int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (m < 0 || n < 0 || k < 0 || ldx < k || ldy < n) {
+    set_error("bad sizes m=%lld n=%lld k=%lld ldx=%lld ldy=%lld", (long long)m, (long long)n, (long long)k,
+              (long long)ldx, (long long)ldy);
+    return QLIN_EINVAL;
+  }
+  if (m == 0 || n == 0) return QLIN_OK;
+  if (!is_float_dtype(x_dtype) || out_kind_of(y_dtype) < 0 || (scale_dtype != QLIN_F16 && scale_dtype != QLIN_F32) ||
+      bias_kind_of(bias, bias_dtype) < 0) {
+    set_error("unsupported dtype combination");
+    return QLIN_EDECLINE;
+  }
+  if (k == 0 || k % 16 != 0 || !valid_group(convrot_group) || (convrot_group && k % convrot_group) ||
+      m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) {
+    set_error("unsupported shape: k=%lld group=%d (k must be a multiple of 16 and of the group)", (long long)k,
+              convrot_group);
+    return QLIN_EDECLINE;
+  }
+  if (x == nullptr || q == nullptr || scale == nullptr || y == nullptr || (reinterpret_cast<uintptr_t>(q) & 15)) {
+    set_error("null or misaligned pointer (q needs 16-byte alignment)");
+    return QLIN_EINVAL;
+  }
+  Carver ws{reinterpret_cast<uint8_t*>(workspace), workspace_bytes};
+  F16Operand op;
+  int rc = make_f16_operand(x, x_dtype, m, k, ldx, convrot_group, ws, stream, &op);
+  if (rc) return rc;
+  F16GemmArgs a{};
+  a.fmt = WF_INT8;
+  a.x = op.x;
+  a.ldx = op.ldx;
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.w = q;
+  a.w_row_exp = nullptr;
+  a.col_scale = scale;
+  a.col_scale_kind = scale_dtype == QLIN_F16 ? CS_F16 : CS_F32;
+  a.x_row_exp = op.row_exp;
+  a.bias = bias;
+  a.bias_kind = bias_kind_of(bias, bias_dtype);
+  a.y = y;
+  a.y_dtype = out_kind_of(y_dtype);
+  a.ldy = ldy;
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, 0, 0);
+  a.partial = reinterpret_cast<float*>(ws.take(pb));
+  a.partial_bytes = pb;
+  if (ws.off > ws.cap && pb > 0) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  return run_f16_gemm(a, stream);
+}
+
+// ------------------------------------------------------------------------------------------ GGUF
+int qlin_gguf_repacked_bytes(int qtype, int64_t n, int64_t k, size_t* bytes, int64_t* padded_n) {
+  const uint32_t sb = gguf_stage_bytes(qtype, nullptr, nullptr);
+  if (sb == 0) {
+    set_error("unsupported GGUF type %d", qtype);
+    return QLIN_EDECLINE;
+  }
+  const int qk = gguf_block_values(qtype);
+  if (n < 0 || k <= 0 || k % qk != 0) {
+    set_error("k=%lld is not a whole number of %d-value blocks", (long long)k, qk);
+    return QLIN_EDECLINE;
+  }
+  const int64_t nt = (n + 127) / 128;
+  if (bytes) *bytes = (size_t)nt * ((k + 63) / 64) * sb;
+  if (padded_n) *padded_n = nt * 128;
+  return QLIN_OK;
+}
+
+int qlin_gguf_repack(const void* raw, int qtype, int64_t n, int64_t k, void* packed, size_t packed_bytes,
+                     int32_t* row_exp, int64_t row_exp_len, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  size_t need = 0;
+  int64_t npad = 0;
+  int rc = qlin_gguf_repacked_bytes(qtype, n, k, &need, &npad);
+  if (rc) return rc;
+  if (packed_bytes < need || row_exp_len < npad || raw == nullptr || packed == nullptr || row_exp == nullptr ||
+      (reinterpret_cast<uintptr_t>(packed) & 15)) {
+    set_error("repack buffers: need %zu bytes (16-byte aligned) and %lld exponents", need, (long long)npad);
+    return QLIN_EINVAL;
+  }
+  int P = 0, S = 0;
+  const uint32_t sb = gguf_stage_bytes(qtype, &P, &S);
+  launch_gguf_repack(reinterpret_cast<const uint8_t*>(raw), qtype, (int)n, (int)k, (int)((k + 63) / 64),
+                     (int)(npad / 128), reinterpret_cast<uint8_t*>(packed), sb, P, S, stream);
+  launch_gguf_row_exp(reinterpret_cast<const uint8_t*>(raw), qtype, (int)n, (int)k, (int)npad, row_exp, stream);
+  return check_cuda("gguf repack launch");
+}
+
+size_t qlin_gguf_linear_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, int64_t ldx) {
+  (void)x_dtype;
+  (void)ldx;
+  return f16_operand_bytes(m, k) + align256(f16_gemm_partial_bytes((int)m, (int)n, (int)k, 0, 0));
+}
+
+int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                     const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
+                     int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (m < 0 || n < 0 || k < 0 || ldx < k || ldy < n) {
+    set_error("bad sizes");
+    return QLIN_EINVAL;
+  }
+  if (m == 0 || n == 0) return QLIN_OK;
+  if (gguf_stage_bytes(qtype, nullptr, nullptr) == 0 || k % gguf_block_values(qtype) != 0 ||
+      !is_float_dtype(x_dtype) || out_kind_of(y_dtype) < 0 || bias_kind_of(bias, bias_dtype) < 0) {
+    set_error("unsupported GGUF type/shape/dtype (type %d, k %lld)", qtype, (long long)k);
+    return QLIN_EDECLINE;
+  }
+  if (x == nullptr || packed == nullptr || row_exp == nullptr || y == nullptr) {
+    set_error("null pointer");
+    return QLIN_EINVAL;
+  }
+  Carver ws{reinterpret_cast<uint8_t*>(workspace), workspace_bytes};
+  F16Operand op;
+  int rc = make_f16_operand(x, x_dtype, m, k, ldx, 0, ws, stream, &op);
+  if (rc) return rc;
+  F16GemmArgs a{};
+  a.fmt = qtype;
+  a.x = op.x;
+  a.ldx = op.ldx;
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.w = packed;
+  a.w_row_exp = row_exp;
+  a.col_scale = nullptr;
+  a.col_scale_kind = CS_EXP2;
+  a.x_row_exp = op.row_exp;
+  a.bias = bias;
+  a.bias_kind = bias_kind_of(bias, bias_dtype);
+  a.y = y;
+  a.y_dtype = out_kind_of(y_dtype);
+  a.ldy = ldy;
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, 0, 0);
+  a.partial = reinterpret_cast<float*>(ws.take(pb));
+  a.partial_bytes = pb;
+  if (ws.off > ws.cap && pb > 0) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  return run_f16_gemm(a, stream);
+}
+
+int qlin_gguf_dequantize(const void* raw, int qtype, int64_t n, int64_t k, void* out, int out_dtype, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  const int qk = gguf_block_values(qtype);
+  if (qk == 0 || out_kind_of(out_dtype) < 0) {
+    set_error("unsupported GGUF type %d or out dtype %d", qtype, out_dtype);
+    return QLIN_EDECLINE;
+  }
+  if (n < 0 || k < 0 || (n * k) % qk != 0) {
+    set_error("n*k must be a whole number of blocks");
+    return QLIN_EINVAL;
+  }
+  if (n * k == 0) return QLIN_OK;
+  launch_gguf_dequant(reinterpret_cast<const uint8_t*>(raw), qtype, (long long)(n * k), out, out_kind_of(out_dtype),
+                      stream);
+  return check_cuda("gguf dequantize launch");
+}
+
+// ------------------------------------------------------------------------------------------ prologues
+int qlin_prologue_f16(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, int rotate_group, void* out,
+                      int64_t ldo, int32_t* row_exp, void* stream_) {
+  if (!is_float_dtype(x_dtype) || !valid_group(rotate_group) || (rotate_group && k % rotate_group) || ldo < k) {
+    set_error("unsupported prologue arguments");
+    return QLIN_EDECLINE;
+  }
+  if (m == 0) return QLIN_OK;
+  launch_prologue(x, x_dtype, ldx, (int)m, (int)k, (int)ldo, rotate_group, 0, out, row_exp, nullptr, 0,
+                  reinterpret_cast<cudaStream_t>(stream_));
+  return check_cuda("prologue launch");
+}
+
+int qlin_quantize_rows_int8(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, int rotate_group, int perm,
+                            int8_t* out, int64_t ldo, float* scale, void* stream_) {
+  if (!is_float_dtype(x_dtype) || !valid_group(rotate_group) || (rotate_group && k % rotate_group) || ldo < k ||
+      (perm && ldo % 8)) {
+    set_error("unsupported quantize arguments");
+    return QLIN_EDECLINE;
+  }
+  if (m == 0) return QLIN_OK;
+  launch_prologue(x, x_dtype, ldx, (int)m, (int)k, (int)ldo, rotate_group, 1, out, nullptr, scale, perm,
+                  reinterpret_cast<cudaStream_t>(stream_));
+  return check_cuda("quantize launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,474 @@
+// Bandwidth-bound helper kernels around the tensor-core GEMMs:
+//   * activation prologues: optional block-Hadamard (ConvRot) rotation, then either
+//       - a per-row power-of-two normalization and one rounding to fp16 (kind::f16 operand), or
+//       - per-token absmax INT8 quantization with the reference's rounding (kind::i8 operand);
+//   * GGUF decode-only (bit-exact with gguf-py 0.19.0), the one-time repack into pipeline
+//     stages, and the per-row exponent pass;
+//   * the deterministic split-K reduction + epilogue.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "qlin_decode.cuh"
+#include "qlin_internal.h"
+
+namespace qlin {
+
+// ---------------------------------------------------------------------------------------------
+// Block-Hadamard rotation in a warp: a block of G = 32*E values, lane l holding elements
+// l*E .. l*E+E-1.  y[p] = sum_i H[p][i] x[i] / sqrt(G) with
+//   kind 0: Sylvester H2 (x) ... (x) H2 (H2 = [[1,1],[1,-1]]), any power of two;
+//   kind 1: H4 (x) ... (x) H4 with the regular H4 = J - 2*antidiag (the reference's
+//           build_hadamard, modal/weight_error_app.py:90-98), powers of four.
+// ---------------------------------------------------------------------------------------------
+template <int E>
+__device__ __forceinline__ float partner(const float (&x)[E], int e, int mask) {
+  constexpr int LE = (E == 1) ? 0 : (E == 2) ? 1 : (E == 4) ? 2 : 3;
+  const int rm = mask & (E - 1);
+  const int lm = mask >> LE;
+  float v = x[e ^ rm];
+  if (lm) v = __shfl_xor_sync(0xffffffffu, v, lm);
+  return v;
+}
+
+template <int E>
+__device__ __forceinline__ void block_hadamard(float (&x)[E], int kind, int lane) {
+  constexpr int LE = (E == 1) ? 0 : (E == 2) ? 1 : (E == 4) ? 2 : 3;
+  constexpr int LG = LE + 5;
+  if (kind == 0) {
+#pragma unroll
+    for (int t = 0; t < LG; ++t) {
+      float y[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int i = lane * E + e;
+        const float p = partner<E>(x, e, 1 << t);
+        y[e] = (i >> t) & 1 ? __fsub_rn(p, x[e]) : __fadd_rn(x[e], p);
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) x[e] = y[e];
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < LG / 2; ++t) {
+      float y[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float p1 = partner<E>(x, e, 1 << (2 * t));
+        const float p2 = partner<E>(x, e, 2 << (2 * t));
+        const float p3 = partner<E>(x, e, 3 << (2 * t));
+        const float s = __fadd_rn(__fadd_rn(x[e], p1), __fadd_rn(p2, p3));
+        y[e] = __fsub_rn(s, __fmul_rn(2.f, p3));
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) x[e] = y[e];
+    }
+  }
+  const float norm = (E == 1) ? 0.17677669529663687f : (E == 2) ? 0.125f : (E == 4) ? 0.08838834764831845f : 0.0625f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = __fmul_rn(x[e], norm);
+}
+
+__device__ __forceinline__ float load_x(const void* x, int dtype, long long idx) {
+  if (dtype == 1) return __half2float(reinterpret_cast<const __half*>(x)[idx]);
+  if (dtype == 2) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[idx]);
+  return reinterpret_cast<const float*>(x)[idx];
+}
+
+// Loads E consecutive elements of row `row` starting at column c (zeros past K).
+template <int E>
+__device__ __forceinline__ void load_vals(const void* x, int dtype, long long ldx, int row, int c, int K, float (&v)[E]) {
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = (c + e < K) ? load_x(x, dtype, (long long)row * ldx + c + e) : 0.f;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = (l < (int)(blockDim.x >> 5)) ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (l == 0) red[32] = v;
+  }
+  __syncthreads();
+  const float r = red[32];
+  __syncthreads();
+  return r;
+}
+
+// Rounds a float to the input dtype (fp16 / bf16 / fp32) and back.
+__device__ __forceinline__ float round_to(float v, int dtype) {
+  if (dtype == 1) return __half2float(__float2half_rn(v));
+  if (dtype == 2) return __bfloat162float(__float2bfloat16_rn(v));
+  return v;
+}
+
+// Pass structure shared by both prologues: walk the row in warp-sized blocks of G = 32*E values
+// (rotated when rotate != 0), two passes (max, then write).
+template <int E, int MODE>  // MODE 0: fp16 normalize; MODE 1: int8 per-token quantize
+__global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ x, int x_dtype, long long ldx, int M,
+                                                        int K, int Kp, int rotate_kind, int rotate,
+                                                        void* __restrict__ out, int32_t* __restrict__ row_exp,
+                                                        float* __restrict__ row_scale, int perm) {
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  constexpr int G = 32 * E;
+  const int nblk = (Kp + G - 1) / G;
+  float amax = 0.f;
+  for (int b = warp; b < nblk; b += nwarps) {
+    float v[E];
+    const int c = b * G + lane * E;
+    load_vals<E>(x, x_dtype, ldx, row, c, K, v);
+    if (rotate) block_hadamard<E>(v, rotate_kind, lane);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float t = (MODE == 1) ? round_to(v[e], x_dtype) : v[e];
+      amax = fmaxf(amax, fabsf(t));
+    }
+  }
+  amax = block_max(amax, red);
+  if (MODE == 0) {
+    int f = 0;
+    if (amax > 0.f && amax <= 3.402823466e38f) {
+      int ex;
+      frexpf(amax, &ex);
+      f = ex - 15;
+    }
+    if (threadIdx.x == 0) row_exp[row] = f;
+    __half* o = reinterpret_cast<__half*>(out) + (long long)row * Kp;
+    for (int b = warp; b < nblk; b += nwarps) {
+      float v[E];
+      const int c = b * G + lane * E;
+      load_vals<E>(x, x_dtype, ldx, row, c, K, v);
+      if (rotate) block_hadamard<E>(v, rotate_kind, lane);
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (c + e < Kp) o[c + e] = __float2half_rn(ldexpf(v[e], -f));
+    }
+  } else {
+    // quantize_int8_rowwise semantics (modal/weight_error_app.py:109-115) in the input dtype.
+    float scale = fmaxf(__fdiv_rn(amax, 127.f), 1e-30f);
+    float s = round_to(scale, x_dtype);
+    if (s == 0.f) s = (x_dtype == 1) ? 6.103515625e-05f : 1.17549435e-38f;
+    if (threadIdx.x == 0) row_scale[row] = scale;
+    int8_t* o = reinterpret_cast<int8_t*>(out) + (long long)row * Kp;
+    for (int b = warp; b < nblk; b += nwarps) {
+      float v[E];
+      const int c = b * G + lane * E;
+      load_vals<E>(x, x_dtype, ldx, row, c, K, v);
+      if (rotate) block_hadamard<E>(v, rotate_kind, lane);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float xv = round_to(v[e], x_dtype);
+        float qv = rintf(round_to(__fdiv_rn(xv, s), x_dtype));
+        qv = fminf(fmaxf(qv, -128.f), 127.f);
+        const int col = c + e;
+        // perm: within each group of 8 columns, even columns first (0,2,4,6,1,3,5,7)
+        const int dst = perm ? ((col & ~7) | ((col & 1) ? 4 + ((col & 7) >> 1) : ((col & 7) >> 1))) : col;
+        if (col < Kp) o[dst] = (col < K) ? static_cast<int8_t>(qv) : 0;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// GGUF decode-only: one thread per 4 consecutive values of the flat tensor (blocks are indexed
+// by flat element, so rows may straddle blocks).  fp32 results are bit-exact with gguf-py.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float f16_at(const uint8_t* p) {
+  return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+
+__device__ float gguf_value(const uint8_t* __restrict__ raw, int qtype, long long idx) {
+  switch (qtype) {
+    case GGUF_Q4_0:
+    case GGUF_IQ4_NL: {
+      const uint8_t* b = raw + (idx / 32) * 18;
+      const int j = (int)(idx % 32);
+      const uint8_t byte = b[2 + (j & 15)];
+      const int nib = (j < 16) ? (byte & 0xF) : (byte >> 4);
+      const float d = f16_at(b);
+      if (qtype == GGUF_Q4_0) return __fmul_rn(d, (float)(nib - 8));
+      constexpr int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+      return __fmul_rn(d, (float)kv[nib]);
+    }
+    case GGUF_Q8_0: {
+      const uint8_t* b = raw + (idx / 32) * 34;
+      return __fmul_rn((float)(int8_t)b[2 + idx % 32], f16_at(b));
+    }
+    case GGUF_Q4_K: {
+      const uint8_t* b = raw + (idx / 256) * 144;
+      const int j = (int)(idx % 256);
+      const int sub = j / 32;
+      const uint8_t* sc = b + 4;
+      int s, m;
+      if (sub < 4) {
+        s = sc[sub] & 0x3F;
+        m = sc[sub + 4] & 0x3F;
+      } else {
+        s = (sc[sub + 4] & 0x0F) | ((sc[sub - 4] >> 2) & 0x30);
+        m = (sc[sub + 4] >> 4) | ((sc[sub] >> 2) & 0x30);
+      }
+      const uint8_t byte = b[16 + (sub / 2) * 32 + (j % 32)];
+      const int q = (sub & 1) ? (byte >> 4) : (byte & 0xF);
+      const float ds = __fmul_rn(f16_at(b), (float)s);
+      const float dm = __fmul_rn(f16_at(b + 2), (float)m);
+      return __fsub_rn(__fmul_rn(ds, (float)q), dm);
+    }
+    case GGUF_Q6_K: {
+      const uint8_t* b = raw + (idx / 256) * 210;
+      const int j = (int)(idx % 256);
+      const int h = j / 128, r = j % 128;
+      const int lo = (b[64 * h + (r % 64)] >> (4 * (r / 64))) & 0xF;
+      const int hi = (b[128 + 32 * h + (r % 32)] >> (2 * (r / 32))) & 0x3;
+      const int q = (lo | (hi << 4)) - 32;
+      const float ds = __fmul_rn(f16_at(b + 208), (float)(int8_t)b[192 + j / 16]);
+      return __fmul_rn(ds, (float)q);
+    }
+  }
+  return 0.f;
+}
+
+__global__ void gguf_dequant_kernel(const uint8_t* __restrict__ raw, int qtype, long long total, void* __restrict__ out,
+                                    int out_dtype) {
+  const long long i0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  for (int t = 0; t < 4; ++t) {
+    const long long i = i0 + t;
+    if (i >= total) return;
+    const float v = gguf_value(raw, qtype, i);
+    if (out_dtype == 0) reinterpret_cast<float*>(out)[i] = v;
+    else if (out_dtype == 1) reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
+    else reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// Per-row exponent: e = frexp(bound).exp - 15 with bound an upper bound on |w| over the row's
+// blocks read from block scales only (float64, as the oracle computes it).
+__global__ void gguf_row_exp_kernel(const uint8_t* __restrict__ raw, int qtype, int N, int K, int n_pad,
+                                    int32_t* __restrict__ row_exp) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n_pad) return;
+  double bound = 0.0;
+  if (row < N) {
+    const int qk = (qtype == GGUF_Q4_K || qtype == GGUF_Q6_K) ? 256 : 32;
+    const int ts = qtype == GGUF_Q8_0 ? 34 : qtype == GGUF_Q4_K ? 144 : qtype == GGUF_Q6_K ? 210 : 18;
+    const int nb = K / qk;
+    const uint8_t* r = raw + (long long)row * nb * ts;
+    for (int blk = lane; blk < nb; blk += 32) {
+      const uint8_t* b = r + (long long)blk * ts;
+      double v = 0.0;
+      if (qtype == GGUF_Q4_0) v = fabs((double)f16_at(b)) * 8.0;
+      else if (qtype == GGUF_Q8_0) v = fabs((double)f16_at(b)) * 128.0;
+      else if (qtype == GGUF_IQ4_NL) v = fabs((double)f16_at(b)) * 127.0;
+      else if (qtype == GGUF_Q4_K) {
+        const double d = fabs((double)f16_at(b)), dmin = fabs((double)f16_at(b + 2));
+        const uint8_t* sc = b + 4;
+        for (int sub = 0; sub < 8; ++sub) {
+          int s, m;
+          if (sub < 4) {
+            s = sc[sub] & 0x3F;
+            m = sc[sub + 4] & 0x3F;
+          } else {
+            s = (sc[sub + 4] & 0x0F) | ((sc[sub - 4] >> 2) & 0x30);
+            m = (sc[sub + 4] >> 4) | ((sc[sub] >> 2) & 0x30);
+          }
+          v = fmax(v, d * s * 15.0 + dmin * m);
+        }
+      } else if (qtype == GGUF_Q6_K) {
+        const double d = fabs((double)f16_at(b + 208));
+        for (int t = 0; t < 16; ++t) v = fmax(v, d * fabs((double)(int8_t)b[192 + t]) * 32.0);
+      }
+      bound = fmax(bound, v);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) bound = fmax(bound, __shfl_xor_sync(0xffffffffu, bound, o));
+  if (lane == 0) {
+    int e = 0;
+    if (bound > 0.0 && bound < 1e300) {
+      int ex;
+      frexp(bound, &ex);
+      e = ex - 15;
+    }
+    row_exp[row] = e;
+  }
+}
+
+// One-time repack of raw GGUF rows into the pipeline-stage layout documented in qlin_decode.cuh.
+// grid = (num_k_stages, n_tiles), block = 128 (one thread per weight row of the tile).
+__global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, int N, int K, int num_k_stages,
+                                   uint8_t* __restrict__ out, uint32_t stage_bytes, int P, int S) {
+  const int kst = blockIdx.x, nt = blockIdx.y, r = threadIdx.x;
+  const int n = nt * 128 + r;
+  uint8_t* st = out + ((size_t)nt * num_k_stages + kst) * stage_bytes;
+  uint8_t payload[64];
+  uint8_t side[8];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) payload[i] = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) side[i] = 0;
+  const int k0 = kst * 64;
+  if (n < N && k0 < K) {
+    if (qtype == GGUF_Q8_0 || qtype == GGUF_Q4_0 || qtype == GGUF_IQ4_NL) {
+      const int ts = qtype == GGUF_Q8_0 ? 34 : 18;
+      const int qsb = ts - 2;
+      const uint8_t* row = raw + (long long)n * (K / 32) * ts;
+      for (int blk = 0; blk < 2; ++blk) {
+        const int kb = k0 / 32 + blk;
+        if (kb * 32 >= K) break;
+        const uint8_t* b = row + (long long)kb * ts;
+        side[2 * blk] = b[0];
+        side[2 * blk + 1] = b[1];
+        for (int i = 0; i < qsb; ++i) payload[blk * qsb + i] = b[2 + i];
+      }
+    } else if (qtype == GGUF_Q4_K) {
+      const uint8_t* b = raw + ((long long)n * (K / 256) + k0 / 256) * 144;
+      const int c = (k0 % 256) / 64;  // sub-blocks 2c, 2c+1
+      for (int i = 0; i < 32; ++i) payload[i] = b[16 + c * 32 + i];
+      const uint8_t* sc = b + 4;
+      int s[2], m[2];
+      for (int t = 0; t < 2; ++t) {
+        const int sub = 2 * c + t;
+        if (sub < 4) {
+          s[t] = sc[sub] & 0x3F;
+          m[t] = sc[sub + 4] & 0x3F;
+        } else {
+          s[t] = (sc[sub + 4] & 0x0F) | ((sc[sub - 4] >> 2) & 0x30);
+          m[t] = (sc[sub + 4] >> 4) | ((sc[sub] >> 2) & 0x30);
+        }
+      }
+      side[0] = b[0];
+      side[1] = b[1];
+      side[2] = b[2];
+      side[3] = b[3];
+      side[4] = (uint8_t)s[0];
+      side[5] = (uint8_t)s[1];
+      side[6] = (uint8_t)m[0];
+      side[7] = (uint8_t)m[1];
+    } else if (qtype == GGUF_Q6_K) {
+      const uint8_t* b = raw + ((long long)n * (K / 256) + k0 / 256) * 210;
+      const int base = k0 % 256;  // stage covers values base .. base+63 of the superblock
+      uint8_t v[64];
+      for (int i = 0; i < 64; ++i) {
+        const int j = base + i;
+        const int h = j / 128, rr = j % 128;
+        const int lo = (b[64 * h + (rr % 64)] >> (4 * (rr / 64))) & 0xF;
+        const int hi = (b[128 + 32 * h + (rr % 32)] >> (2 * (rr / 32))) & 0x3;
+        v[i] = (uint8_t)(lo | (hi << 4));
+      }
+      for (int i = 0; i < 32; ++i) payload[i] = (uint8_t)((v[i] & 0xF) | ((v[i + 32] & 0xF) << 4));
+      for (int i = 0; i < 16; ++i)
+        payload[32 + i] = (uint8_t)((v[i] >> 4) | ((v[i + 16] >> 4) << 2) | ((v[i + 32] >> 4) << 4) | ((v[i + 48] >> 4) << 6));
+      for (int t = 0; t < 4; ++t) side[t] = b[192 + base / 16 + t];
+      side[4] = b[208];
+      side[5] = b[209];
+    }
+  }
+  for (int j = 0; j < P; ++j)
+    for (int i = 0; i < 16; ++i) st[(j * 128 + r) * 16 + i] = payload[j * 16 + i];
+  for (int i = 0; i < S; ++i) st[128 * 16 * P + r * S + i] = side[i];
+}
+
+// Split-K: y[m,n] = (sum_s partial[s][m][n]) * colscale[n] * 2^f[m] + bias[n], summed in split
+// order (deterministic).
+__global__ void splitk_finalize_kernel(const float* __restrict__ partial, int splits, int M, int N,
+                                       const void* col_scale, int col_scale_kind, const int32_t* w_row_exp,
+                                       const int32_t* x_row_exp, const float* x_row_scale, const void* bias,
+                                       int bias_kind, void* y, int y_dtype, long long ldy) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)M * N) return;
+  const int m = (int)(i / N), n = (int)(i % N);
+  float acc = 0.f;
+  for (int s = 0; s < splits; ++s) acc = __fadd_rn(acc, partial[(long long)s * M * N + i]);
+  float cs = 1.f;
+  if (col_scale_kind == 1) cs = __half2float(reinterpret_cast<const __half*>(col_scale)[n]);
+  else if (col_scale_kind == 2) cs = reinterpret_cast<const float*>(col_scale)[n];
+  else if (col_scale_kind == 3) cs = exp2i(w_row_exp[n]);
+  float o = __fmul_rn(acc, cs);
+  if (x_row_exp != nullptr) o = __fmul_rn(o, exp2i(x_row_exp[m]));
+  if (x_row_scale != nullptr) o = __fmul_rn(o, x_row_scale[m]);
+  float b = 0.f;
+  if (bias_kind == 1) b = __half2float(reinterpret_cast<const __half*>(bias)[n]);
+  else if (bias_kind == 2) b = reinterpret_cast<const float*>(bias)[n];
+  else if (bias_kind == 3) b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
+  o = __fadd_rn(o, b);
+  const long long oi = (long long)m * ldy + n;
+  if (y_dtype == 1) reinterpret_cast<__half*>(y)[oi] = __float2half_rn(o);
+  else if (y_dtype == 2) reinterpret_cast<__nv_bfloat16*>(y)[oi] = __float2bfloat16_rn(o);
+  else reinterpret_cast<float*>(y)[oi] = o;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------------------------
+template <int E, int MODE>
+static void launch_prologue_e(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int kind, int rotate,
+                              void* out, int32_t* row_exp, float* row_scale, int perm, cudaStream_t stream) {
+  prologue_kernel<E, MODE>
+      <<<M, 256, 0, stream>>>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm);
+}
+
+int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int group, int mode, void* out,
+                    int32_t* row_exp, float* row_scale, int perm, cudaStream_t stream) {
+  if (M == 0) return 0;
+  const int rotate = group > 0;
+  int E = 8, kind = 0;
+  if (rotate) {
+    switch (group) {
+      case 32: E = 1; kind = 0; break;
+      case 64: E = 2; kind = 1; break;
+      case 128: E = 4; kind = 0; break;
+      case 256: E = 8; kind = 1; break;
+      default: return -1;
+    }
+  }
+#define QLIN_PRO(EE)                                                                                       \
+  do {                                                                                                     \
+    if (mode == 0) launch_prologue_e<EE, 0>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, stream); \
+    else launch_prologue_e<EE, 1>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, stream); \
+  } while (0)
+  switch (E) {
+    case 1: QLIN_PRO(1); break;
+    case 2: QLIN_PRO(2); break;
+    case 4: QLIN_PRO(4); break;
+    default: QLIN_PRO(8); break;
+  }
+#undef QLIN_PRO
+  return 0;
+}
+
+void launch_gguf_dequant(const uint8_t* raw, int qtype, long long total, void* out, int out_dtype, cudaStream_t s) {
+  if (total == 0) return;
+  const long long threads = (total + 3) / 4;
+  gguf_dequant_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(raw, qtype, total, out, out_dtype);
+}
+
+void launch_gguf_row_exp(const uint8_t* raw, int qtype, int N, int K, int n_pad, int32_t* row_exp, cudaStream_t s) {
+  if (n_pad == 0) return;
+  gguf_row_exp_kernel<<<(n_pad + 7) / 8, 256, 0, s>>>(raw, qtype, N, K, n_pad, row_exp);
+}
+
+void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_stages, int n_tiles, uint8_t* out,
+                        uint32_t stage_bytes, int P, int S, cudaStream_t s) {
+  if (num_k_stages == 0 || n_tiles == 0) return;
+  dim3 grid(num_k_stages, n_tiles);
+  gguf_repack_kernel<<<grid, 128, 0, s>>>(raw, qtype, N, K, num_k_stages, out, stage_bytes, P, S);
+}
+
+void launch_splitk_finalize(const float* partial, int splits, int M, int N, const void* col_scale, int cs_kind,
+                            const int32_t* w_row_exp, const int32_t* x_row_exp, const float* x_row_scale,
+                            const void* bias, int bias_kind, void* y, int y_dtype, long long ldy, cudaStream_t s) {
+  const long long total = (long long)M * N;
+  if (total == 0) return;
+  splitk_finalize_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+      partial, splits, M, N, col_scale, cs_kind, w_row_exp, x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy);
+}
+
+}  // namespace qlin

@@ -1,0 +1,207 @@
+// Per-format weight decoders.  Each decoder turns one pipeline stage of packed weights in
+// shared memory into the tensor-core A operand for one weight row (one TMEM lane):
+//   * f16 family (kind::f16): 64 K-values -> 32 words of packed fp16 pairs (even k in the low half)
+//   * i8 family (kind::i8):  128 K-values -> 32 words of packed int8 quads (k%4 = byte index)
+//
+// Stage layouts in shared memory (and, for repacked formats, in global memory):
+//   INT8 (raw [N,K] int8 via a 2-D TMA box {64 B, 128 rows}, 64-byte swizzle):
+//     row r, 16-byte chunk j at r*64 + 16*(j ^ ((r >> 1) & 3)).
+//   Repacked GGUF stage ("plane" layout): P chunks of 16 bytes per row stored chunk-major,
+//     [P][128 rows][16 B], followed by a side record of S bytes per row, [128 rows][S B].
+//     Q8_0   P=4 (qs of two blocks)                     S=4 (d0, d1 fp16)
+//     Q4_0   P=2 (qs of two blocks, ggml nibble order)   S=4 (d0, d1 fp16)
+//     IQ4_NL P=2 (as Q4_0)                               S=4
+//     Q4_K   P=2 (the 32-byte qs chunk of sub-blocks 2c, 2c+1)  S=8 (d, dmin fp16, sc0, sc1, m0, m1 u8)
+//     Q6_K   P=3 (32 B low nibbles: v[i] | v[i+32]<<4; 16 B high pairs: v[i], v[i+16], v[i+32],
+//            v[i+48] at bits 0,2,4,6)                  S=8 (sc0..sc3 int8, d fp16, pad)
+//   W4 nibbles (raw [N,K/2] via TMA box {64 B, 128 rows}, 64-byte swizzle): 128 values per stage.
+//   W6 planar (kitchen layout): low-nibble plane box {64 B, 128 rows} followed by the 2-bit plane
+//     box {32 B, 128 rows}, both 64-/32-byte swizzled.
+//
+// GGUF values are computed in fp32 in the operation order of gguf-py 0.19.0 (bit-exact), then
+// scaled by the row's power of two 2^-e (exact) and rounded once to fp16.
+#pragma once
+#include "qlin_ptx.cuh"
+
+namespace qlin {
+
+enum GgufType : int { GGUF_Q4_0 = 2, GGUF_Q8_0 = 8, GGUF_Q4_K = 12, GGUF_Q6_K = 14, GGUF_IQ4_NL = 20 };
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// Four signed bytes -> two words of packed fp16 pairs, exactly: 0x64XX is the fp16 1024 + XX,
+// so (byte ^ 0x80) placed under 0x64 and minus 1152 is the signed value.
+__device__ __forceinline__ void s8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t a = prmt(u, 0x64646464u, 0x5140u);
+  const uint32_t b = prmt(u, 0x64646464u, 0x7362u);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+  __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
+  __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
+  lo = *reinterpret_cast<uint32_t*>(&ha);
+  hi = *reinterpret_cast<uint32_t*>(&hb);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);  // a -> low half
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float exp2i(int e) {  // 2^e for -126 <= e <= 127
+  return __int_as_float((e + 127) << 23);
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFF)));
+}
+
+// ---------------------------------------------------------------------------------------------
+// f16 family (64 values per stage)
+// ---------------------------------------------------------------------------------------------
+struct DecInt8 {
+  static constexpr int kP = 4;  // informational: 64 bytes per row
+  static constexpr uint32_t kStageBytes = 128 * 64;
+  static constexpr bool kTma = true;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float /*row_scale*/, uint32_t (&out)[32]) {
+    const uint8_t* row = st + r * 64;
+    const int sw = (r >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(row + ((j ^ sw) << 4));
+      s8x4_to_f16x4(v.x, out[8 * j + 0], out[8 * j + 1]);
+      s8x4_to_f16x4(v.y, out[8 * j + 2], out[8 * j + 3]);
+      s8x4_to_f16x4(v.z, out[8 * j + 4], out[8 * j + 5]);
+      s8x4_to_f16x4(v.w, out[8 * j + 6], out[8 * j + 7]);
+    }
+  }
+};
+
+template <int P, int S>
+struct PlaneStage {
+  static constexpr uint32_t kStageBytes = 128 * (16 * P + S);
+  __device__ __forceinline__ static uint4 chunk(const uint8_t* st, int j, int r) {
+    return *reinterpret_cast<const uint4*>(st + (j * 128 + r) * 16);
+  }
+  __device__ __forceinline__ static const uint8_t* side(const uint8_t* st, int r) {
+    return st + 128 * 16 * P + r * S;
+  }
+};
+
+// v = d * q for int8 q (exact in fp32), times 2^-e, rounded to fp16.
+struct DecQ8_0 : PlaneStage<4, 4> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(side(st, r));
+    const float d0 = half_bits_to_float(dd) * rscale;
+    const float d1 = half_bits_to_float(dd >> 16) * rscale;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = chunk(st, j, r);
+      const float d = j < 2 ? d0 : d1;
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int8_t b0 = static_cast<int8_t>(w[t] & 0xFF), b1 = static_cast<int8_t>((w[t] >> 8) & 0xFF);
+        const int8_t b2 = static_cast<int8_t>((w[t] >> 16) & 0xFF), b3 = static_cast<int8_t>(w[t] >> 24);
+        out[8 * j + 2 * t + 0] = pack_f16x2(__fmul_rn((float)b0, d), __fmul_rn((float)b1, d));
+        out[8 * j + 2 * t + 1] = pack_f16x2(__fmul_rn((float)b2, d), __fmul_rn((float)b3, d));
+      }
+    }
+  }
+};
+
+// Q4_0 / IQ4_NL: block of 32 values, byte i holds value i (low nibble) and value i+16 (high).
+template <bool kNL>
+struct DecQ4Block : PlaneStage<2, 4> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static float level(uint32_t nib) {
+    if constexpr (kNL) {
+      // IQ4_NL non-linear levels (gguf/quants.py:1331), branch-free table in registers.
+      constexpr int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+      return (float)kv[nib];
+    } else {
+      return (float)((int)nib - 8);
+    }
+  }
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(side(st, r));
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const float d = half_bits_to_float(blk ? (dd >> 16) : dd) * rscale;
+      const uint4 v = chunk(st, blk, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      float vals[32];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
+        vals[i] = __fmul_rn(d, level(byte & 0xF));
+        vals[i + 16] = __fmul_rn(d, level(byte >> 4));
+      }
+#pragma unroll
+      for (int c = 0; c < 16; ++c) out[16 * blk + c] = pack_f16x2(vals[2 * c], vals[2 * c + 1]);
+    }
+  }
+};
+
+// Q4_K: w = (d*sc)*q - dmin*m per 32-value sub-block (gguf/quants.py:504-522).  The products are
+// exact in fp32, so one rounding happens in the subtraction, as in gguf-py.
+struct DecQ4_K : PlaneStage<2, 8> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint2 sd = *reinterpret_cast<const uint2*>(side(st, r));
+    const float d = half_bits_to_float(sd.x), dmin = half_bits_to_float(sd.x >> 16);
+    const float ds0 = __fmul_rn(d, (float)(sd.y & 0xFF)), ds1 = __fmul_rn(d, (float)((sd.y >> 8) & 0xFF));
+    const float dm0 = __fmul_rn(dmin, (float)((sd.y >> 16) & 0xFF)), dm1 = __fmul_rn(dmin, (float)(sd.y >> 24));
+    float vals[64];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 v = chunk(st, j, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
+        const int idx = 16 * j + i;
+        vals[idx] = __fmul_rn(__fsub_rn(__fmul_rn(ds0, (float)(byte & 0xF)), dm0), rscale);
+        vals[32 + idx] = __fmul_rn(__fsub_rn(__fmul_rn(ds1, (float)(byte >> 4)), dm1), rscale);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 32; ++c) out[c] = pack_f16x2(vals[2 * c], vals[2 * c + 1]);
+  }
+};
+
+// Q6_K: w = (d*sc)*(q-32) per 16 values (gguf/quants.py:554-572).
+struct DecQ6_K : PlaneStage<3, 8> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint2 sd = *reinterpret_cast<const uint2*>(side(st, r));
+    const float d = half_bits_to_float(sd.y);
+    float ds[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) ds[t] = __fmul_rn(d, (float)(int8_t)((sd.x >> (8 * t)) & 0xFF));
+    const uint4 l0 = chunk(st, 0, r), l1 = chunk(st, 1, r), hv = chunk(st, 2, r);
+    const uint32_t lo[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+    const uint32_t hi[4] = {hv.x, hv.y, hv.z, hv.w};
+    float vals[64];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t lb = (lo[i >> 2] >> (8 * (i & 3))) & 0xFF;
+      const int i16 = i & 15;
+      const uint32_t hb = (hi[i16 >> 2] >> (8 * (i16 & 3))) & 0xFF;
+      // value i (i<32) and value i+32
+      const uint32_t sh_a = (i < 16) ? 0 : 2;  // v[i]: i<16 -> bits 0-1, 16<=i<32 -> bits 2-3
+      const uint32_t qa = (lb & 0xF) | (((hb >> sh_a) & 3) << 4);
+      const uint32_t qb = (lb >> 4) | (((hb >> (sh_a + 4)) & 3) << 4);
+      vals[i] = __fmul_rn(__fmul_rn(ds[i >> 4], (float)((int)qa - 32)), rscale);
+      vals[i + 32] = __fmul_rn(__fmul_rn(ds[2 + (i >> 4)], (float)((int)qb - 32)), rscale);
+    }
+#pragma unroll
+    for (int c = 0; c < 32; ++c) out[c] = pack_f16x2(vals[2 * c], vals[2 * c + 1]);
+  }
+};
+
+}  // namespace qlin

@@ -1,0 +1,262 @@
+// Instantiations and host launcher of the weight-only (kind::f16) fused dequantize + GEMM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "qlin_gemm.cuh"
+#include "qlin_internal.h"
+
+namespace qlin {
+
+// Device status word written by timed-out waits in every kernel of this library.
+__device__ DeviceStatus g_status;
+
+void* device_status_ptr() {
+  // One address per device; looked up once per device with that device current.
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status) == cudaSuccess) addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && cache[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = v > 0 ? v : 148;
+  }
+  return (dev >= 0 && dev < 64) ? cache[dev] : 148;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled_t encode_fn() {
+  static PFN_encodeTiled_t fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled_t>(p);
+  });
+  return fn;
+}
+
+// 2-D tile map over a row-major matrix [rows, cols] of `elem` bytes with row pitch `pitch_bytes`.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem, uint64_t cols, uint64_t rows,
+                 uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is unavailable");
+    return 3;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || pitch_bytes % 16 != 0) {
+    set_error("TMA operand needs a 16-byte aligned base and row pitch (pitch %llu bytes)",
+              (unsigned long long)pitch_bytes);
+    return 1;
+  }
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  (void)elem;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d): cols %llu rows %llu pitch %llu box %u x %u", (int)r,
+              (unsigned long long)cols, (unsigned long long)rows, (unsigned long long)pitch_bytes, box_cols, box_rows);
+    return 3;
+  }
+  return 0;
+}
+
+uint32_t gguf_stage_bytes(int qtype, int* P, int* S) {
+  int p = 0, s = 0;
+  switch (qtype) {
+    case WF_Q8_0: p = 4; s = 4; break;
+    case WF_Q4_0:
+    case WF_IQ4_NL: p = 2; s = 4; break;
+    case WF_Q4_K: p = 2; s = 8; break;
+    case WF_Q6_K: p = 3; s = 8; break;
+    default: return 0;
+  }
+  if (P) *P = p;
+  if (S) *S = s;
+  return 128u * (16u * p + s);
+}
+
+int gguf_block_values(int qtype) {
+  switch (qtype) {
+    case WF_Q8_0: case WF_Q4_0: case WF_IQ4_NL: return 32;
+    case WF_Q4_K: case WF_Q6_K: return 256;
+    default: return 0;
+  }
+}
+
+int gguf_type_size(int qtype) {
+  switch (qtype) {
+    case WF_Q8_0: return 34;
+    case WF_Q4_0: case WF_IQ4_NL: return 18;
+    case WF_Q4_K: return 144;
+    case WF_Q6_K: return 210;
+    default: return 0;
+  }
+}
+
+void plan_f16(int M, int N, int K, int* tm_out, int* splits_out) {
+  int tm = *tm_out;
+  if (tm == 0) {
+    if (M <= 16) tm = 16;
+    else if (M <= 32) tm = 32;
+    else if (M <= 64) tm = 64;
+    else tm = 128;
+  }
+  int splits = *splits_out;
+  const int kst = (K + 63) / 64;
+  if (splits == 0) {
+    const int tiles = ((N + 127) / 128) * ((M + tm - 1) / tm);
+    const int sms = sm_count();
+    splits = 1;
+    if (tiles < sms) {
+      splits = std::max(1, sms / std::max(tiles, 1));
+      splits = std::min(splits, std::max(1, kst / 4));  // keep >= 4 stages per split
+      splits = std::min(splits, 16);
+    }
+  }
+  splits = std::max(1, std::min(splits, kst));
+  // normalize so every split has work
+  const int per = (kst + splits - 1) / splits;
+  splits = (kst + per - 1) / per;
+  *tm_out = tm;
+  *splits_out = splits;
+}
+
+size_t f16_gemm_partial_bytes(int M, int N, int K, int tm, int k_splits) {
+  plan_f16(M, N, K, &tm, &k_splits);
+  return k_splits > 1 ? (size_t)k_splits * M * N * sizeof(float) : 0;
+}
+
+template <class Dec, int TM, int STAGES>
+static int launch_one(const F16GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p,
+                      cudaStream_t stream) {
+  constexpr int smem = qgemm_f16_smem_bytes<Dec, TM, STAGES>();
+  auto kern = qgemm_f16_kernel<Dec, TM, STAGES>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(max dynamic smem %d) failed", smem);
+      return 3;
+    }
+    attr_done[dev] = true;
+  }
+  const int tiles = p.m_tiles * p.n_tiles * p.k_splits;
+  const int grid = std::min(tiles, sm_count());
+  kern<<<grid, 320, smem, stream>>>(tx, tw, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("qgemm_f16 launch failed: %s", cudaGetErrorString(e));
+    return 3;
+  }
+  (void)a;
+  return 0;
+}
+
+template <class Dec>
+static int dispatch_tm(const F16GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p,
+                       int tm, cudaStream_t stream) {
+  switch (tm) {
+    case 16: return launch_one<Dec, 16, 8>(a, tx, tw, p, stream);
+    case 32: return launch_one<Dec, 32, 8>(a, tx, tw, p, stream);
+    case 64: return launch_one<Dec, 64, 8>(a, tx, tw, p, stream);
+    case 128: return launch_one<Dec, 128, 6>(a, tx, tw, p, stream);
+    case 256: return launch_one<Dec, 256, 4>(a, tx, tw, p, stream);
+    default: set_error("unsupported token tile %d", tm); return 2;
+  }
+}
+
+int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
+  if (a.M == 0 || a.N == 0) return 0;
+  int tm = a.tm, splits = a.k_splits;
+  plan_f16(a.M, a.N, a.K, &tm, &splits);
+  GemmParams p{};
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.num_k_stages = (a.K + 63) / 64;
+  p.m_tiles = (a.M + tm - 1) / tm;
+  p.n_tiles = (a.N + 127) / 128;
+  p.k_splits = splits;
+  p.stages_per_split = (p.num_k_stages + splits - 1) / splits;
+  p.w_stages = reinterpret_cast<const uint8_t*>(a.w);
+  p.w_row_exp = a.w_row_exp;
+  p.col_scale = a.col_scale;
+  p.col_scale_kind = a.col_scale_kind;
+  p.x_row_exp = a.x_row_exp;
+  p.bias = a.bias;
+  p.bias_kind = a.bias_kind;
+  p.y = a.y;
+  p.y_dtype = a.y_dtype;
+  p.ldy = a.ldy;
+  p.partial = nullptr;
+  p.status = reinterpret_cast<DeviceStatus*>(device_status_ptr());
+  if (splits > 1) {
+    const size_t need = (size_t)splits * a.M * a.N * sizeof(float);
+    if (a.partial == nullptr || a.partial_bytes < need) {
+      set_error("split-K workspace too small: need %zu bytes", need);
+      return 2;
+    }
+    p.partial = a.partial;
+  }
+  CUtensorMap tx, tw;
+  int rc = make_tmap_2d(&tx, a.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)a.K, (uint64_t)a.M,
+                        (uint64_t)a.ldx * 2, 64, (uint32_t)tm, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (a.fmt == WF_INT8) {
+    rc = make_tmap_2d(&tw, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, 64,
+                      128, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  } else {
+    tw = tx;  // unused by bulk-copy decoders
+  }
+  switch (a.fmt) {
+    case WF_INT8: rc = dispatch_tm<DecInt8>(a, tx, tw, p, tm, stream); break;
+    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(a, tx, tw, p, tm, stream); break;
+    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(a, tx, tw, p, tm, stream); break;
+    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(a, tx, tw, p, tm, stream); break;
+    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(a, tx, tw, p, tm, stream); break;
+    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(a, tx, tw, p, tm, stream); break;
+    default: set_error("unknown weight format %d", a.fmt); return 2;
+  }
+  if (rc) return rc;
+  if (splits > 1) {
+    launch_splitk_finalize(p.partial, splits, a.M, a.N, a.col_scale, a.col_scale_kind, a.w_row_exp, a.x_row_exp,
+                           nullptr, a.bias, a.bias_kind, a.y, a.y_dtype, a.ldy, stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      set_error("split-K finalize launch failed: %s", cudaGetErrorString(e));
+      return 3;
+    }
+  }
+  return 0;
+}
+
+}  // namespace qlin

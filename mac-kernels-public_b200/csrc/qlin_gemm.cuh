@@ -1,0 +1,295 @@
+// Fused dequantize + GEMM on the 5th-generation tensor cores (sm_100a).
+//
+//   Y[m, n] = colscale[n] * rowscale[m] * sum_k Wdec[n, k] * X[m, k]  (+ bias[n])
+//
+// Weight-stationary orientation: the decoded weight tile is the MMA's A operand and lives in
+// tensor memory (TMEM), written by decoder warps with tcgen05.st; the activation tile is the B
+// operand, streamed by TMA into 128-byte-swizzled shared memory; the fp32 accumulator D[n, m]
+// is in TMEM too.  A weight tile is 128 rows (the MMA's M); a token tile is TM rows (the
+// MMA's N, 16..256), so small batches only shrink the MMA's N while the weight stream stays
+// the same.  Keeping A in TMEM leaves shared-memory bandwidth to the activation operand.
+//
+// Warp roles (320 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer (activations via tensor map; weights via tensor map or bulk copy)
+//   warp 1      TMEM allocator + single-thread MMA issuer
+//   warps 2..5  decoders: one weight row per thread, smem -> registers -> TMEM (A operand)
+//   warps 6..9  epilogue: TMEM -> registers, scales, bias, cast, global stores
+// Pipelines: STAGES-deep ring (full / a_full / empty) and a double-buffered accumulator
+// (acc_full / acc_empty) so the epilogue of one tile overlaps the MMAs of the next.
+#pragma once
+#include <cuda.h>
+
+#include "qlin_decode.cuh"
+
+namespace qlin {
+
+
+struct GemmParams {
+  int M, N, K;
+  int num_k_stages;  // stages over the padded K
+  int m_tiles, n_tiles, k_splits;
+  int stages_per_split;
+  // weights
+  const uint8_t* w_stages;  // repacked stage chunks [n_tile][k_stage][stage_bytes] (non-TMA decoders)
+  const int32_t* w_row_exp;  // per weight row exponent e (2^-e applied at decode, 2^e in epilogue)
+  // epilogue
+  const void* col_scale;
+  int col_scale_kind;
+  const int32_t* x_row_exp;  // per token exponent f (activation was scaled by 2^-f), or null
+  const void* bias;
+  int bias_kind;  // 0 none, 1 fp16, 2 fp32, 3 bf16
+  void* y;
+  int y_dtype;
+  long long ldy;
+  float* partial;  // split-K partial sums [k_splits][M][N]; null when k_splits == 1
+  DeviceStatus* status;
+};
+
+template <int TM, int STAGES>
+struct F16Cfg {
+  static constexpr int kThreads = 320;
+  static constexpr int kXStageBytes = TM * 128;  // TM rows x 64 fp16
+  static constexpr int kAccBufs = (2 * TM + STAGES * 32 <= 512) ? 2 : 1;
+  static constexpr int kAccCols = TM;
+  static constexpr int kACol0 = kAccBufs * TM;  // first TMEM column of the A stages
+  static constexpr uint32_t kTmemCols = 512;
+};
+
+__device__ __forceinline__ float load_bias(const void* bias, int kind, int n) {
+  if (kind == 1) return __half2float(reinterpret_cast<const __half*>(bias)[n]);
+  if (kind == 2) return reinterpret_cast<const float*>(bias)[n];
+  if (kind == 3) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
+  return 0.f;
+}
+
+__device__ __forceinline__ float load_colscale(const GemmParams& p, int n) {
+  switch (p.col_scale_kind) {
+    case CS_F16: return __half2float(reinterpret_cast<const __half*>(p.col_scale)[n]);
+    case CS_F32: return reinterpret_cast<const float*>(p.col_scale)[n];
+    case CS_EXP2: return exp2i(p.w_row_exp[n]);
+    default: return 1.f;
+  }
+}
+
+__device__ __forceinline__ void store_out(void* y, int dtype, long long idx, float v) {
+  if (dtype == OUT_F16) reinterpret_cast<__half*>(y)[idx] = __float2half_rn(v);
+  else if (dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(y)[idx] = v;
+}
+
+template <class Dec, int TM, int STAGES>
+__global__ void __launch_bounds__(320, 1)
+qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                 const GemmParams p) {
+  using Cfg = F16Cfg<TM, STAGES>;
+  constexpr uint32_t kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sx = smem;                                 // STAGES x kXStageBytes
+  uint8_t* sw = sx + STAGES * Cfg::kXStageBytes;      // STAGES x kWStage
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sw + STAGES * kWStage);
+  uint64_t* full = bars;                    // [STAGES]
+  uint64_t* a_full = full + STAGES;         // [STAGES]
+  uint64_t* empty = a_full + STAGES;        // [STAGES]
+  uint64_t* acc_full = empty + STAGES;      // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint64_t* drain = acc_empty + 2;          // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.m_tiles * p.n_tiles * p.k_splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&a_full[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_x);
+    if constexpr (Dec::kTma) prefetch_tmap(&tmap_w);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ----------------------------------------------------------------- producer
+    if (elect_one()) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int mt = t % p.m_tiles;
+        const int rest = t / p.m_tiles;
+        const int nt = rest % p.n_tiles;
+        const int ks = rest / p.n_tiles;
+        const int s0 = ks * p.stages_per_split;
+        const int s1 = min(p.num_k_stages, s0 + p.stages_per_split);
+        for (int kst = s0; kst < s1; ++kst, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes + Dec::kStageBytes);
+          tma_load_2d(sx + s * Cfg::kXStageBytes, &tmap_x, &full[s], kst * 64, mt * TM);
+          if constexpr (Dec::kTma) {
+            tma_load_2d(sw + s * kWStage, &tmap_w, &full[s], kst * 64, nt * 128);
+          } else {
+            const uint8_t* src = p.w_stages + ((size_t)nt * p.num_k_stages + kst) * Dec::kStageBytes;
+            bulk_load(sw + s * kWStage, src, Dec::kStageBytes, &full[s]);
+          }
+        }
+      }
+      if (!ok) {
+        // Let copies already in flight land before the CTA's shared memory goes away.
+        for (uint32_t j = (it >= (uint32_t)STAGES ? it - STAGES : 0); j < it; ++j) {
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(smem_u32(&full[j % STAGES]), (j / STAGES) & 1)) {
+            if (globaltimer() - t0 > QLIN_WAIT_TIMEOUT_NS) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, TM);
+      uint32_t it = 0, tile_i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tile_i) {
+        const int ks = (t / p.m_tiles) / p.n_tiles;
+        const int s0 = ks * p.stages_per_split;
+        const int s1 = min(p.num_k_stages, s0 + p.stages_per_split);
+        const int b = (Cfg::kAccBufs == 2) ? (tile_i & 1) : 0;
+        const uint32_t aph = (Cfg::kAccBufs == 2) ? ((tile_i >> 1) & 1) : (tile_i & 1);
+        if (!mbar_wait(&acc_empty[b], aph ^ 1, abort_flag, p.status, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * Cfg::kAccCols;
+        for (int kst = s0; kst < s1; ++kst, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&a_full[s], ph, abort_flag, p.status, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_tmem = tmem_base + Cfg::kACol0 + s * 32;
+          const uint64_t b_desc = smem_desc_sw128(smem_u32(sx + s * Cfg::kXStageBytes));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            mma_f16_ts(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, (kst > s0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[b]);
+      }
+      // Wait until every MMA this thread issued has completed before TMEM is released.
+      tc_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(smem_u32(drain), 0)) {
+        if (globaltimer() - t0 > QLIN_WAIT_TIMEOUT_NS) break;
+      }
+    }
+  } else if (warp < 6) {
+    // ----------------------------------------------------------------- decoders
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // weight row within the tile == TMEM lane
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      const int nt = (t / p.m_tiles) % p.n_tiles;
+      const int ks = (t / p.m_tiles) / p.n_tiles;
+      const int s0 = ks * p.stages_per_split;
+      const int s1 = min(p.num_k_stages, s0 + p.stages_per_split);
+      const int n = nt * 128 + r;
+      float rscale = 1.f;
+      if (p.w_row_exp != nullptr && p.col_scale_kind == CS_EXP2) rscale = exp2i(-p.w_row_exp[min(n, p.N - 1)]);
+      for (int kst = s0; kst < s1; ++kst, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag, p.status, 4)) { ok = false; break; }
+        uint32_t a[32];
+        Dec::decode(sw + s * kWStage, r, rscale, a);
+        tmem_st32(tmem_base + ((uint32_t)(quarter * 32) << 16) + Cfg::kACol0 + s * 32, a);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[s]);
+      }
+    }
+  } else {
+    // ----------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    uint32_t tile_i = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_i) {
+      const int mt = t % p.m_tiles;
+      const int nt = (t / p.m_tiles) % p.n_tiles;
+      const int ks = (t / p.m_tiles) / p.n_tiles;
+      const int b = (Cfg::kAccBufs == 2) ? (tile_i & 1) : 0;
+      const uint32_t aph = (Cfg::kAccBufs == 2) ? ((tile_i >> 1) & 1) : (tile_i & 1);
+      if (!mbar_wait(&acc_full[b], aph, abort_flag, p.status, 5)) break;
+      tc_fence_after();
+      const int n = nt * 128 + r;
+      const bool n_ok = n < p.N;
+      float cs = 1.f, bias = 0.f;
+      if (p.k_splits == 1 && n_ok) {
+        cs = load_colscale(p, n);
+        bias = load_bias(p.bias, p.bias_kind, n);
+      }
+#pragma unroll 1
+      for (int c0 = 0; c0 < TM; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * Cfg::kAccCols + c0, v);
+        tmem_wait_ld();
+        if (n_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = mt * TM + c0 + j;
+            if (m < p.M) {
+              float acc = __uint_as_float(v[j]);
+              if (p.k_splits > 1) {
+                p.partial[((size_t)ks * p.M + m) * p.N + n] = acc;
+              } else {
+                float o = __fmul_rn(acc, cs);
+                if (p.x_row_exp != nullptr) o = __fmul_rn(o, exp2i(__ldg(&p.x_row_exp[m])));
+                o = __fadd_rn(o, bias);
+                store_out(p.y, p.y_dtype, (long long)m * p.ldy + n, o);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+template <class Dec, int TM, int STAGES>
+constexpr int qgemm_f16_smem_bytes() {
+  constexpr int kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
+  return 1024 /*align slack*/ + STAGES * (TM * 128 + kWStage) + (3 * STAGES + 5) * 8 + 16;
+}
+
+}  // namespace qlin

@@ -1,0 +1,56 @@
+// Host-side declarations shared by the library's translation units (not part of the ABI).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace qlin {
+
+int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int group, int mode, void* out,
+                    int32_t* row_exp, float* row_scale, int perm, cudaStream_t stream);
+void launch_gguf_dequant(const uint8_t* raw, int qtype, long long total, void* out, int out_dtype, cudaStream_t s);
+void launch_gguf_row_exp(const uint8_t* raw, int qtype, int N, int K, int n_pad, int32_t* row_exp, cudaStream_t s);
+void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_stages, int n_tiles, uint8_t* out,
+                        uint32_t stage_bytes, int P, int S, cudaStream_t s);
+void launch_splitk_finalize(const float* partial, int splits, int M, int N, const void* col_scale, int cs_kind,
+                            const int32_t* w_row_exp, const int32_t* x_row_exp, const float* x_row_scale,
+                            const void* bias, int bias_kind, void* y, int y_dtype, long long ldy, cudaStream_t s);
+
+// Weight formats of the f16 (weight-only) GEMM family.
+enum WFormat : int { WF_INT8 = 0, WF_Q8_0 = 8, WF_Q4_0 = 2, WF_Q4_K = 12, WF_Q6_K = 14, WF_IQ4_NL = 20 };
+
+struct F16GemmArgs {
+  int fmt;
+  const void* x;  // fp16 activations [M, ldx] (prologue output or caller's fp16 tensor)
+  long long ldx;
+  int M, N, K;
+  const void* w;  // INT8: raw int8 [N, K]; GGUF: repacked stages
+  const int32_t* w_row_exp;
+  const void* col_scale;
+  int col_scale_kind;
+  const int32_t* x_row_exp;
+  const void* bias;
+  int bias_kind;
+  void* y;
+  int y_dtype;
+  long long ldy;
+  float* partial;  // split-K workspace (or null)
+  size_t partial_bytes;
+  int tm;           // token tile (0 = auto)
+  int k_splits;     // 0 = auto
+};
+
+// Returns 0 on success, a positive QLIN_* code on failure (message via set_error).
+int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream);
+size_t f16_gemm_partial_bytes(int M, int N, int K, int tm, int k_splits);
+void plan_f16(int M, int N, int K, int* tm, int* k_splits);
+
+uint32_t gguf_stage_bytes(int qtype, int* P, int* S);
+int gguf_block_values(int qtype);
+int gguf_type_size(int qtype);
+
+void set_error(const char* fmt, ...);
+int sm_count();
+void* device_status_ptr();
+
+}  // namespace qlin

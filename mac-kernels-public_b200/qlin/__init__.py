@@ -1,0 +1,232 @@
+"""qlin: B200-native quantized linears behind the comfy-kitchen operator surface.
+
+Python signatures follow the reference's callers (roblennon/mac-kernels-public):
+  int8_linear          bench/bench_ck01_int8.py:57, bench/bench_lora_fused_rank.py:39
+  gguf_linear          bench/bench_gguf_linear.py:120
+  dequantize_gguf      docs/upstream/comfy-kitchen-mps-followups.md:43
+  w4a8_int8_linear     bench/bench_lora_fused_rank.py:42-44, bench/bench_lora_sidepath_kernel.py:78
+  quantize_int8_rowwise  modal/weight_error_app.py:109-115 (activation quantizer of the A8 formats)
+
+Every op runs the CUDA library (libqlin.so, sm_100a) on the tensors' device and the current
+stream.  There is no CPU or eager fallback: unsupported inputs raise `QlinDecline`
+(a NotImplementedError), the way the kitchen registry reports an unsupported backend.
+Leading dimensions of x are flattened; empty contractions return before any launch.
+"""
+from __future__ import annotations
+
+import weakref
+
+import torch
+
+from . import _lib
+from ._lib import QlinDecline, QlinError, check, lib
+
+__all__ = ["int8_linear", "gguf_linear", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear",
+           "quantize_int8_rowwise", "prologue_f16", "repack_gguf", "GGUF_TYPES", "QlinDecline", "QlinError",
+           "device_status"]
+
+# ggml type id -> (name, values per block, bytes per block)
+GGUF_TYPES = {2: ("Q4_0", 32, 18), 8: ("Q8_0", 32, 34), 12: ("Q4_K", 256, 144), 14: ("Q6_K", 256, 210),
+              20: ("IQ4_NL", 32, 18)}
+GGUF_IDS = {v[0]: k for k, v in GGUF_TYPES.items()}
+_DT = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.int8: 3, torch.uint8: 4, torch.int32: 5,
+       torch.float8_e4m3fn: 6}
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise NotImplementedError("qlin runs on CUDA tensors only (there is no CPU path)")
+
+
+def _workspace(nbytes, device):
+    if nbytes == 0:
+        return None, 0
+    return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+
+
+def _flatten_x(x):
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    return x2
+
+
+def _out(x, n, out_dtype):
+    lead = x.shape[:-1]
+    return torch.empty(*lead, n, dtype=out_dtype or x.dtype, device=x.device)
+
+
+def device_status(reset=True):
+    import ctypes
+    where = ctypes.c_uint32(0)
+    code = lib.qlin_device_status(1 if reset else 0, ctypes.byref(where))
+    return code, where.value
+
+
+# ---------------------------------------------------------------------------------------------- INT8
+def int8_linear(x, qdata, scale, bias=None, out_dtype=None, convrot=False, convrot_groupsize=256,
+                lora_down=None, lora_up=None, lora_scale=None):
+    """y = rot(x) . (qdata * scale)^T + bias, weight-only INT8 (qdata int8 [N, K], stored rotated when
+    convrot).  `scale` is per output channel, [N] or [N, 1], fp32 or fp16; a scalar scale is broadcast.
+    The unmerged LoRA arguments run beside the layer: y += lora_scale * (x . down^T) . up^T."""
+    _require_cuda(x, qdata)
+    if qdata.dtype != torch.int8 or qdata.dim() != 2:
+        raise QlinDecline(1, "int8_linear: qdata must be a 2-D int8 tensor")
+    n, k = qdata.shape
+    if x.shape[-1] != k:
+        raise ValueError(f"int8_linear: x has {x.shape[-1]} features, weight has {k}")
+    y = _out(x, n, out_dtype)
+    if x.numel() == 0 or n == 0:
+        return y
+    if k == 0:
+        y.zero_()
+        if bias is not None:
+            y += bias.to(y.dtype)
+        return y
+    x2 = _flatten_x(x)
+    m = x2.shape[0]
+    sc = scale.reshape(-1)
+    if sc.numel() == 1:
+        sc = sc.expand(n)
+    if sc.dtype not in (torch.float32, torch.float16):
+        sc = sc.float()
+    sc = sc.contiguous()
+    q = qdata.contiguous()
+    b = None if bias is None else bias.contiguous()
+    if b is not None and b.dtype not in (torch.float16, torch.float32, torch.bfloat16):
+        b = b.float()
+    group = convrot_groupsize if convrot else 0
+    ws, wsb = _workspace(lib.qlin_int8_linear_workspace(m, n, k), x.device)
+    y2 = y.view(m, n)
+    check(lib.qlin_int8_linear(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), q.data_ptr(), n, sc.data_ptr(),
+                               _DT[sc.dtype], None if b is None else b.data_ptr(), 0 if b is None else _DT[b.dtype],
+                               group, y2.data_ptr(), _DT[y2.dtype], n, None if ws is None else ws.data_ptr(), wsb,
+                               _stream(x.device)), "qlin_int8_linear")
+    if lora_down is not None:
+        _lora_beside(y, x, lora_down, lora_up, lora_scale)
+    return y
+
+
+def _lora_beside(y, x, down, up, scale):
+    """Unmerged LoRA beside the layer in fp32: y += scale * (x . down^T) . up^T."""
+    s = 1.0 if scale is None else float(scale)
+    side = torch.nn.functional.linear(torch.nn.functional.linear(x.float(), down.float()), up.float())
+    y.add_((side * s).to(y.dtype))
+
+
+# ---------------------------------------------------------------------------------------------- GGUF
+_REPACK_CACHE: dict = {}
+
+
+def _repack_key(weight, qtype, shape):
+    return (weight.data_ptr(), weight.device.index, int(qtype), tuple(shape), weight._version)
+
+
+def repack_gguf(weight, qtype, shape):
+    """One-time repack of raw ggml blocks into the resident stage layout; cached per weight
+    tensor (dropped when the tensor is freed or modified in place)."""
+    import ctypes
+    n, k = int(shape[0]), int(shape[1])
+    key = _repack_key(weight, qtype, (n, k))
+    hit = _REPACK_CACHE.get(key)
+    if hit is not None:
+        return hit
+    nbytes = ctypes.c_size_t(0)
+    npad = ctypes.c_int64(0)
+    check(lib.qlin_gguf_repacked_bytes(int(qtype), n, k, ctypes.byref(nbytes), ctypes.byref(npad)),
+          "qlin_gguf_repacked_bytes")
+    raw = weight.contiguous()
+    packed = torch.empty(nbytes.value, dtype=torch.uint8, device=weight.device)
+    row_exp = torch.empty(npad.value, dtype=torch.int32, device=weight.device)
+    check(lib.qlin_gguf_repack(raw.data_ptr(), int(qtype), n, k, packed.data_ptr(), nbytes.value,
+                               row_exp.data_ptr(), npad.value, _stream(weight.device)), "qlin_gguf_repack")
+    entry = (packed, row_exp)
+    _REPACK_CACHE[key] = entry
+    try:
+        weakref.finalize(weight, _REPACK_CACHE.pop, key, None)
+    except TypeError:
+        pass
+    return entry
+
+
+def gguf_linear(x, weight, qtype, shape, bias=None, out_dtype=None, lora_down=None, lora_up=None, lora_scale=None):
+    """y = x . dequant_gguf(weight)^T + bias for raw ggml blocks `weight` (uint8, rows of whole
+    blocks) of logical `shape` (N, K); bias joins the fp32 sum before the one rounding."""
+    _require_cuda(x, weight)
+    qtype = int(qtype)
+    if qtype not in GGUF_TYPES:
+        raise QlinDecline(1, f"gguf_linear: type {qtype} is not supported")
+    n, k = int(shape[0]), int(shape[1])
+    if x.shape[-1] != k:
+        raise ValueError(f"gguf_linear: x has {x.shape[-1]} features, weight has {k}")
+    y = _out(x, n, out_dtype)
+    if x.numel() == 0 or n == 0:
+        return y
+    x2 = _flatten_x(x)
+    m = x2.shape[0]
+    packed, row_exp = repack_gguf(weight, qtype, (n, k))
+    b = None if bias is None else bias.contiguous()
+    if b is not None and b.dtype not in (torch.float16, torch.float32, torch.bfloat16):
+        b = b.float()
+    ws, wsb = _workspace(lib.qlin_gguf_linear_workspace(m, n, k, _DT[x2.dtype], x2.stride(0)), x.device)
+    y2 = y.view(m, n)
+    check(lib.qlin_gguf_linear(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), packed.data_ptr(),
+                               row_exp.data_ptr(), qtype, n, None if b is None else b.data_ptr(),
+                               0 if b is None else _DT[b.dtype], y2.data_ptr(), _DT[y2.dtype], n,
+                               None if ws is None else ws.data_ptr(), wsb, _stream(x.device)), "qlin_gguf_linear")
+    if lora_down is not None:
+        _lora_beside(y, x, lora_down, lora_up, lora_scale)
+    return y
+
+
+def dequantize_gguf(weight, qtype, shape, out_dtype=torch.float32):
+    """Decode-only, bit-exact with gguf-py 0.19.0 (fp16 / bf16 outputs round that value once)."""
+    _require_cuda(weight)
+    n, k = int(shape[0]), int(shape[1])
+    out = torch.empty(n, k, dtype=out_dtype, device=weight.device)
+    raw = weight.contiguous()
+    check(lib.qlin_gguf_dequantize(raw.data_ptr(), int(qtype), n, k, out.data_ptr(), _DT[out_dtype],
+                                   _stream(weight.device)), "qlin_gguf_dequantize")
+    return out
+
+
+# ---------------------------------------------------------------------------------------------- prologues
+def prologue_f16(x, rotate_group=0):
+    """(fp16 [M, Kp] operand, int32 row exponents): rotation + power-of-two row scaling."""
+    x2 = _flatten_x(x)
+    m, k = x2.shape
+    kp = (k + 63) // 64 * 64
+    out = torch.empty(m, kp, dtype=torch.float16, device=x.device)
+    rexp = torch.empty(m, dtype=torch.int32, device=x.device)
+    check(lib.qlin_prologue_f16(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), rotate_group, out.data_ptr(), kp,
+                                rexp.data_ptr(), _stream(x.device)), "qlin_prologue_f16")
+    return out, rexp
+
+
+def quantize_int8_rowwise(x, rotate_group=0, perm=False):
+    """Per-token INT8 quantization with the reference's rounding; returns (q int8 [M, K], scale fp32 [M, 1])."""
+    x2 = _flatten_x(x)
+    m, k = x2.shape
+    kp = (k + 127) // 128 * 128 if perm else k
+    q = torch.empty(m, kp, dtype=torch.int8, device=x.device)
+    s = torch.empty(m, 1, dtype=torch.float32, device=x.device)
+    check(lib.qlin_quantize_rows_int8(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), rotate_group, 1 if perm else 0,
+                                      q.data_ptr(), kp, s.data_ptr(), _stream(x.device)), "qlin_quantize_rows_int8")
+    return (q if kp == k else q[:, :k]), s
+
+
+# ---------------------------------------------------------------------------------------------- W4A8 / W6A8
+def w4a8_linear(*args, **kwargs):  # defined in _w4a8 once the kind::i8 kernels are built
+    from ._w4a8 import w4a8_linear as impl
+    return impl(*args, **kwargs)
+
+
+def w4a8_int8_linear(*args, **kwargs):
+    from ._w4a8 import w4a8_int8_linear as impl
+    return impl(*args, **kwargs)

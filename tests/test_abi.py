@@ -1,0 +1,58 @@
+"""CPU checks of the drop-in boundary: libqlin.so loads without a GPU and exports every entry
+point include/qlin.h declares; host-side argument checks answer without launching anything."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "qlin.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(qlin_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from qlin import _lib
+    names = declared_symbols()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(_lib.lib, n)]
+    assert not missing, missing
+    assert set(names) <= set(_lib.SIGNATURES), set(names) - set(_lib.SIGNATURES)
+
+
+def test_version_and_host_side_declines_without_gpu():
+    from qlin import _lib
+    lib = _lib.lib
+    assert lib.qlin_version().startswith(b"qlin")
+    size = ctypes.c_size_t(0)
+    npad = ctypes.c_int64(0)
+    # unsupported GGUF type and a K that is not whole blocks decline on the host
+    assert lib.qlin_gguf_repacked_bytes(3, 10, 256, ctypes.byref(size), ctypes.byref(npad)) == 1
+    assert lib.qlin_gguf_repacked_bytes(12, 10, 300, ctypes.byref(size), ctypes.byref(npad)) == 1
+    assert lib.qlin_gguf_repacked_bytes(12, 130, 512, ctypes.byref(size), ctypes.byref(npad)) == 0
+    assert npad.value == 256 and size.value == 2 * 8 * 128 * 40
+    assert b"block" in lib.qlin_last_error() or lib.qlin_last_error() == b""
+    # workspace queries are pure host arithmetic
+    assert lib.qlin_int8_linear_workspace(4096, 12288, 3072) >= 4096 * 3072 * 2
+
+
+def test_kitchen_signatures_match_reference_surface():
+    import inspect
+    import qlin
+    assert list(inspect.signature(qlin.int8_linear).parameters) == [
+        "x", "qdata", "scale", "bias", "out_dtype", "convrot", "convrot_groupsize", "lora_down", "lora_up",
+        "lora_scale"]
+    assert list(inspect.signature(qlin.gguf_linear).parameters) == [
+        "x", "weight", "qtype", "shape", "bias", "out_dtype", "lora_down", "lora_up", "lora_scale"]
+    assert list(inspect.signature(qlin.dequantize_gguf).parameters) == ["weight", "qtype", "shape", "out_dtype"]
+
+
+def test_cpu_tensors_are_refused_loudly():
+    import torch
+    import qlin
+    with pytest.raises(NotImplementedError):
+        qlin.int8_linear(torch.zeros(2, 16), torch.zeros(4, 16, dtype=torch.int8), torch.ones(4))

@@ -1,0 +1,202 @@
+"""GPU parity of the weight-only (kind::f16) path through the C-ABI: GGUF decode bit-exact with
+gguf-py 0.19.0 via the oracle, GGUF and INT8 ConvRot linears within the north-star tolerance
+(max |y - ref| / max |ref| <= 2e-3 for fp16 outputs, against a float64 reference)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import qlin_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float16: 2e-3, torch.bfloat16: 8e-3, torch.float32: 2e-3}
+
+
+@pytest.fixture(scope="module")
+def qlin():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import qlin as q
+    return q
+
+
+def _check_status(qlin):
+    code, where = qlin.device_status(reset=True)
+    assert code == 0, f"a kernel timed out waiting (where={where:#x})"
+
+
+@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_gguf_dequantize_bit_exact(qlin, qtype, out_dtype):
+    name, qk, ts = O.GGUF_TYPES[qtype]
+    raw = O.random_gguf_blocks(qtype, 40, 768 if qk == 256 else 544, seed=qtype)
+    n, k = 40, (768 if qk == 256 else 544)
+    flat = raw.reshape(-1, ts)
+    offs = {"Q4_0": [0], "Q8_0": [0], "IQ4_NL": [0], "Q4_K": [0, 2], "Q6_K": [208]}[name]
+    for i, v in enumerate([0.0, 65504.0, -65504.0, 2.0 ** -24, -(2.0 ** -20), 6.1e-5]):
+        for off in offs:
+            flat[i, off:off + 2] = np.array([v], dtype=np.float16).view(np.uint8)
+    ref = O.gguf_dequantize(raw, qtype, n, k)
+    got = qlin.dequantize_gguf(torch.from_numpy(raw).cuda(), qtype, (n, k), out_dtype).cpu()
+    want = torch.from_numpy(ref).to(out_dtype)
+    assert torch.equal(got.view(-1).float().isnan(), want.view(-1).float().isnan())
+    assert torch.equal(got.float().nan_to_num(), want.float().nan_to_num())
+    if out_dtype == torch.float32:
+        assert np.array_equal(got.numpy().view(np.uint32), ref.view(np.uint32))
+    _check_status(qlin)
+
+
+def test_gguf_dequantize_rows_straddling_blocks(qlin):
+    raw = O.random_gguf_blocks(12, 3, 1024, seed=5)  # 12 superblocks
+    ref = O.gguf_dequantize(raw, 12, 6, 512)
+    got = qlin.dequantize_gguf(torch.from_numpy(raw).cuda(), 12, (6, 512), torch.float32).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+def test_gguf_repack_row_exponents(qlin, qtype):
+    n, k = 200, 1024
+    raw = O.random_gguf_blocks(qtype, n, k, seed=11 + qtype)
+    packed, rexp = qlin.repack_gguf(torch.from_numpy(raw).cuda(), qtype, (n, k))
+    want = O.gguf_row_exponent(O.gguf_row_bound(raw, qtype, n, k))
+    got = rexp.cpu().numpy()
+    assert got.shape[0] == 256
+    assert np.array_equal(got[:n], want)
+    assert np.all(got[n:] == 0)
+
+
+def _gguf_case(qtype, m, n, k, seed, x_dtype=torch.float16, bias=True, scale=None):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=g).to(x_dtype)
+    raw = O.random_gguf_blocks(qtype, n, k, seed=seed, scale=scale)
+    b = (torch.randn(n, generator=g) * 0.1).to(torch.float16) if bias else None
+    w = O.gguf_dequantize(raw, qtype, n, k)
+    ref = O.linear_f64(x.float().numpy(), w, None if b is None else b.float().numpy())
+    return x, raw, b, ref
+
+
+@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+@pytest.mark.parametrize("m", [1, 7, 16, 33, 130, 300])
+def test_gguf_linear_matches_fp64(qlin, qtype, m):
+    n, k = 384, 1024
+    x, raw, b, ref = _gguf_case(qtype, m, n, k, seed=m * 31 + qtype)
+    y = qlin.gguf_linear(x.cuda(), torch.from_numpy(raw).cuda(), qtype, (n, k), bias=None if b is None else b.cuda())
+    assert y.dtype == torch.float16 and y.shape == (m, n)
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.max_abs_rel(got, ref) <= 2e-3, O.max_abs_rel(got, ref)
+    _check_status(qlin)
+
+
+@pytest.mark.parametrize("qtype", [8, 12])
+@pytest.mark.parametrize("x_dtype,out_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float32),
+                                               (torch.float32, torch.float16)])
+def test_gguf_linear_dtypes_and_ragged_n(qlin, qtype, x_dtype, out_dtype):
+    m, n, k = 45, 200, 768 if qtype == 12 else 800
+    x, raw, b, ref = _gguf_case(qtype, m, n, k, seed=7, x_dtype=x_dtype)
+    y = qlin.gguf_linear(x.cuda(), torch.from_numpy(raw).cuda(), qtype, (n, k), bias=b.cuda(), out_dtype=out_dtype)
+    assert y.dtype == out_dtype
+    assert O.max_abs_rel(y.float().cpu().numpy(), ref) <= TOL[out_dtype]
+
+
+def test_gguf_linear_large_activations_and_scales(qlin):
+    # H3-scale activations (|x| ~ 3e4) against large block scales: the row exponents keep the fp16
+    # operands finite.
+    m, n, k = 64, 256, 512
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(m, k, generator=g) * 3e4).to(torch.float16)
+    raw = O.random_gguf_blocks(8, n, k, seed=3, scale=30.0)
+    w = O.gguf_dequantize(raw, 8, n, k)
+    ref = O.linear_f64(x.float().numpy(), w)
+    y = qlin.gguf_linear(x.cuda(), torch.from_numpy(raw).cuda(), 8, (n, k), out_dtype=torch.float32)
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.max_abs_rel(got, ref) <= 2e-3
+
+
+def test_gguf_linear_nd_input_and_empty(qlin):
+    n, k = 128, 512
+    raw = torch.from_numpy(O.random_gguf_blocks(2, n, k, seed=1)).cuda()
+    x = torch.randn(2, 5, k, device="cuda", dtype=torch.float16)
+    y = qlin.gguf_linear(x, raw, 2, (n, k))
+    assert y.shape == (2, 5, n)
+    y2 = qlin.gguf_linear(x.reshape(10, k), raw, 2, (n, k))
+    assert torch.equal(y.reshape(10, n), y2)
+    e = qlin.gguf_linear(torch.empty(0, k, device="cuda", dtype=torch.float16), raw, 2, (n, k))
+    assert e.shape == (0, n)
+
+
+@pytest.mark.parametrize("group", [0, 128, 256])
+@pytest.mark.parametrize("m", [1, 16, 100, 256])
+def test_int8_convrot_linear_matches_fp64(qlin, group, m):
+    n, k = 320, 1024
+    x, q, s, b = O.cfg_int8_convrot(m, k, n, seed=m + group)
+    ref = O.int8_convrot_linear_ref(x.float().numpy(), q.numpy(), s.float().numpy(), b.float().numpy(),
+                                    group=group or 128, convrot=group > 0)
+    y = qlin.int8_linear(x.cuda(), q.cuda(), s.cuda(), b.cuda(), torch.float16, convrot=group > 0,
+                         convrot_groupsize=group or 256)
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.max_abs_rel(got, ref) <= 2e-3, O.max_abs_rel(got, ref)
+    _check_status(qlin)
+
+
+@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("scale_dtype", [torch.float32, torch.float16])
+def test_int8_linear_dtypes_and_scale_shapes(qlin, x_dtype, scale_dtype):
+    m, n, k = 77, 256, 768
+    x, q, s, b = O.cfg_int8_convrot(m, k, n, seed=5)
+    x = x.to(x_dtype)
+    ref = O.int8_convrot_linear_ref(x.float().numpy(), q.numpy(), s.float().numpy(), None, group=256)
+    y = qlin.int8_linear(x.cuda(), q.cuda(), s.to(scale_dtype).reshape(n, 1).cuda(), None, torch.float32,
+                         convrot=True, convrot_groupsize=256)
+    assert O.max_abs_rel(y.cpu().numpy(), ref) <= 2e-3
+
+
+def test_int8_linear_extreme_rows(qlin):
+    # rows with an outlier of 16000, tiny rows (2^-26) and zero rows
+    m, n, k = 48, 128, 512
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(m, k, generator=g)
+    x[0, 3] = 16000.0
+    x[1] *= 2.0 ** -26
+    x[2] = 0
+    x = x.to(torch.float16)
+    q = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int32).to(torch.int8)
+    s = torch.full((n,), 1e-3)
+    ref = O.int8_convrot_linear_ref(x.float().numpy(), q.numpy(), s.numpy(), None, group=128)
+    y = qlin.int8_linear(x.cuda(), q.cuda(), s.cuda(), None, torch.float32, convrot=True, convrot_groupsize=128)
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.all(got[2] == 0)
+    for r in range(m):  # per-row check so the tiny row is held to its own scale
+        if np.abs(ref[r]).max() > 0:
+            assert O.max_abs_rel(got[r], ref[r]) <= 2e-3, r
+
+
+def test_prologue_rotation_matches_oracle(qlin):
+    m, k = 33, 1024
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(m, k, generator=g).to(torch.float16)
+    for group in (128, 256):
+        xr, f = qlin.prologue_f16(x.cuda(), group)
+        got = xr[:, :k].float().cpu().numpy() * np.ldexp(1.0, f.cpu().numpy().astype(np.int64))[:, None]
+        ref = O.rotate_rows(x.float().numpy(), group)
+        assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max()
+        amax = np.abs(xr.float().cpu().numpy()).max(axis=1)
+        assert np.all((amax >= 2 ** 14) & (amax <= 2 ** 15))
+
+
+@pytest.mark.parametrize("x_dtype", [torch.float16, torch.bfloat16])
+def test_quantize_rows_int8_bit_exact(qlin, x_dtype):
+    m, k = 64, 1536
+    g = torch.Generator().manual_seed(12)
+    x = (torch.randn(m, k, generator=g) * torch.linspace(0.01, 50, m)[:, None]).to(x_dtype)
+    x[3] = 0
+    q_ref, s_ref = O.quantize_int8_rowwise(x)
+    q, s = qlin.quantize_int8_rowwise(x.cuda())
+    assert torch.equal(q.cpu(), q_ref)
+    assert torch.equal(s.cpu(), s_ref)
+    qp, _ = qlin.quantize_int8_rowwise(x.cuda(), perm=True)
+    perm = np.array([0, 2, 4, 6, 1, 3, 5, 7])
+    want = q_ref.numpy().reshape(m, -1, 8)[:, :, perm].reshape(m, -1)
+    assert np.array_equal(qp.cpu().numpy()[:, :k], want)
