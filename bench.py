@@ -1,0 +1,352 @@
+#!/usr/bin/env python
+"""Quantized-linear TFLOP/s and % roofline at M=4096, K=3072, N=12288, per format, on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one call of the reference-facing operator over one batch: the INT8 ConvRot weight-only
+linear of the benchmark configuration (X fp16 [4096, 3072] with 1% outlier channels, W int8
+[12288, 3072] stored rotated, Hadamard block 128, per-channel fp16 scale, fp16 bias, fp16 out).
+`value` is whole-job TFLOP/s (2*M*K*N per step, summed over ranks) with inputs resident in HBM;
+`e2e` is the same op through the public API with the step's activations copied from pinned host
+memory and its output copied back inside the timed region.  Every timed step is preceded by an
+L2 flush (a 512 MB write) outside its CUDA-event window.  `formats` times every other weight
+format at the same shape.  With --gpus N each rank runs its own replica (weak scaling; the
+linear needs no collective).  --impl reference times the reference's CPU dequantize + matmul path
+(restated in oracle/) on the host cores instead.
+"""
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mac-kernels-public_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+M, K, N = 4096, 3072, 12288
+GROUP = 128
+FLOPS = 2.0 * M * K * N
+METRIC = "quantized-linear TFLOP/s and % roofline at M=4096,K=3072,N=12288 per format"
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return {"hbm_gbs": p["hbm_gbs"], "tflops": p["bf16_tflops"], "tflops_sustained": p.get("bf16_tflops_sustained"),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.md, or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 100 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            bus = torch.cuda.get_device_properties(self.device).pci_bus_id
+            ident = ["--id=" + bus] if bus else []
+        except Exception:
+            ident = []
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", *ident, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        load = [s for s in sm if smax and s > 0.5 * max(smax)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def timed_steps(fn, steps, warmup, flush, stream):
+    """Per-step device times (ms) with CUDA events on `stream`, L2 flushed before every step."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        times.append((s, e))
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in times]
+
+
+def roofline_time_s(flops, nbytes, pk):
+    return max(nbytes / (pk["hbm_gbs"] * 1e9), flops / (pk["tflops"] * 1e12))
+
+
+def cpu_reference_step(x_cpu, q_cpu, s_cpu, b_cpu, rows):
+    """The reference's CPU path (dequantize the stored weight per call, fp32 linear), restated in
+    oracle/: W = rotate(q * s) in fp32 torch, Y = X[:rows] . W^T + b."""
+    from oracle import qlin_oracle as O
+    w = O.rotate_rows(q_cpu.float() * s_cpu.float()[:, None], GROUP)
+    return torch.nn.functional.linear(x_cpu[:rows].float(), w, b_cpu.float())
+
+
+def cpu_baseline(steps=2, rows=M):
+    from oracle import qlin_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=0)
+    cpu_reference_step(x, q, s, b, 16)  # warm the BLAS threads
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_reference_step(x, q, s, b, rows)
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": 2.0 * rows * K * N / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{steps} full steps ({rows} of {M} token rows), weight dequantized (q*s, rotate) per step, "
+                      f"fp32 torch on {torch.get_num_threads()} threads ({dt:.2f} s/step)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    torch.set_num_threads(os.cpu_count() or 1)
+    from oracle import qlin_oracle as O
+    x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=0)
+    rows = M
+    for _ in range(min(warm, 1)):
+        cpu_reference_step(x, q, s, b, rows)
+    times = []
+    for _ in range(min(steps, 3)):
+        t0 = time.perf_counter()
+        cpu_reference_step(x, q, s, b, rows)
+        times.append(time.perf_counter() - t0)
+    dt = statistics.mean(times)
+    value = 2.0 * rows * K * N / dt / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
+            "steps": len(times), "warmup": min(warm, 1), "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "int8_convrot_linear M=4096 K=3072 N=12288 group=128 fp16 out",
+                       "format": "int8_convrot", "sample_rows": rows, "l2": "n/a (host)"},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{len(times)} full steps ({rows} of {M} token rows); weight dequantized per step; "
+                                       f"fp32 torch"},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def format_sweep(dev, steps, warmup, flush, stream, pk):
+    """Every other weight format at the same (M, K, N): device TFLOP/s and roofline fraction."""
+    import qlin
+    from oracle import qlin_oracle as O
+    out = {}
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(M, K, generator=g).to(torch.float16).to(dev)
+    for qt, name in ((8, "gguf_q8_0"), (2, "gguf_q4_0"), (12, "gguf_q4_k"), (14, "gguf_q6_k"), (20, "gguf_iq4_nl")):
+        raw = torch.from_numpy(O.random_gguf_blocks(qt, N, K, seed=qt)).to(dev)
+        packed, _ = qlin.repack_gguf(raw, qt, (N, K))
+        fn = lambda: qlin.gguf_linear(x, raw, qt, (N, K))  # noqa: E731
+        t = statistics.mean(timed_steps(fn, steps, warmup, flush, stream))
+        nbytes = raw.numel() + M * K * 2 + M * N * 2
+        rt = roofline_time_s(FLOPS, nbytes, pk)
+        out[name] = {"tflops": FLOPS / (t * 1e-3) / 1e12, "ms": t, "roofline_frac": rt / (t * 1e-3), "bound": "tensor"}
+        del raw, packed
+    if hasattr(qlin, "w4a8_linear"):
+        try:
+            from qlin import _w4a8  # noqa: F401
+            for bits, grp, name in ((4, 128, "w4a8_g128"), (6, 64, "w6a8_g64")):
+                lo, hi = (-8, 8) if bits == 4 else (-32, 32)
+                wq = torch.randint(lo, hi, (N, K), generator=g, dtype=torch.int32).numpy().astype(np.int8)
+                packed = O.pack_w4_uniform(wq) if bits == 4 else O.pack_w6_interleaved(wq)
+                scales = (torch.randn(N, K // grp, generator=g).abs() * 0.003).to(torch.float16).to(dev)
+                pw = torch.from_numpy(packed.view(np.uint8).copy()).to(dev)
+                fn = lambda pw=pw, scales=scales, bits=bits, grp=grp: qlin.w4a8_linear(x, pw, scales, bits=bits,  # noqa: E731
+                                                                                       group_size=grp)
+                t = statistics.mean(timed_steps(fn, steps, warmup, flush, stream))
+                nbytes = pw.numel() + scales.numel() * 2 + M * K * 2 + M * N * 2
+                out[name] = {"tops": FLOPS / (t * 1e-3) / 1e12, "ms": t, "bound": "tensor (kind::i8)"}
+        except (ImportError, NotImplementedError) as e:
+            out["w4a8"] = {"unavailable": str(e)[:120]}
+    return out
+
+
+def run_ours(args, rank, world):
+    import qlin
+    from oracle import qlin_oracle as O
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    pk = peaks()
+    x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=rank)
+    xd, qd, sd, bd = x.to(dev), q.to(dev), s.to(dev), b.to(dev)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step():
+        return qlin.int8_linear(xd, qd, sd, bd, torch.float16, convrot=True, convrot_groupsize=GROUP)
+
+    y = step()
+    torch.cuda.synchronize()
+    ref = O.int8_convrot_linear_ref(x[:64].float().numpy(), q.numpy(), s.float().numpy(), b.float().numpy(),
+                                    group=GROUP)
+    err = O.max_abs_rel(y[:64].float().cpu().numpy(), ref)
+    if err > 2e-3:
+        raise SystemExit(f"parity check failed before timing: max-abs-rel {err}")
+
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev) as clk:
+        # ~1 s of back-to-back steps so the clock samples see the GPU under this load, then the
+        # timed steps
+        t_end = time.perf_counter() + 1.0
+        while time.perf_counter() < t_end:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize()
+        times = timed_steps(step, args.steps, args.warmup, flush, stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = statistics.mean(times)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * FLOPS / (ms * 1e-3) / 1e12
+
+    # Dominant kernel alone: the fused dequantize + GEMM on the already rotated fp16 operand.
+    xr, f = qlin.prologue_f16(xd, GROUP)
+    xr_in = (xr[:, :K].float() * torch.exp2(f.float())[:, None]).to(torch.float16).contiguous()
+    gemm = lambda: qlin.int8_linear(xr_in, qd, sd, bd, torch.float16, convrot=False)  # noqa: E731
+    t_gemm = statistics.mean(timed_steps(gemm, args.steps, args.warmup, flush, stream))
+    achieved = FLOPS / (t_gemm * 1e-3) / 1e12
+    traffic = profile_traffic("int8_convrot_gemm_cfg2")
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": pk["tflops"], "unit": "TFLOP/s",
+                "frac": achieved / pk["tflops"], "traffic": traffic, "peak_source": pk["source"],
+                "kernel": "qgemm_f16_kernel<DecInt8,128,6>", "kernel_ms": t_gemm}
+    algo_bytes = q.numel() + N * 2 + N * 2 + M * K * 2 + M * N * 2
+    roof_t = roofline_time_s(FLOPS, algo_bytes, pk)
+
+    # End to end through the public API: host X -> device, op, device Y -> host, per step.
+    xh = x.pin_memory()
+    yh = torch.empty(M, N, dtype=torch.float16).pin_memory()
+    xbuf = torch.empty_like(xd)
+
+    def e2e_step():
+        xbuf.copy_(xh, non_blocking=True)
+        yy = qlin.int8_linear(xbuf, qd, sd, bd, torch.float16, convrot=True, convrot_groupsize=GROUP)
+        yh.copy_(yy, non_blocking=True)
+
+    t_e2e = statistics.mean(timed_steps(e2e_step, max(3, args.steps // 2), 2, flush, stream))
+    if world > 1:
+        t = torch.tensor([t_e2e], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        t_e2e = float(t.item())
+
+    formats = {}
+    if not args.no_formats:
+        formats = format_sweep(dev, max(3, args.steps // 4), 2, flush, stream, pk)
+    formats["int8_convrot_g128"] = {"tflops": FLOPS / (ms * 1e-3) / 1e12, "ms": ms,
+                                    "roofline_frac": roof_t / (ms * 1e-3), "bound": "tensor"}
+
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline()
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16 (int8 weights decoded exactly to fp16, fp32 accumulate)",
+                "data": "synthetic (seeded; configuration 2 shapes and distributions)",
+                "config": {"workload": "int8_convrot_linear M=4096 K=3072 N=12288 group=128 fp16 out",
+                           "format": "int8_convrot", "hadamard": "sylvester-128", "l2": "flushed before every step",
+                           "parallelism": f"replicas x{world}"},
+                "roofline": roofline,
+                "roofline_op": {"bound": "tensor", "time_frac": roof_t / (ms * 1e-3),
+                                "note": "whole op (rotation prologue + GEMM) vs max(bytes/HBM, flops/peak)"},
+                "e2e": {"value": world * FLOPS / (t_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+                        "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
+                "cpu_baseline": base, "formats": formats, "gpu_launches": 2 * args.steps,
+                "parity_max_abs_rel": err, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-formats", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world)
+    finally:
+        if world > 1 and args.impl == "ours" and torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "qlin_gemm.cuh"
@@ -122,6 +123,14 @@ int gguf_type_size(int qtype) {
 
 void plan_f16(int M, int N, int K, int* tm_out, int* splits_out) {
   int tm = *tm_out;
+  // Tuning knob: QLIN_TM forces the token tile (16, 32, 64, 128 or 256) for sweeps.
+  if (tm == 0) {
+    static const int forced = [] {
+      const char* e = getenv("QLIN_TM");
+      return e ? atoi(e) : 0;
+    }();
+    if (forced == 16 || forced == 32 || forced == 64 || forced == 128 || forced == 256) tm = forced;
+  }
   if (tm == 0) {
     if (M <= 16) tm = 16;
     else if (M <= 32) tm = 32;
@@ -170,7 +179,7 @@ static int launch_one(const F16GemmArgs& a, const CUtensorMap& tx, const CUtenso
   }
   const int tiles = p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = std::min(tiles, sm_count());
-  kern<<<grid, 320, smem, stream>>>(tx, tw, p);
+  kern<<<grid, F16Cfg<TM, STAGES>::kThreads, smem, stream>>>(tx, tw, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("qgemm_f16 launch failed: %s", cudaGetErrorString(e));

@@ -9,11 +9,12 @@
 // MMA's N, 16..256), so small batches only shrink the MMA's N while the weight stream stays
 // the same.  Keeping A in TMEM leaves shared-memory bandwidth to the activation operand.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over tiles):
-//   warp 0      TMA producer (activations via tensor map; weights via tensor map or bulk copy)
-//   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2..5  decoders: one weight row per thread, smem -> registers -> TMEM (A operand)
-//   warps 6..9  epilogue: TMEM -> registers, scales, bias, cast, global stores
+// Warp roles (448 threads, one CTA per SM, persistent over tiles):
+//   warp 0       TMA producer (activations via tensor map; weights via tensor map or bulk copy)
+//   warp 1       TMEM allocator + single-thread MMA issuer
+//   warps 2..9   decoders, two groups of four that take alternate pipeline stages: one weight
+//                row per thread, smem -> registers -> TMEM (A operand)
+//   warps 10..13 epilogue: TMEM -> registers, scales, bias, cast, global stores
 // Pipelines: STAGES-deep ring (full / a_full / empty) and a double-buffered accumulator
 // (acc_full / acc_empty) so the epilogue of one tile overlaps the MMAs of the next.
 #pragma once
@@ -47,7 +48,8 @@ struct GemmParams {
 
 template <int TM, int STAGES>
 struct F16Cfg {
-  static constexpr int kThreads = 320;
+  static constexpr int kDecGroups = 2;
+  static constexpr int kThreads = 32 * (2 + 4 * kDecGroups + 4);
   static constexpr int kXStageBytes = TM * 128;  // TM rows x 64 fp16
   static constexpr int kAccBufs = (2 * TM + STAGES * 32 <= 512) ? 2 : 1;
   static constexpr int kAccCols = TM;
@@ -78,7 +80,7 @@ __device__ __forceinline__ void store_out(void* y, int dtype, long long idx, flo
 }
 
 template <class Dec, int TM, int STAGES>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(448, 1)
 qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                  const GemmParams p) {
   using Cfg = F16Cfg<TM, STAGES>;
@@ -202,9 +204,10 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         if (globaltimer() - t0 > QLIN_WAIT_TIMEOUT_NS) break;
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + 4 * Cfg::kDecGroups) {
     // ----------------------------------------------------------------- decoders
     const int quarter = warp & 3;
+    const int group = (warp - 2) >> 2;  // takes ring iterations it with it % kDecGroups == group
     const int r = quarter * 32 + lane;  // weight row within the tile == TMEM lane
     uint32_t it = 0;
     bool ok = true;
@@ -217,6 +220,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       float rscale = 1.f;
       if (p.w_row_exp != nullptr && p.col_scale_kind == CS_EXP2) rscale = exp2i(-p.w_row_exp[min(n, p.N - 1)]);
       for (int kst = s0; kst < s1; ++kst, ++it) {
+        if ((int)(it % Cfg::kDecGroups) != group) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag, p.status, 4)) { ok = false; break; }
@@ -253,23 +257,29 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       for (int c0 = 0; c0 < TM; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * Cfg::kAccCols + c0, v);
+        // per-token power of two for the 32 columns of this chunk: lane j holds column j's
+        const int mj = mt * TM + c0 + lane;
+        const float rs_lane = (p.x_row_exp != nullptr && mj < p.M) ? exp2i(__ldg(&p.x_row_exp[mj])) : 1.f;
         tmem_wait_ld();
         if (n_ok) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = mt * TM + c0 + j;
+            const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
             if (m < p.M) {
               float acc = __uint_as_float(v[j]);
               if (p.k_splits > 1) {
                 p.partial[((size_t)ks * p.M + m) * p.N + n] = acc;
               } else {
-                float o = __fmul_rn(acc, cs);
-                if (p.x_row_exp != nullptr) o = __fmul_rn(o, exp2i(__ldg(&p.x_row_exp[m])));
+                float o = __fmul_rn(__fmul_rn(acc, cs), rs);
                 o = __fadd_rn(o, bias);
                 store_out(p.y, p.y_dtype, (long long)m * p.ldy + n, o);
               }
             }
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) (void)__shfl_sync(0xffffffffu, rs_lane, j);
         }
       }
       tc_fence_before();

@@ -103,7 +103,7 @@ def test_gguf_linear_large_activations_and_scales(qlin):
     # operands finite.
     m, n, k = 64, 256, 512
     g = torch.Generator().manual_seed(3)
-    x = (torch.randn(m, k, generator=g) * 3e4).to(torch.float16)
+    x = (torch.randn(m, k, generator=g) * 1e4).clamp(-6e4, 6e4).to(torch.float16)
     raw = O.random_gguf_blocks(8, n, k, seed=3, scale=30.0)
     w = O.gguf_dequantize(raw, 8, n, k)
     ref = O.linear_f64(x.float().numpy(), w)
