@@ -82,6 +82,19 @@ int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
                      const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
                      int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The GGUF linear above with no workspace argument: the scratch (fp16 activation copy and split-K
+ * partial sums) lives in a fixed 16 MiB array in device memory that the library reserves on every
+ * device that loads it, until the process exits.  It has no counterpart in the reference; it is
+ * for callers that cannot allocate device memory at call time: hosts without a caching allocator
+ * (cudaMalloc synchronizes the device and costs far more than the layer) and hosts with a fixed
+ * memory budget or allocation-free steady state.  Calls whose scratch need exceeds 16 MiB are
+ * rejected with QLIN_EINVAL and a message; nothing is allocated.  The first call on a device
+ * looks up the scratch address (make that call before any stream capture).  Calls on one device
+ * share the scratch, so calls that overlap on the GPU race: order them on one stream. */
+int qlin_gguf_linear_noalloc(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                             const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
+                             int y_dtype, int64_t ldy, void* stream);
+
 /* Decode-only, bit-exact with gguf-py 0.19.0 (f32 out; f16 / bf16 out = that value rounded once).
  * Blocks are indexed by flat element, so rows may straddle blocks.  Replaces comfy-kitchen
  * `dequantize_gguf(weight, qtype, shape, out_dtype)` (docs/upstream/comfy-kitchen-mps-followups.md:43). */

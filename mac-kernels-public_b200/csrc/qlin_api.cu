@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/qlin.h"
 #include "qlin_internal.h"
@@ -92,6 +93,38 @@ static int make_f16_operand(const void* x, int x_dtype, int64_t m, int64_t k, in
 }
 
 static bool valid_group(int g) { return g == 0 || g == 32 || g == 64 || g == 128 || g == 256; }
+
+// Scratch for qlin_gguf_linear_noalloc: a fixed 16 MiB array in every device's global memory,
+// reserved when the library's module is loaded on that device and held until the process exits.
+// It replaces the caller's workspace (the fp16 activation copy and the split-K partial sums).
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch for the current device.  In host code the symbol is only
+// a host-side stand-in; the real address comes from cudaGetSymbolAddress, looked up once per
+// device with that device current.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("qlin_gguf_linear_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+    return QLIN_ECUDA;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("qlin_gguf_linear_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
+      return QLIN_ECUDA;
+    }
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return QLIN_OK;
+}
 
 }  // namespace qlin
 
@@ -271,6 +304,34 @@ int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
     return QLIN_EINVAL;
   }
   return run_f16_gemm(a, stream);
+}
+
+// Same computation as qlin_gguf_linear, with the workspace taken from the library's static device
+// scratch instead of the caller.  Nothing is allocated, so it suits callers that cannot allocate
+// device memory at call time.  The first call on a device looks up the scratch address (make it
+// before any stream capture).  All calls on a device share one scratch: calls that overlap on
+// the GPU (different streams, or other threads) race and must be ordered by the caller.
+// Every scratch byte a call reads is written earlier in the same call, so stale contents from a
+// previous call are never read and nothing needs clearing.
+int qlin_gguf_linear_noalloc(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                             const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
+                             int y_dtype, int64_t ldy, void* stream) {
+  if (m < 0 || n < 0 || k < 0) {
+    set_error("qlin_gguf_linear_noalloc: bad sizes");
+    return QLIN_EINVAL;
+  }
+  const size_t need = qlin_gguf_linear_workspace(m, n, k, x_dtype, ldx);
+  if (need > kNoAllocScratchBytes) {
+    set_error("qlin_gguf_linear_noalloc: this call needs %zu bytes of scratch, more than the fixed %zu bytes "
+              "(16 MiB); use qlin_gguf_linear with a caller workspace",
+              need, kNoAllocScratchBytes);
+    return QLIN_EINVAL;
+  }
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return qlin_gguf_linear(x, x_dtype, m, k, ldx, packed, row_exp, qtype, n, bias, bias_dtype, y, y_dtype, ldy,
+                          scratch, kNoAllocScratchBytes, stream);
 }
 
 int qlin_gguf_dequantize(const void* raw, int qtype, int64_t n, int64_t k, void* out, int out_dtype, void* stream_) {
