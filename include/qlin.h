@@ -101,6 +101,31 @@ int qlin_gguf_linear_noalloc(const void* x, int x_dtype, int64_t m, int64_t k, i
 int qlin_gguf_dequantize(const void* raw, int qtype, int64_t n, int64_t k, void* out, int out_dtype, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * W4A8 / W6A8 packed-weight linears on the integer tensor cores (kind::i8, int32 accumulation).
+ * Replaces comfy-kitchen `w4a8_int8_linear(x, qdata, s_rel, s_channel, ..., group_size,
+ * convrot_groupsize, out_dtype)` (bench/bench_lora_fused_rank.py:42-44; positional form
+ * bench/bench_lora_sidepath_kernel.py:78) for symmetric uniform weights:
+ *   bits 4: values in [-8, 7] stored as nibbles u = q + 8, two per byte, even column in the low
+ *           nibble (the kitchen's nibble order, modal/weight_error_app.py:145-152), [n, k/2] bytes;
+ *   bits 6: values in [-32, 31]; qlin_w4a8_repack converts layout 0 (four values per three bytes:
+ *           u0 | u1<<6 | u2<<12 | u3<<18 little-endian, u = q + 32) or layout 1 (the kitchen planar
+ *           6-bit packing, modal/weight_error_app.py:145-152) into the kernel's stage layout.
+ * Scales: group != 0 -> fp16 group scales [n, k/group] (group a multiple of 32 dividing k);
+ *         group == 0 -> fp32 per-channel scales [n].
+ * Activations are rotated (rotate_group, 0 = none) and quantized per token exactly like
+ * qlin_quantize_rows_int8; each group's int32 sum is exact; Y = sx[m] * sum_g s[n,g] * P_g + bias
+ * in fp32, rounded once.  Requires k % 128 == 0.
+ * ------------------------------------------------------------------------------------------ */
+int qlin_w4a8_repacked_bytes(int bits, int layout, int64_t n, int64_t k, size_t* bytes);
+int qlin_w4a8_repack(const void* packed, int bits, int layout, int64_t n, int64_t k, void* out, size_t out_bytes,
+                     void* stream);
+size_t qlin_w4a8_linear_workspace(int64_t m, int64_t n, int64_t k, int rotate_group);
+int qlin_w4a8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* w, int bits, int group,
+                     int64_t n, const void* scales, int scale_dtype, int rotate_group, const void* bias,
+                     int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * Activation prologues (exposed for tests and for callers that reuse one prologue across
  * several linears sharing an input).
  *   qlin_prologue_f16: optional block-Hadamard rotation, then per-row power-of-two scaling

@@ -9,6 +9,7 @@
 #include "../../include/qlin.h"
 #include "qlin_internal.h"
 #include "qlin_ptx.cuh"
+#include "qlin_gemm_i8.cuh"
 
 namespace qlin {
 
@@ -349,6 +350,88 @@ int qlin_gguf_dequantize(const void* raw, int qtype, int64_t n, int64_t k, void*
   launch_gguf_dequant(reinterpret_cast<const uint8_t*>(raw), qtype, (long long)(n * k), out, out_kind_of(out_dtype),
                       stream);
   return check_cuda("gguf dequantize launch");
+}
+
+// ------------------------------------------------------------------------------------------ W4A8 / W6A8
+int qlin_w4a8_repacked_bytes(int bits, int layout, int64_t n, int64_t k, size_t* bytes) {
+  if ((bits != 4 && bits != 6) || layout < 0 || layout > 1 || (bits == 4 && layout != 0) || n < 0 || k <= 0 ||
+      k % 128 != 0) {
+    set_error("unsupported packed-weight format bits=%d layout=%d k=%lld (k must be a multiple of 128)", bits, layout,
+              (long long)k);
+    return QLIN_EDECLINE;
+  }
+  if (bytes) *bytes = bits == 4 ? (size_t)n * k / 2 : w6_repacked_bytes((int)n, (int)k);
+  return QLIN_OK;
+}
+
+int qlin_w4a8_repack(const void* packed, int bits, int layout, int64_t n, int64_t k, void* out, size_t out_bytes,
+                     void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  size_t need = 0;
+  int rc = qlin_w4a8_repacked_bytes(bits, layout, n, k, &need);
+  if (rc) return rc;
+  if (out_bytes < need || packed == nullptr || out == nullptr || (reinterpret_cast<uintptr_t>(out) & 15)) {
+    set_error("repack output needs %zu bytes, 16-byte aligned", need);
+    return QLIN_EINVAL;
+  }
+  if (need == 0) return QLIN_OK;
+  if (bits == 4) {
+    if (cudaMemcpyAsync(out, packed, need, cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
+      return check_cuda("w4 repack copy");
+    return QLIN_OK;
+  }
+  launch_w6_repack(reinterpret_cast<const uint8_t*>(packed), layout, (int)n, (int)k, reinterpret_cast<uint8_t*>(out),
+                   stream);
+  return check_cuda("w6 repack launch");
+}
+
+size_t qlin_w4a8_linear_workspace(int64_t m, int64_t n, int64_t k, int rotate_group) {
+  (void)n;
+  (void)rotate_group;
+  return align256((size_t)m * round_up(k, 128)) + align256((size_t)m * 4);
+}
+
+int qlin_w4a8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* w, int bits, int group,
+                     int64_t n, const void* scales, int scale_dtype, int rotate_group, const void* bias,
+                     int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                     void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (m < 0 || n < 0 || k < 0 || ldx < k || ldy < n) {
+    set_error("bad sizes");
+    return QLIN_EINVAL;
+  }
+  if (m == 0 || n == 0) return QLIN_OK;
+  const bool per_channel = group == 0;
+  if ((bits != 4 && bits != 6) || k % 128 != 0 || !is_float_dtype(x_dtype) || out_kind_of(y_dtype) < 0 ||
+      bias_kind_of(bias, bias_dtype) < 0 || !valid_group(rotate_group) || (rotate_group && k % rotate_group) ||
+      (per_channel ? scale_dtype != QLIN_F32 : (scale_dtype != QLIN_F16 || group % 32 != 0 || k % group != 0)) ||
+      m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) {
+    set_error("unsupported W%dA8 arguments: k=%lld group=%d scale dtype %d (k must be a multiple of 128 and of "
+              "the group; group scales fp16, per-channel scales fp32)",
+              bits, (long long)k, group, scale_dtype);
+    return QLIN_EDECLINE;
+  }
+  if (x == nullptr || w == nullptr || scales == nullptr || y == nullptr || (reinterpret_cast<uintptr_t>(w) & 15)) {
+    set_error("null or misaligned pointer (weights need 16-byte alignment)");
+    return QLIN_EINVAL;
+  }
+  Carver ws{reinterpret_cast<uint8_t*>(workspace), workspace_bytes};
+  const int64_t kp = round_up(k, 128);
+  int8_t* xq = reinterpret_cast<int8_t*>(ws.take((size_t)m * kp));
+  float* sx = reinterpret_cast<float*>(ws.take((size_t)m * 4));
+  if (ws.off > ws.cap || workspace == nullptr) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  if (launch_prologue(x, x_dtype, ldx, (int)m, (int)k, (int)kp, rotate_group, 1, xq, nullptr, sx, 1, stream) != 0) {
+    set_error("unsupported rotation group %d", rotate_group);
+    return QLIN_EDECLINE;
+  }
+  int rc = check_cuda("quantize launch");
+  if (rc) return rc;
+  return run_i8_gemm(bits, xq, kp, sx, (int)m, (int)n, (int)k, w, per_channel ? (int)k : group, scales,
+                     per_channel ? I8S_CHANNEL_F32 : I8S_GROUP_F16, bias, bias_kind_of(bias, bias_dtype), y,
+                     out_kind_of(y_dtype), ldy, stream);
 }
 
 // ------------------------------------------------------------------------------------------ prologues

@@ -205,3 +205,79 @@ struct DecQ6_K : PlaneStage<3, 8> {
 };
 
 }  // namespace qlin
+
+namespace qlin {
+
+// ---------------------------------------------------------------------------------------------
+// i8 family (kind::i8, 128 K-values per stage).  The activation operand is stored with every
+// group of 8 columns permuted to 0,2,4,6,1,3,5,7, so TMEM column 2j holds the weights of
+// columns 8j+{0,2,4,6} and column 2j+1 those of 8j+{1,3,5,7}.
+// ---------------------------------------------------------------------------------------------
+
+// Symmetric 4-bit weights stored as unsigned nibbles u = q + 8 (even column in the low nibble),
+// raw [N, K/2] bytes via a TMA box {64 B, 128 rows} with 64-byte swizzle.  Output bytes are
+// 16*q (exact in int8); the epilogue divides by 16.
+struct DecW4 {
+  static constexpr uint32_t kStageBytes = 128 * 64;
+  static constexpr bool kTma = true;
+  static constexpr float kInvScale = 1.0f / 16.0f;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, uint32_t (&out)[32]) {
+    const uint8_t* row = st + r * 64;
+    const int sw = (r >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(row + ((j ^ sw) << 4));
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t s = w[t] ^ 0x88888888u;  // nibble = two's complement of q
+        out[8 * j + 2 * t + 0] = (s << 4) & 0xF0F0F0F0u;  // columns 0,2,4,6 of these 8
+        out[8 * j + 2 * t + 1] = s & 0xF0F0F0F0u;         // columns 1,3,5,7
+      }
+    }
+  }
+};
+
+// Symmetric 6-bit weights in the repacked "W6 planes" layout (one stage = 128 values per row):
+// per unit u of 16 values, L0 / L1 hold the low nibbles of values 0-7 / 8-15 (value i in nibble
+// i) and T holds the high 2 bits: byte b bits 0-1 = value 2b, 2-3 = 2b+1, 4-5 = 8+2b, 6-7 = 9+2b.
+// Stage chunk: [6 planes][128 rows][16 B]; planes 0-3 carry L0,L1 of units 0..7, planes 4-5 the T
+// words of units 0..7.  Output bytes are 4*q = (4u) ^ 0x80; the epilogue divides by 4.
+struct DecW6 {
+  static constexpr uint32_t kStageBytes = 128 * 96;
+  static constexpr bool kTma = false;
+  static constexpr float kInvScale = 0.25f;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, uint32_t (&out)[32]) {
+    uint32_t L[16], T[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(st + (j * 128 + r) * 16);
+      L[4 * j] = v.x;
+      L[4 * j + 1] = v.y;
+      L[4 * j + 2] = v.z;
+      L[4 * j + 3] = v.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(st + ((4 + j) * 128 + r) * 16);
+      T[4 * j] = v.x;
+      T[4 * j + 1] = v.y;
+      T[4 * j + 2] = v.z;
+      T[4 * j + 3] = v.w;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t l0 = L[2 * u], l1 = L[2 * u + 1], t = T[u];
+      const uint32_t o0 = (l0 & 0x0F0F0F0Fu) | ((t & 0x03030303u) << 4);
+      const uint32_t o1 = ((l0 >> 4) & 0x0F0F0F0Fu) | ((t & 0x0C0C0C0Cu) << 2);
+      const uint32_t o2 = (l1 & 0x0F0F0F0Fu) | (t & 0x30303030u);
+      const uint32_t o3 = ((l1 >> 4) & 0x0F0F0F0Fu) | ((t >> 2) & 0x30303030u);
+      out[4 * u + 0] = (o0 << 2) ^ 0x80808080u;
+      out[4 * u + 1] = (o1 << 2) ^ 0x80808080u;
+      out[4 * u + 2] = (o2 << 2) ^ 0x80808080u;
+      out[4 * u + 3] = (o3 << 2) ^ 0x80808080u;
+    }
+  }
+};
+
+}  // namespace qlin

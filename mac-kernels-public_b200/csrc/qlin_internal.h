@@ -49,6 +49,13 @@ uint32_t gguf_stage_bytes(int qtype, int* P, int* S);
 int gguf_block_values(int qtype);
 int gguf_type_size(int qtype);
 
+void launch_w6_repack(const uint8_t* src, int layout, int N, int K, uint8_t* out, cudaStream_t s);
+size_t w6_repacked_bytes(int N, int K);
+int plan_i8_tm(int M);
+int run_i8_gemm(int bits, const void* xq, long long kp, const float* sx, int M, int N, int K, const void* w, int group,
+                const void* scales, int scale_kind, const void* bias, int bias_kind, void* y, int y_dtype,
+                long long ldy, cudaStream_t stream);
+
 void set_error(const char* fmt, ...);
 int sm_count();
 void* device_status_ptr();

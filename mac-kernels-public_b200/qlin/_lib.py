@@ -34,12 +34,11 @@ SIGNATURES = {
     "qlin_gguf_dequantize": (_i, [_p, _i, _i64, _i64, _p, _i, _p]),
     "qlin_prologue_f16": (_i, [_p, _i, _i64, _i64, _i64, _i, _p, _i64, _p, _p]),
     "qlin_quantize_rows_int8": (_i, [_p, _i, _i64, _i64, _i64, _i, _i, _p, _i64, _p, _p]),
-    "qlin_w4a8_linear_workspace": (_sz, [_i64, _i64, _i64, _i]),
     "qlin_w4a8_repacked_bytes": (_i, [_i, _i, _i64, _i64, ctypes.POINTER(_sz)]),
     "qlin_w4a8_repack": (_i, [_p, _i, _i, _i64, _i64, _p, _sz, _p]),
-    "qlin_w4a8_linear": (_i, [_p, _i, _i64, _i64, _i64, _p, _i, _i, _i64, _p, _i, _i, _p, _i, _p, _i, _i64, _p, _sz, _p]),
-    "qlin_kitchen_w4a8_linear": (_i, [_p, _i, _i64, _i64, _i64, _p, _i, _i64, _p, _p, _p, _i, _i, _p, _i, _p, _i,
-                                      _i64, _p, _sz, _p]),
+    "qlin_w4a8_linear_workspace": (_sz, [_i64, _i64, _i64, _i]),
+    "qlin_w4a8_linear": (_i, [_p, _i, _i64, _i64, _i64, _p, _i, _i, _i64, _p, _i, _i, _p, _i, _p, _i, _i64, _p, _sz,
+                              _p]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

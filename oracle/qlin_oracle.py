@@ -239,19 +239,27 @@ def unpack_w6_interleaved(packed: np.ndarray, k: int) -> np.ndarray:
     return out
 
 
-def grouped_linear_a8(x_fp16: np.ndarray, wq: np.ndarray, group_scale: np.ndarray, group: int,
-                      bias=None):
+def grouped_linear_a8(x, wq: np.ndarray, group_scale: np.ndarray, group: int, bias=None):
     """Reference for the W4A8 / W6A8 benchmark layouts.
 
-    Activations are quantized per token with `quantize_int8_rowwise` (fp16 arithmetic, fp32
-    scale).  For every K-group g the int32 partial P_g = xq[:, g] . wq[:, g]^T is formed exactly
-    (int64 here), then Y = sx[m] * sum_g s[n, g] * P_g[m, n] (+ bias), in float64.
-    Returns (Y float64, xq int8, sx float32, P int64 [groups, M, N] when small)."""
-    xq, sx = quantize_int8_rowwise(torch.from_numpy(np.asarray(x_fp16, dtype=np.float16)))
-    xq = xq.numpy().astype(np.int64)
-    sx = sx.numpy().astype(np.float64).reshape(-1, 1)
+    Activations are quantized per token with `quantize_int8_rowwise` in their own dtype (a numpy
+    array is taken as fp16; a torch tensor keeps its dtype).  For every K-group g the int32
+    partial P_g = xq[:, g] . wq[:, g]^T is formed exactly (int64 here), then
+    Y = sx[m] * sum_g s[n, g] * P_g[m, n] (+ bias), in float64.
+    Returns (Y float64, xq int8, sx float32)."""
+    xt = x if isinstance(x, torch.Tensor) else torch.from_numpy(np.asarray(x, dtype=np.float16))
+    xq, sx = quantize_int8_rowwise(xt)
+    return grouped_linear_from_codes(xq.numpy(), sx.numpy(), wq, group_scale, group, bias), xq.numpy(), sx.numpy()
+
+
+def grouped_linear_from_codes(xq, sx, wq, group_scale, group: int, bias=None) -> np.ndarray:
+    """Y = sx[m] * sum_g s[n, g] * P_g[m, n] (+ bias) from already-quantized activations;
+    group 0 means one group over all of K with per-channel scales s[n]."""
+    xq = np.asarray(xq, dtype=np.int64)
+    sx = np.asarray(sx, dtype=np.float64).reshape(-1, 1)
     wq = np.asarray(wq, dtype=np.int64)
     n, k = wq.shape
+    group = group or k
     groups = k // group
     s = np.asarray(group_scale, dtype=np.float64).reshape(n, groups)
     y = np.zeros((xq.shape[0], n), dtype=np.float64)
@@ -262,7 +270,7 @@ def grouped_linear_a8(x_fp16: np.ndarray, wq: np.ndarray, group_scale: np.ndarra
     y *= sx
     if bias is not None:
         y += np.asarray(bias, dtype=np.float64)[None, :]
-    return y, xq.astype(np.int8), sx.astype(np.float32)
+    return y
 
 
 def int_group_partials(xq: np.ndarray, wq: np.ndarray, group: int) -> np.ndarray:
