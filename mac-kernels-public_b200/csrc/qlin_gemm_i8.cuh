@@ -10,10 +10,11 @@
 // group.  With one group spanning all of K (per-channel scales) this is a plain int8 GEMM with
 // the scale in the epilogue.
 //
-// Warp roles (576 threads, one CTA per SM, persistent):
+// Warp roles (448 threads, one CTA per SM, persistent):
 //   warp 0        TMA producer            warp 1   TMEM alloc + MMA issuer
-//   warps 2..9    decoders (two groups of four, alternate stages) -> TMEM A operand (int8)
-//   warps 10..17  rescale + epilogue: two warps per TMEM lane quarter, half the columns each
+//   warps 2..5    decoders -> TMEM A operand (int8); each pass decodes two consecutive stages
+//                 and waits for both TMEM stores at once, which hides the store latency
+//   warps 6..13   rescale + epilogue: two warps per TMEM lane quarter, half the columns each
 #pragma once
 #include <cuda.h>
 
@@ -49,9 +50,36 @@ __device__ __forceinline__ float load_bias_i8(const void* bias, int kind, int n)
   return 0.f;
 }
 
+// (a0, a1) += s * ((f0, f1) - 1.5*2^23) with the packed fp32x2 pipe: the subtraction is exact
+// (Sterbenz), so each lane gets s * P rounded once and added once.
+__device__ __forceinline__ void ffma2_sub_magic(float s, float f0, float f1, float& a0, float& a1) {
+  asm("{\n\t.reg .b64 f, m, sc, acc;\n\t"
+      "mov.b64 f, {%2, %3};\n\t"
+      "mov.b64 m, {%4, %4};\n\t"
+      "mov.b64 sc, {%5, %5};\n\t"
+      "mov.b64 acc, {%0, %1};\n\t"
+      "sub.rn.f32x2 f, f, m;\n\t"
+      "fma.rn.f32x2 acc, sc, f, acc;\n\t"
+      "mov.b64 {%0, %1}, acc;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(f0), "f"(f1), "f"(12582912.0f), "f"(s));
+}
+
+// Writes the bit pattern of 1.5*2^23 into COLS consecutive 32-bit TMEM columns of this warp's lanes.
+template <int COLS>
+__device__ __forceinline__ void tmem_fill_bias(uint32_t taddr) {
+  uint32_t r[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) r[i] = 0x4B400000u;
+  static_assert(COLS % 16 == 0, "whole 16-column stores");
+#pragma unroll
+  for (int c = 0; c + 32 <= COLS; c += 32) tmem_st32(taddr + c, r);
+  if constexpr (COLS % 32 != 0) tmem_st16(taddr + (COLS / 32) * 32, *reinterpret_cast<const uint32_t(*)[16]>(r));
+}
+
 template <int TM, int STAGES>
 struct I8Cfg {
-  static constexpr int kDecGroups = 2;
+  static constexpr int kDecGroups = 1;
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 32 * (2 + 4 * kDecGroups + kEpiWarps);
   static constexpr int kXStageBytes = TM * 128;  // TM rows x 128 int8
@@ -112,6 +140,17 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (warp >= 2 + 4 * Cfg::kDecGroups && p.group <= 128) {
+    // Biased accumulators: every int32 buffer starts at the bit pattern of 1.5*2^23, so after the
+    // group's MMAs it holds the float 1.5*2^23 + P exactly (|P| < 2^22).
+    const int ew = warp - (2 + 4 * Cfg::kDecGroups);
+    const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+    for (int b = 0; b < 2; ++b) tmem_fill_bias<TM / 2>(tmem_base + lanes + b * TM + (ew >> 2) * (TM / 2));
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   if (warp == 0) {
     if (elect_one()) {
@@ -146,11 +185,13 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_s8_s32(128, TM);
+      const uint32_t first_acc = p.group <= 128 ? 1u : 0u;  // biased buffers: accumulate onto the bias
       uint32_t it = 0, g_all = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         uint32_t b = 0;
         uint32_t accumulate = 0;
+        int gk = 0;  // K position inside the current group (no divisions on this thread's path)
         for (int kst = 0; kst < p.num_k_stages && ok; ++kst, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -160,18 +201,19 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           const uint64_t b_desc = smem_desc_sw128(smem_u32(sx + s * Cfg::kXStageBytes));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const int kpos = kst * 128 + kk * 32;
-            if (kpos % p.group == 0) {  // first MMA of a group: wait for its accumulator buffer
+            if (gk == 0) {  // first MMA of a group: wait for its accumulator buffer
               b = g_all & 1;
               if (!mbar_wait(&acc_empty[b], ((g_all >> 1) & 1) ^ 1, abort_flag, p.status, 13)) { ok = false; break; }
               tc_fence_after();
-              accumulate = 0;
+              accumulate = first_acc;
             }
             mma_i8_ts(tmem_base + b * TM, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, accumulate);
             accumulate = 1;
-            if ((kpos + 32) % p.group == 0) {
+            gk += 32;
+            if (gk == p.group) {
               tc_commit(&acc_full[b]);
               ++g_all;
+              gk = 0;
             }
           }
           if (!ok) break;
@@ -186,23 +228,32 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     }
   } else if (warp < 2 + 4 * Cfg::kDecGroups) {
     const int quarter = warp & 3;
-    const int dgroup = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
+    const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      for (int kst = 0; kst < p.num_k_stages; ++kst, ++it) {
-        if ((int)(it % Cfg::kDecGroups) != dgroup) continue;
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, abort_flag, p.status, 14)) { ok = false; break; }
+      for (int kst = 0; kst < p.num_k_stages; kst += 2) {
+        const bool two = kst + 1 < p.num_k_stages;
+        const int s0 = it % STAGES, s1 = (it + 1) % STAGES;
+        if (!mbar_wait(&full[s0], (it / STAGES) & 1, abort_flag, p.status, 14)) { ok = false; break; }
         uint32_t a[32];
-        Dec::decode(sw + s * kWStage, r, a);
-        tmem_st32(tmem_base + ((uint32_t)(quarter * 32) << 16) + Cfg::kACol0 + s * 32, a);
+        Dec::decode(sw + s0 * kWStage, r, a);
+        tmem_st32(tmem_base + lanes + Cfg::kACol0 + s0 * 32, a);
+        if (two) {
+          if (!mbar_wait(&full[s1], ((it + 1) / STAGES) & 1, abort_flag, p.status, 14)) { ok = false; break; }
+          uint32_t a1[32];
+          Dec::decode(sw + s1 * kWStage, r, a1);
+          tmem_st32(tmem_base + lanes + Cfg::kACol0 + s1 * 32, a1);
+        }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[s]);
+        if (lane == 0) {
+          mbar_arrive(&a_full[s0]);
+          if (two) mbar_arrive(&a_full[s1]);
+        }
+        it += two ? 2 : 1;
       }
     }
   } else {
@@ -222,24 +273,42 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       float accf[kHalf];
 #pragma unroll
       for (int j = 0; j < kHalf; ++j) accf[j] = 0.f;
+      const __half* gscale = reinterpret_cast<const __half*>(p.scales) + (size_t)min(n, p.N - 1) * p.groups_per_row;
+      float s_next = 0.f;
+      if (n_ok) s_next = (p.scale_kind == I8S_GROUP_F16) ? __half2float(gscale[0]) : reinterpret_cast<const float*>(p.scales)[n];
+      // Exact int32 -> fp32 through the 1.5*2^23 magic number while |P| < 2^22 (groups of <= 128
+      // values of 8-bit x 8-bit products); larger groups use the conversion instruction.
+      const bool magic = p.group <= 128;
       for (int g = 0; g < groups_per_tile; ++g, ++g_all) {
-        float sg = 0.f;
-        if (n_ok) {
-          sg = (p.scale_kind == I8S_GROUP_F16)
-                   ? __half2float(reinterpret_cast<const __half*>(p.scales)[(size_t)n * p.groups_per_row + g])
-                   : reinterpret_cast<const float*>(p.scales)[n];
-        }
+        const float sg = s_next;
+        if (n_ok && p.scale_kind == I8S_GROUP_F16 && g + 1 < groups_per_tile) s_next = __half2float(gscale[g + 1]);
         const uint32_t b = g_all & 1;
         if (!mbar_wait(&acc_full[b], (g_all >> 1) & 1, abort_flag, p.status, 15)) { ok = false; break; }
         tc_fence_after();
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + b * TM + half * kHalf;
+        if (magic) {
 #pragma unroll
-        for (int c0 = 0; c0 < kHalf; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(taddr + c0, v);
-          tmem_wait_ld();
+          for (int c0 = 0; c0 < kHalf; c0 += 32) {
+            constexpr int W = kHalf < 32 ? kHalf : 32;
+            uint32_t v[32];
+            if constexpr (W == 32) tmem_ld32(taddr + c0, v);
+            else tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) accf[c0 + j] = fmaf(sg, (float)(int32_t)v[j], accf[c0 + j]);
+            for (int j = 0; j < W; j += 2) ffma2_sub_magic(sg, __uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                         accf[c0 + j], accf[c0 + j + 1]);
+          }
+          tmem_fill_bias<kHalf>(taddr);  // re-bias the buffer for the group that reuses it
+          tmem_wait_st();
+        } else {
+#pragma unroll
+          for (int c0 = 0; c0 < kHalf; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(taddr + c0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) accf[c0 + j] = fmaf(sg, (float)(int32_t)v[j], accf[c0 + j]);
+          }
         }
         tc_fence_before();
         __syncwarp();
