@@ -7,6 +7,7 @@
 //   * the deterministic split-K reduction + epilogue.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <algorithm>
 #include <cstdint>
 
 #include "qlin_decode.cuh"
@@ -107,13 +108,60 @@ __device__ __forceinline__ float round_to(float v, int dtype) {
   return v;
 }
 
-// Pass structure shared by both prologues: walk the row in warp-sized blocks of G = 32*E values
-// (rotated when rotate != 0), two passes (max, then write).
+// Loads E consecutive elements with one vector load when the row is 16-byte aligned (fp16 / bf16 /
+// fp32 inputs), else element by element; zeros past K.
+template <int E>
+__device__ __forceinline__ void load_vec(const void* x, int dtype, long long ldx, int row, int c, int K, bool vec,
+                                         float (&v)[E]) {
+  if (vec && c + E <= K) {
+    if (dtype == 0) {
+      const float* p = reinterpret_cast<const float*>(x) + (long long)row * ldx + c;
+      if constexpr (E >= 4) {
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+          const float4 f = *reinterpret_cast<const float4*>(p + e);
+          v[e] = f.x; v[e + 1] = f.y; v[e + 2] = f.z; v[e + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = p[e];
+      }
+      return;
+    }
+    const uint16_t* p = reinterpret_cast<const uint16_t*>(x) + (long long)row * ldx + c;
+    uint32_t w[E / 2 > 0 ? E / 2 : 1];
+    if constexpr (E == 8) {
+      const uint4 q = *reinterpret_cast<const uint4*>(p);
+      w[0] = q.x; w[1] = q.y; w[2] = q.z; w[3] = q.w;
+    } else if constexpr (E == 4) {
+      const uint2 q = *reinterpret_cast<const uint2*>(p);
+      w[0] = q.x; w[1] = q.y;
+    } else if constexpr (E == 2) {
+      w[0] = *reinterpret_cast<const uint32_t*>(p);
+    } else {
+      w[0] = p[0];
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const unsigned short h = (unsigned short)((w[e >> 1] >> (16 * (e & 1))) & 0xFFFF);
+      v[e] = dtype == 1 ? __half2float(__ushort_as_half(h)) : __bfloat162float(__ushort_as_bfloat16(h));
+    }
+    return;
+  }
+  load_vals<E>(x, dtype, ldx, row, c, K, v);
+}
+
+// Both prologues: walk the row in warp-sized blocks of G = 32*E values (rotated when rotate != 0).
+// When `staged`, pass 1 keeps the rotated row in shared memory (fp32) and pass 2 reads it from
+// there; otherwise pass 2 reloads and re-rotates.  Pass 2 writes 8 consecutive columns per thread
+// (one 16-byte fp16 store or one 8-byte int8 store).
 template <int E, int MODE>  // MODE 0: fp16 normalize; MODE 1: int8 per-token quantize
 __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ x, int x_dtype, long long ldx, int M,
                                                         int K, int Kp, int rotate_kind, int rotate,
                                                         void* __restrict__ out, int32_t* __restrict__ row_exp,
-                                                        float* __restrict__ row_scale, int perm) {
+                                                        float* __restrict__ row_scale, int perm, int staged,
+                                                        int vec) {
+  extern __shared__ float srow[];
   __shared__ float red[33];
   const int row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -124,12 +172,128 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
   for (int b = warp; b < nblk; b += nwarps) {
     float v[E];
     const int c = b * G + lane * E;
-    load_vals<E>(x, x_dtype, ldx, row, c, K, v);
+    load_vec<E>(x, x_dtype, ldx, row, c, K, vec != 0, v);
     if (rotate) block_hadamard<E>(v, rotate_kind, lane);
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       float t = (MODE == 1) ? round_to(v[e], x_dtype) : v[e];
       amax = fmaxf(amax, fabsf(t));
+      if (staged) srow[c + e] = v[e];
+    }
+  }
+  amax = block_max(amax, red);  // contains __syncthreads, so srow is complete afterwards
+  // Pass 2 helpers
+  auto value_at = [&](int c, float (&v8)[8]) {
+    if (staged) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v8[e] = srow[c + e];
+    }
+  };
+  if (MODE == 0) {
+    int f = 0;
+    if (amax > 0.f && amax <= 3.402823466e38f) {
+      int ex;
+      frexpf(amax, &ex);
+      f = ex - 15;
+    }
+    if (threadIdx.x == 0) row_exp[row] = f;
+    __half* o = reinterpret_cast<__half*>(out) + (long long)row * Kp;
+    if (staged) {
+      for (int c = threadIdx.x * 8; c < Kp; c += blockDim.x * 8) {
+        float v8[8];
+        value_at(c, v8);
+        uint4 pk;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pw[e] = pack_f16x2(ldexpf(v8[2 * e], -f), ldexpf(v8[2 * e + 1], -f));
+        *reinterpret_cast<uint4*>(o + c) = pk;
+      }
+    } else {
+      for (int b = warp; b < nblk; b += nwarps) {
+        float v[E];
+        const int c = b * G + lane * E;
+        load_vec<E>(x, x_dtype, ldx, row, c, K, vec != 0, v);
+        if (rotate) block_hadamard<E>(v, rotate_kind, lane);
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (c + e < Kp) o[c + e] = __float2half_rn(ldexpf(v[e], -f));
+      }
+    }
+  } else {
+    // quantize_int8_rowwise semantics (modal/weight_error_app.py:109-115) in the input dtype.
+    float scale = fmaxf(__fdiv_rn(amax, 127.f), 1e-30f);
+    float s = round_to(scale, x_dtype);
+    if (s == 0.f) s = (x_dtype == 1) ? 6.103515625e-05f : 1.17549435e-38f;
+    if (threadIdx.x == 0) row_scale[row] = scale;
+    int8_t* o = reinterpret_cast<int8_t*>(out) + (long long)row * Kp;
+    auto quant = [&](float v) {
+      const float xv = round_to(v, x_dtype);
+      const float qv = rintf(round_to(__fdiv_rn(xv, s), x_dtype));
+      return (int)fminf(fmaxf(qv, -128.f), 127.f);
+    };
+    if (staged) {
+      for (int c = threadIdx.x * 8; c < Kp; c += blockDim.x * 8) {
+        float v8[8];
+        value_at(c, v8);
+        int q[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = (c + e < K) ? quant(v8[e]) : 0;
+        // perm: within each group of 8 columns, even columns first (0,2,4,6,1,3,5,7)
+        uint32_t lo, hi;
+        if (perm) {
+          lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) | ((uint32_t)(q[6] & 0xFF) << 24);
+          hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+        } else {
+          lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+          hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+        }
+        *reinterpret_cast<uint2*>(o + c) = make_uint2(lo, hi);
+      }
+    } else {
+      for (int b = warp; b < nblk; b += nwarps) {
+        float v[E];
+        const int c = b * G + lane * E;
+        load_vec<E>(x, x_dtype, ldx, row, c, K, vec != 0, v);
+        if (rotate) block_hadamard<E>(v, rotate_kind, lane);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int col = c + e;
+          const int dst = perm ? ((col & ~7) | ((col & 1) ? 4 + ((col & 7) >> 1) : ((col & 7) >> 1))) : col;
+          if (col < Kp) o[dst] = (col < K) ? static_cast<int8_t>(quant(v[e])) : 0;
+        }
+      }
+    }
+  }
+}
+
+// Register-resident variant: each warp keeps its BPW blocks (E values per lane each) in registers
+// between the row-max pass and the write pass, so the row is read from HBM once.  Used when
+// ceil(Kp / G) <= 8 * BPW.  Stores are E-wide vectors (fp16) or, for int8, 8-column groups.
+template <int E, int MODE, int BPW>
+__global__ void __launch_bounds__(512) prologue_reg_kernel(const void* __restrict__ x, int x_dtype, long long ldx,
+                                                            int M, int K, int Kp, int rotate_kind, int rotate,
+                                                            void* __restrict__ out, int32_t* __restrict__ row_exp,
+                                                            float* __restrict__ row_scale, int perm, int vec) {
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  constexpr int G = 32 * E;
+  const int nblk = (Kp + G - 1) / G;
+  float v[BPW][E];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < BPW; ++i) {
+    const int b = warp + nw * i;
+    if (b < nblk) {
+      const int c = b * G + lane * E;
+      load_vec<E>(x, x_dtype, ldx, row, c, K, vec != 0, v[i]);
+      if (rotate) block_hadamard<E>(v[i], rotate_kind, lane);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if (MODE == 1) v[i][e] = round_to(v[i][e], x_dtype);
+        amax = fmaxf(amax, fabsf(v[i][e]));
+      }
     }
   }
   amax = block_max(amax, red);
@@ -142,36 +306,58 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
     }
     if (threadIdx.x == 0) row_exp[row] = f;
     __half* o = reinterpret_cast<__half*>(out) + (long long)row * Kp;
-    for (int b = warp; b < nblk; b += nwarps) {
-      float v[E];
-      const int c = b * G + lane * E;
-      load_vals<E>(x, x_dtype, ldx, row, c, K, v);
-      if (rotate) block_hadamard<E>(v, rotate_kind, lane);
 #pragma unroll
-      for (int e = 0; e < E; ++e)
-        if (c + e < Kp) o[c + e] = __float2half_rn(ldexpf(v[e], -f));
+    for (int i = 0; i < BPW; ++i) {
+      const int b = warp + nw * i;
+      if (b < nblk) {
+        const int c = b * G + lane * E;
+        if (c + E <= Kp) {
+          uint32_t w[(E + 1) / 2];
+#pragma unroll
+          for (int e = 0; e < E; e += 2)
+            w[e / 2] = pack_f16x2(ldexpf(v[i][e], -f), E > 1 ? ldexpf(v[i][e + 1 < E ? e + 1 : e], -f) : 0.f);
+          if constexpr (E == 8) *reinterpret_cast<uint4*>(o + c) = make_uint4(w[0], w[1], w[2], w[3]);
+          else if constexpr (E == 4) *reinterpret_cast<uint2*>(o + c) = make_uint2(w[0], w[1]);
+          else if constexpr (E == 2) *reinterpret_cast<uint32_t*>(o + c) = w[0];
+          else o[c] = __float2half_rn(ldexpf(v[i][0], -f));
+        }
+      }
     }
   } else {
-    // quantize_int8_rowwise semantics (modal/weight_error_app.py:109-115) in the input dtype.
     float scale = fmaxf(__fdiv_rn(amax, 127.f), 1e-30f);
     float s = round_to(scale, x_dtype);
     if (s == 0.f) s = (x_dtype == 1) ? 6.103515625e-05f : 1.17549435e-38f;
     if (threadIdx.x == 0) row_scale[row] = scale;
     int8_t* o = reinterpret_cast<int8_t*>(out) + (long long)row * Kp;
-    for (int b = warp; b < nblk; b += nwarps) {
-      float v[E];
-      const int c = b * G + lane * E;
-      load_vals<E>(x, x_dtype, ldx, row, c, K, v);
-      if (rotate) block_hadamard<E>(v, rotate_kind, lane);
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const float xv = round_to(v[e], x_dtype);
-        float qv = rintf(round_to(__fdiv_rn(xv, s), x_dtype));
-        qv = fminf(fmaxf(qv, -128.f), 127.f);
-        const int col = c + e;
-        // perm: within each group of 8 columns, even columns first (0,2,4,6,1,3,5,7)
-        const int dst = perm ? ((col & ~7) | ((col & 1) ? 4 + ((col & 7) >> 1) : ((col & 7) >> 1))) : col;
-        if (col < Kp) o[dst] = (col < K) ? static_cast<int8_t>(qv) : 0;
+    for (int i = 0; i < BPW; ++i) {
+      const int b = warp + nw * i;
+      if (b < nblk) {
+        const int c = b * G + lane * E;
+        int q[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float qv = rintf(round_to(__fdiv_rn(v[i][e], s), x_dtype));
+          q[e] = (c + e < K) ? (int)fminf(fmaxf(qv, -128.f), 127.f) : 0;
+        }
+        if constexpr (E == 8) {
+          uint32_t lo, hi;
+          if (perm) {  // even columns first within the group of 8
+            lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) | ((uint32_t)(q[6] & 0xFF) << 24);
+            hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+          } else {
+            lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+            hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+          }
+          if (c + 8 <= Kp) *reinterpret_cast<uint2*>(o + c) = make_uint2(lo, hi);
+        } else {
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const int col = c + e;
+            const int dst = perm ? ((col & ~7) | ((col & 1) ? 4 + ((col & 7) >> 1) : ((col & 7) >> 1))) : col;
+            if (col < Kp) o[dst] = static_cast<int8_t>(q[e]);
+          }
+        }
       }
     }
   }
@@ -408,11 +594,43 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int sp
 // ---------------------------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------------------------
+template <int E, int MODE, int BPW>
+static void launch_reg(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int kind, int rotate,
+                       void* out, int32_t* row_exp, float* row_scale, int perm, int vec, cudaStream_t stream) {
+  const int nblk = (Kp + 32 * E - 1) / (32 * E);
+  const int warps = std::min(16, std::max(1, (nblk + BPW - 1) / BPW));
+  prologue_reg_kernel<E, MODE, BPW>
+      <<<M, 32 * warps, 0, stream>>>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, vec);
+}
+
 template <int E, int MODE>
 static void launch_prologue_e(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int kind, int rotate,
                               void* out, int32_t* row_exp, float* row_scale, int perm, cudaStream_t stream) {
-  prologue_kernel<E, MODE>
-      <<<M, 256, 0, stream>>>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm);
+  const int esz = x_dtype == 0 ? 4 : 2;
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) | (uintptr_t)(ldx * esz)) & 15) == 0;
+  const bool out_ok = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && Kp % 8 == 0;
+  const int nblk = (Kp + 32 * E - 1) / (32 * E);
+  constexpr int kMaxBpw = 64 / E;  // at most 64 staged values per thread
+  if (out_ok && nblk <= 16 * kMaxBpw) {
+    // up to 16 warps per row; the fewest blocks per warp that cover the row
+    const int bpw = (nblk + 15) / 16;
+    if (bpw <= 1) return launch_reg<E, MODE, 1>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, vec, stream);
+    if (bpw <= 2) return launch_reg<E, MODE, 2>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, vec, stream);
+    if (bpw <= 4) return launch_reg<E, MODE, 4>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, vec, stream);
+    if (bpw <= 8) return launch_reg<E, MODE, (8 <= kMaxBpw ? 8 : kMaxBpw)>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, vec, stream);
+    if constexpr (kMaxBpw >= 16) {
+      if (bpw <= 16) return launch_reg<E, MODE, 16>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, vec, stream);
+    }
+    if constexpr (kMaxBpw >= 32) {
+      if (bpw <= 32) return launch_reg<E, MODE, 32>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, vec, stream);
+    }
+    if constexpr (kMaxBpw >= 64) {
+      return launch_reg<E, MODE, 64>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, vec, stream);
+    }
+  }
+  // Long rows: two passes over global memory (the second mostly from L2).
+  prologue_kernel<E, MODE><<<M, 256, 0, stream>>>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale,
+                                                  perm, 0, vec ? 1 : 0);
 }
 
 int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int group, int mode, void* out,
