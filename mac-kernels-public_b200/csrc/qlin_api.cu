@@ -1,6 +1,7 @@
 // The C ABI (include/qlin.h): argument checks, workspace carving, prologue + GEMM sequencing.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -155,7 +156,7 @@ int qlin_device_status(int reset, uint32_t* where) {
 
 // ------------------------------------------------------------------------------------------ INT8
 size_t qlin_int8_linear_workspace(int64_t m, int64_t n, int64_t k) {
-  return f16_operand_bytes(m, k) + align256(f16_gemm_partial_bytes((int)m, (int)n, (int)k, 0, 0));
+  return f16_operand_bytes(m, k) + align256(f16_gemm_partial_bytes((int)m, (int)n, (int)k, WF_INT8, 0, 0));
 }
 
 int qlin_int8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q, int64_t n,
@@ -204,7 +205,7 @@ int qlin_int8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
   a.y = y;
   a.y_dtype = out_kind_of(y_dtype);
   a.ldy = ldy;
-  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, 0, 0);
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, WF_INT8, 0, 0);
   a.partial = reinterpret_cast<float*>(ws.take(pb));
   a.partial_bytes = pb;
   if (ws.off > ws.cap && pb > 0) {
@@ -252,10 +253,14 @@ int qlin_gguf_repack(const void* raw, int qtype, int64_t n, int64_t k, void* pac
   return check_cuda("gguf repack launch");
 }
 
+// Workspace of the GGUF linear for any of the supported types (the largest plan's partials).
 size_t qlin_gguf_linear_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, int64_t ldx) {
   (void)x_dtype;
   (void)ldx;
-  return f16_operand_bytes(m, k) + align256(f16_gemm_partial_bytes((int)m, (int)n, (int)k, 0, 0));
+  size_t pb = 0;
+  for (int fmt : {WF_Q8_0, WF_Q6_K})
+    pb = std::max(pb, f16_gemm_partial_bytes((int)m, (int)n, (int)k, fmt, 0, 0));
+  return f16_operand_bytes(m, k) + align256(pb);
 }
 
 int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
@@ -297,7 +302,7 @@ int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
   a.y = y;
   a.y_dtype = out_kind_of(y_dtype);
   a.ldy = ldy;
-  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, 0, 0);
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, qtype, 0, 0);
   a.partial = reinterpret_cast<float*>(ws.take(pb));
   a.partial_bytes = pb;
   if (ws.off > ws.cap && pb > 0) {

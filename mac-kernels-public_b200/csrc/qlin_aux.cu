@@ -562,33 +562,48 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
   for (int i = 0; i < S; ++i) st[128 * 16 * P + r * S + i] = side[i];
 }
 
-// Split-K: y[m,n] = (sum_s partial[s][m][n]) * colscale[n] * 2^f[m] + bias[n], summed in split
-// order (deterministic).
-__global__ void splitk_finalize_kernel(const float* __restrict__ partial, int splits, int M, int N,
+// Split-K: y[m,n] = (sum_s partial[s][n][m]) * colscale[n] * 2^f[m] + bias[n], summed in split
+// order (deterministic).  The partials are n-major ([split][N][Mp]) so the GEMM epilogue writes
+// each thread's tokens contiguously; a 32x32 shared-memory tile transposes them here.
+// grid = (ceil(M/32), ceil(N/32)), block = (32, 8).
+__global__ void splitk_finalize_kernel(const float* __restrict__ partial, int splits, int M, int N, int Mp,
                                        const void* col_scale, int col_scale_kind, const int32_t* w_row_exp,
                                        const int32_t* x_row_exp, const float* x_row_scale, const void* bias,
                                        int bias_kind, void* y, int y_dtype, long long ldy) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long long)M * N) return;
-  const int m = (int)(i / N), n = (int)(i % N);
-  float acc = 0.f;
-  for (int s = 0; s < splits; ++s) acc = __fadd_rn(acc, partial[(long long)s * M * N + i]);
-  float cs = 1.f;
-  if (col_scale_kind == 1) cs = __half2float(reinterpret_cast<const __half*>(col_scale)[n]);
-  else if (col_scale_kind == 2) cs = reinterpret_cast<const float*>(col_scale)[n];
-  else if (col_scale_kind == 3) cs = exp2i(w_row_exp[n]);
-  float o = __fmul_rn(acc, cs);
-  if (x_row_exp != nullptr) o = __fmul_rn(o, exp2i(x_row_exp[m]));
-  if (x_row_scale != nullptr) o = __fmul_rn(o, x_row_scale[m]);
-  float b = 0.f;
-  if (bias_kind == 1) b = __half2float(reinterpret_cast<const __half*>(bias)[n]);
-  else if (bias_kind == 2) b = reinterpret_cast<const float*>(bias)[n];
-  else if (bias_kind == 3) b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
-  o = __fadd_rn(o, b);
-  const long long oi = (long long)m * ldy + n;
-  if (y_dtype == 1) reinterpret_cast<__half*>(y)[oi] = __float2half_rn(o);
-  else if (y_dtype == 2) reinterpret_cast<__nv_bfloat16*>(y)[oi] = __float2bfloat16_rn(o);
-  else reinterpret_cast<float*>(y)[oi] = o;
+  __shared__ float tile[32][33];
+  const int m0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const size_t plane = (size_t)N * Mp;
+  for (int i = ty; i < 32; i += 8) {
+    const int n = n0 + i, m = m0 + tx;
+    float acc = 0.f;
+    if (n < N && m < M) {
+      const float* pp = partial + (size_t)n * Mp + m;
+      for (int s = 0; s < splits; ++s) acc = __fadd_rn(acc, pp[s * plane]);
+    }
+    tile[i][tx] = acc;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int m = m0 + i, n = n0 + tx;
+    if (m >= M || n >= N) continue;
+    float cs = 1.f;
+    if (col_scale_kind == 1) cs = __half2float(reinterpret_cast<const __half*>(col_scale)[n]);
+    else if (col_scale_kind == 2) cs = reinterpret_cast<const float*>(col_scale)[n];
+    else if (col_scale_kind == 3) cs = exp2i(w_row_exp[n]);
+    float o = __fmul_rn(tile[tx][i], cs);
+    if (x_row_exp != nullptr) o = __fmul_rn(o, exp2i(x_row_exp[m]));
+    if (x_row_scale != nullptr) o = __fmul_rn(o, x_row_scale[m]);
+    float b = 0.f;
+    if (bias_kind == 1) b = __half2float(reinterpret_cast<const __half*>(bias)[n]);
+    else if (bias_kind == 2) b = reinterpret_cast<const float*>(bias)[n];
+    else if (bias_kind == 3) b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
+    o = __fadd_rn(o, b);
+    const long long oi = (long long)m * ldy + n;
+    if (y_dtype == 1) reinterpret_cast<__half*>(y)[oi] = __float2half_rn(o);
+    else if (y_dtype == 2) reinterpret_cast<__nv_bfloat16*>(y)[oi] = __float2bfloat16_rn(o);
+    else reinterpret_cast<float*>(y)[oi] = o;
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -680,13 +695,14 @@ void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_s
   gguf_repack_kernel<<<grid, 128, 0, s>>>(raw, qtype, N, K, num_k_stages, out, stage_bytes, P, S);
 }
 
-void launch_splitk_finalize(const float* partial, int splits, int M, int N, const void* col_scale, int cs_kind,
-                            const int32_t* w_row_exp, const int32_t* x_row_exp, const float* x_row_scale,
-                            const void* bias, int bias_kind, void* y, int y_dtype, long long ldy, cudaStream_t s) {
-  const long long total = (long long)M * N;
-  if (total == 0) return;
-  splitk_finalize_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
-      partial, splits, M, N, col_scale, cs_kind, w_row_exp, x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy);
+void launch_splitk_finalize(const float* partial, int splits, int M, int N, int Mp, const void* col_scale,
+                            int cs_kind, const int32_t* w_row_exp, const int32_t* x_row_exp,
+                            const float* x_row_scale, const void* bias, int bias_kind, void* y, int y_dtype,
+                            long long ldy, cudaStream_t s) {
+  if (M == 0 || N == 0) return;
+  dim3 grid((M + 31) / 32, (N + 31) / 32);
+  splitk_finalize_kernel<<<grid, dim3(32, 8), 0, s>>>(partial, splits, M, N, Mp, col_scale, cs_kind, w_row_exp,
+                                                      x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy);
 }
 
 }  // namespace qlin

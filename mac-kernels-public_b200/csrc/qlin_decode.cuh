@@ -91,90 +91,134 @@ struct PlaneStage {
   }
 };
 
-// v = d * q for int8 q (exact in fp32), times 2^-e, rounded to fp16.
+// Scale d * 2^-e as an fp16 pair.  Exact whenever d * 2^-e is a normal fp16 (the row exponent
+// puts the row's largest |w| in [2^14, 2^15), so only blocks more than ~2^22 smaller than the
+// row's largest can fall below the normal range).
+__device__ __forceinline__ __half2 scale_pair(uint32_t d_bits, float rscale) {
+  const __half h = __float2half_rn(__fmul_rn(half_bits_to_float(d_bits), rscale));
+  return __halves2half2(h, h);
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, __half2 d) {
+  __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), d);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Four unsigned bytes b (0..255) -> (b0 - off, b1 - off) and (b2 - off, b3 - off) as exact fp16
+// pairs, off in 0..1024: 0x64XX is the fp16 1024 + XX.
+__device__ __forceinline__ void u8x4_to_f16x4(uint32_t u, uint32_t bias_pair, uint32_t& lo, uint32_t& hi) {
+  const uint32_t a = prmt(u, 0x64646464u, 0x5140u);
+  const uint32_t b = prmt(u, 0x64646464u, 0x7362u);
+  const __half2 bias = *reinterpret_cast<const __half2*>(&bias_pair);
+  __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
+  __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
+  lo = *reinterpret_cast<uint32_t*>(&ha);
+  hi = *reinterpret_cast<uint32_t*>(&hb);
+}
+
+// Q8_0: w = q * d.  int8 -> fp16 exactly, then one correctly rounded fp16 multiply by d * 2^-e:
+// RN16(q * d * 2^-e), the same single rounding as the fp32 decode followed by the fp16 cast.
 struct DecQ8_0 : PlaneStage<4, 4> {
   static constexpr bool kTma = false;
   __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
     const uint32_t dd = *reinterpret_cast<const uint32_t*>(side(st, r));
-    const float d0 = half_bits_to_float(dd) * rscale;
-    const float d1 = half_bits_to_float(dd >> 16) * rscale;
+    const __half2 d0 = scale_pair(dd & 0xFFFF, rscale), d1 = scale_pair(dd >> 16, rscale);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint4 v = chunk(st, j, r);
-      const float d = j < 2 ? d0 : d1;
+      const __half2 d = j < 2 ? d0 : d1;
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        const int8_t b0 = static_cast<int8_t>(w[t] & 0xFF), b1 = static_cast<int8_t>((w[t] >> 8) & 0xFF);
-        const int8_t b2 = static_cast<int8_t>((w[t] >> 16) & 0xFF), b3 = static_cast<int8_t>(w[t] >> 24);
-        out[8 * j + 2 * t + 0] = pack_f16x2(__fmul_rn((float)b0, d), __fmul_rn((float)b1, d));
-        out[8 * j + 2 * t + 1] = pack_f16x2(__fmul_rn((float)b2, d), __fmul_rn((float)b3, d));
+        uint32_t lo, hi;
+        s8x4_to_f16x4(w[t], lo, hi);
+        out[8 * j + 2 * t + 0] = hmul2_u32(lo, d);
+        out[8 * j + 2 * t + 1] = hmul2_u32(hi, d);
       }
     }
   }
 };
 
 // Q4_0 / IQ4_NL: block of 32 values, byte i holds value i (low nibble) and value i+16 (high).
+// Q4_0 value = nib - 8 (exact fp16 via the magic number with offset 1032); IQ4_NL value = the
+// non-linear level (gguf/quants.py:1331) looked up with prmt over four registers of int8 levels.
 template <bool kNL>
 struct DecQ4Block : PlaneStage<2, 4> {
   static constexpr bool kTma = false;
-  __device__ __forceinline__ static float level(uint32_t nib) {
-    if constexpr (kNL) {
-      // IQ4_NL non-linear levels (gguf/quants.py:1331), branch-free table in registers.
-      constexpr int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
-      return (float)kv[nib];
-    } else {
-      return (float)((int)nib - 8);
-    }
+  // nibbles (one per byte, 0..15) -> int8 levels of IQ4_NL, one per byte
+  __device__ __forceinline__ static uint32_t nl_levels(uint32_t x) {
+    const uint32_t t = x & 0x07070707u;
+    const uint32_t u = t | (t >> 4);
+    const uint32_t sel = (u & 0xFFu) | ((u >> 8) & 0xFF00u);
+    const uint32_t lo = prmt(0xBFAD9881u, 0xF6EADDCFu, sel);  // levels 0..7: -127 -104 -83 -65 -49 -35 -22 -10
+    const uint32_t hi = prmt(0x26190D01u, 0x71594535u, sel);  // levels 8..15: 1 13 25 38 53 69 89 113
+    const uint32_t m = ((x >> 3) & 0x01010101u) * 0xFFu;      // bytes whose nibble is >= 8
+    return (hi & m) | (lo & ~m);
   }
   __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
     const uint32_t dd = *reinterpret_cast<const uint32_t*>(side(st, r));
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
-      const float d = half_bits_to_float(blk ? (dd >> 16) : dd) * rscale;
+      const __half2 d = scale_pair(blk ? (dd >> 16) : (dd & 0xFFFF), rscale);
       const uint4 v = chunk(st, blk, r);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-      float vals[32];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
-        vals[i] = __fmul_rn(d, level(byte & 0xF));
-        vals[i + 16] = __fmul_rn(d, level(byte >> 4));
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t nlo = w[t] & 0x0F0F0F0Fu, nhi = (w[t] >> 4) & 0x0F0F0F0Fu;  // values 4t.., 16+4t..
+        uint32_t a0, a1, b0, b1;
+        if constexpr (kNL) {
+          s8x4_to_f16x4(nl_levels(nlo), a0, a1);
+          s8x4_to_f16x4(nl_levels(nhi), b0, b1);
+        } else {
+          u8x4_to_f16x4(nlo, 0x64086408u, a0, a1);  // fp16 1032 = 1024 + 8
+          u8x4_to_f16x4(nhi, 0x64086408u, b0, b1);
+        }
+        out[16 * blk + 2 * t + 0] = hmul2_u32(a0, d);
+        out[16 * blk + 2 * t + 1] = hmul2_u32(a1, d);
+        out[16 * blk + 8 + 2 * t + 0] = hmul2_u32(b0, d);
+        out[16 * blk + 8 + 2 * t + 1] = hmul2_u32(b1, d);
       }
-#pragma unroll
-      for (int c = 0; c < 16; ++c) out[16 * blk + c] = pack_f16x2(vals[2 * c], vals[2 * c + 1]);
     }
   }
 };
 
-// Q4_K: w = (d*sc)*q - dmin*m per 32-value sub-block (gguf/quants.py:504-522).  The products are
-// exact in fp32, so one rounding happens in the subtraction, as in gguf-py.
+// Small non-negative integer (< 2^23) as float, exactly, without the conversion unit.
+__device__ __forceinline__ float small_uint_to_float(uint32_t q) {
+  return __fsub_rn(__uint_as_float(0x4B000000u | q), 8388608.0f);
+}
+
+// Q4_K: w = (d*sc)*q - dmin*m per 32-value sub-block (gguf/quants.py:504-522).  d*sc and dmin*m
+// are exact products; with 2^-e folded into both, fma(ds', q, -dm') rounds once exactly where
+// gguf-py's subtraction rounds.  Then one rounding to fp16.
 struct DecQ4_K : PlaneStage<2, 8> {
   static constexpr bool kTma = false;
   __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
     const uint2 sd = *reinterpret_cast<const uint2*>(side(st, r));
-    const float d = half_bits_to_float(sd.x), dmin = half_bits_to_float(sd.x >> 16);
+    const float d = __fmul_rn(half_bits_to_float(sd.x), rscale), dmin = __fmul_rn(half_bits_to_float(sd.x >> 16), rscale);
     const float ds0 = __fmul_rn(d, (float)(sd.y & 0xFF)), ds1 = __fmul_rn(d, (float)((sd.y >> 8) & 0xFF));
-    const float dm0 = __fmul_rn(dmin, (float)((sd.y >> 16) & 0xFF)), dm1 = __fmul_rn(dmin, (float)(sd.y >> 24));
-    float vals[64];
+    const float dm0 = -__fmul_rn(dmin, (float)((sd.y >> 16) & 0xFF)), dm1 = -__fmul_rn(dmin, (float)(sd.y >> 24));
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const uint4 v = chunk(st, j, r);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
-        const int idx = 16 * j + i;
-        vals[idx] = __fmul_rn(__fsub_rn(__fmul_rn(ds0, (float)(byte & 0xF)), dm0), rscale);
-        vals[32 + idx] = __fmul_rn(__fsub_rn(__fmul_rn(ds1, (float)(byte >> 4)), dm1), rscale);
+      for (int t = 0; t < 4; ++t) {
+        // bytes 16j+4t .. +3: low nibbles are values i, high nibbles values 32+i
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t x = w[t] >> (8 * 2 * h);  // bytes (2h, 2h+1) in the low half
+          const float q0 = small_uint_to_float(x & 0xF), q1 = small_uint_to_float((x >> 8) & 0xF);
+          const float p0 = small_uint_to_float((x >> 4) & 0xF), p1 = small_uint_to_float((x >> 12) & 0xF);
+          const int i = 16 * j + 4 * t + 2 * h;  // value index of q0 (even)
+          out[i / 2] = pack_f16x2(__fmaf_rn(ds0, q0, dm0), __fmaf_rn(ds0, q1, dm0));
+          out[16 + i / 2] = pack_f16x2(__fmaf_rn(ds1, p0, dm1), __fmaf_rn(ds1, p1, dm1));
+        }
       }
     }
-#pragma unroll
-    for (int c = 0; c < 32; ++c) out[c] = pack_f16x2(vals[2 * c], vals[2 * c + 1]);
   }
 };
 
-// Q6_K: w = (d*sc)*(q-32) per 16 values (gguf/quants.py:554-572).
+// Q6_K: w = (d*sc)*(q-32) per 16 values (gguf/quants.py:554-572); 2^-e folded into d*sc (exact).
 struct DecQ6_K : PlaneStage<3, 8> {
   static constexpr bool kTma = false;
   __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
@@ -182,7 +226,7 @@ struct DecQ6_K : PlaneStage<3, 8> {
     const float d = half_bits_to_float(sd.y);
     float ds[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) ds[t] = __fmul_rn(d, (float)(int8_t)((sd.x >> (8 * t)) & 0xFF));
+    for (int t = 0; t < 4; ++t) ds[t] = __fmul_rn(__fmul_rn(d, (float)(int8_t)((sd.x >> (8 * t)) & 0xFF)), rscale);
     const uint4 l0 = chunk(st, 0, r), l1 = chunk(st, 1, r), hv = chunk(st, 2, r);
     const uint32_t lo[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
     const uint32_t hi[4] = {hv.x, hv.y, hv.z, hv.w};
@@ -192,12 +236,12 @@ struct DecQ6_K : PlaneStage<3, 8> {
       const uint32_t lb = (lo[i >> 2] >> (8 * (i & 3))) & 0xFF;
       const int i16 = i & 15;
       const uint32_t hb = (hi[i16 >> 2] >> (8 * (i16 & 3))) & 0xFF;
-      // value i (i<32) and value i+32
       const uint32_t sh_a = (i < 16) ? 0 : 2;  // v[i]: i<16 -> bits 0-1, 16<=i<32 -> bits 2-3
       const uint32_t qa = (lb & 0xF) | (((hb >> sh_a) & 3) << 4);
       const uint32_t qb = (lb >> 4) | (((hb >> (sh_a + 4)) & 3) << 4);
-      vals[i] = __fmul_rn(__fmul_rn(ds[i >> 4], (float)((int)qa - 32)), rscale);
-      vals[i + 32] = __fmul_rn(__fmul_rn(ds[2 + (i >> 4)], (float)((int)qb - 32)), rscale);
+      // (q - 32) exactly: magic 2^23 + q minus (2^23 + 32)
+      vals[i] = __fmul_rn(ds[i >> 4], __fsub_rn(__uint_as_float(0x4B000000u | qa), 8388640.0f));
+      vals[i + 32] = __fmul_rn(ds[2 + (i >> 4)], __fsub_rn(__uint_as_float(0x4B000000u | qb), 8388640.0f));
     }
 #pragma unroll
     for (int c = 0; c < 32; ++c) out[c] = pack_f16x2(vals[2 * c], vals[2 * c + 1]);

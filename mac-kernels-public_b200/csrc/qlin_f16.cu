@@ -88,6 +88,31 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return 0;
 }
 
+// 3-D tile map over a dense [d2][d1][d0] array of `elem`-byte elements (d0 contiguous).
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem, uint64_t d0, uint64_t d1,
+                 uint64_t d2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is unavailable");
+    return 3;
+  }
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * elem, d0 * d1 * elem};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || strides[0] % 16 != 0) {
+    set_error("TMA store target needs 16-byte alignment");
+    return 1;
+  }
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+    return 3;
+  }
+  return 0;
+}
+
 uint32_t gguf_stage_bytes(int qtype, int* P, int* S) {
   int p = 0, s = 0;
   switch (qtype) {
@@ -121,24 +146,40 @@ int gguf_type_size(int qtype) {
   }
 }
 
-void plan_f16(int M, int N, int K, int* tm_out, int* splits_out) {
+// Token tile and K-split plan.  Small M: the smallest tile that holds M (<= 256) and K split
+// across CTAs until the grid covers the SMs.  Large M: 192-token tiles (decode cost per MMA
+// cycle drops by a third against 128, and the accumulator is still double-buffered in TMEM);
+// 256 for Q6_K, whose decode is the heaviest; 128 for INT8 when M splits evenly into 128s.
+void plan_f16(int M, int N, int K, int fmt, int* tm_out, int* splits_out) {
   int tm = *tm_out;
-  // Tuning knob: QLIN_TM forces the token tile (16, 32, 64, 128 or 256) for sweeps.
+  // Tuning knob: QLIN_TM forces the token tile (16, 32, 64, 128, 192 or 256) for sweeps.
   if (tm == 0) {
     static const int forced = [] {
       const char* e = getenv("QLIN_TM");
       return e ? atoi(e) : 0;
     }();
-    if (forced == 16 || forced == 32 || forced == 64 || forced == 128 || forced == 256) tm = forced;
+    if (forced == 16 || forced == 32 || forced == 64 || forced == 128 || forced == 192 || forced == 256) tm = forced;
   }
   if (tm == 0) {
     if (M <= 16) tm = 16;
     else if (M <= 32) tm = 32;
     else if (M <= 64) tm = 64;
-    else tm = 128;
+    else if (M <= 128) tm = 128;
+    else if (M <= 256) tm = 256;  // one token tile; the grid is filled by splitting K
+    else if (fmt == WF_Q6_K) tm = 256;
+    else if (fmt == WF_INT8 && M % 128 == 0 && M % 192 != 0) tm = 128;
+    else tm = 192;
   }
   int splits = *splits_out;
   const int kst = (K + 63) / 64;
+  if (splits == 0) {
+    // Tuning knob: QLIN_SPLITS forces the number of K splits for sweeps.
+    static const int forced_splits = [] {
+      const char* e = getenv("QLIN_SPLITS");
+      return e ? atoi(e) : 0;
+    }();
+    if (forced_splits > 0) splits = forced_splits;
+  }
   if (splits == 0) {
     const int tiles = ((N + 127) / 128) * ((M + tm - 1) / tm);
     const int sms = sm_count();
@@ -157,14 +198,15 @@ void plan_f16(int M, int N, int K, int* tm_out, int* splits_out) {
   *splits_out = splits;
 }
 
-size_t f16_gemm_partial_bytes(int M, int N, int K, int tm, int k_splits) {
-  plan_f16(M, N, K, &tm, &k_splits);
-  return k_splits > 1 ? (size_t)k_splits * M * N * sizeof(float) : 0;
+size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits) {
+  plan_f16(M, N, K, fmt, &tm, &k_splits);
+  const size_t mp = (size_t)(M + tm - 1) / tm * tm;
+  return k_splits > 1 ? (size_t)k_splits * N * mp * sizeof(float) : 0;
 }
 
 template <class Dec, int TM, int STAGES>
-static int launch_one(const F16GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p,
-                      cudaStream_t stream) {
+static int launch_one(const F16GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp,
+                      const GemmParams& p, cudaStream_t stream) {
   constexpr int smem = qgemm_f16_smem_bytes<Dec, TM, STAGES>();
   auto kern = qgemm_f16_kernel<Dec, TM, STAGES>;
   static bool attr_done[64] = {false};
@@ -179,7 +221,7 @@ static int launch_one(const F16GemmArgs& a, const CUtensorMap& tx, const CUtenso
   }
   const int tiles = p.m_tiles * p.n_tiles * p.k_splits;
   const int grid = std::min(tiles, sm_count());
-  kern<<<grid, F16Cfg<TM, STAGES>::kThreads, smem, stream>>>(tx, tw, p);
+  kern<<<grid, F16Cfg<TM, STAGES>::kThreads, smem, stream>>>(tx, tw, tp, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("qgemm_f16 launch failed: %s", cudaGetErrorString(e));
@@ -190,14 +232,15 @@ static int launch_one(const F16GemmArgs& a, const CUtensorMap& tx, const CUtenso
 }
 
 template <class Dec>
-static int dispatch_tm(const F16GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p,
-                       int tm, cudaStream_t stream) {
+static int dispatch_tm(const F16GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp,
+                       const GemmParams& p, int tm, cudaStream_t stream) {
   switch (tm) {
-    case 16: return launch_one<Dec, 16, 8>(a, tx, tw, p, stream);
-    case 32: return launch_one<Dec, 32, 8>(a, tx, tw, p, stream);
-    case 64: return launch_one<Dec, 64, 8>(a, tx, tw, p, stream);
-    case 128: return launch_one<Dec, 128, 6>(a, tx, tw, p, stream);
-    case 256: return launch_one<Dec, 256, 4>(a, tx, tw, p, stream);
+    case 16: return launch_one<Dec, 16, 8>(a, tx, tw, tp, p, stream);
+    case 32: return launch_one<Dec, 32, 8>(a, tx, tw, tp, p, stream);
+    case 64: return launch_one<Dec, 64, 8>(a, tx, tw, tp, p, stream);
+    case 128: return launch_one<Dec, 128, 6>(a, tx, tw, tp, p, stream);
+    case 192: return launch_one<Dec, 192, 4>(a, tx, tw, tp, p, stream);
+    case 256: return launch_one<Dec, 256, 4>(a, tx, tw, tp, p, stream);
     default: set_error("unsupported token tile %d", tm); return 2;
   }
 }
@@ -205,7 +248,7 @@ static int dispatch_tm(const F16GemmArgs& a, const CUtensorMap& tx, const CUtens
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return 0;
   int tm = a.tm, splits = a.k_splits;
-  plan_f16(a.M, a.N, a.K, &tm, &splits);
+  plan_f16(a.M, a.N, a.K, a.fmt, &tm, &splits);
   GemmParams p{};
   p.M = a.M;
   p.N = a.N;
@@ -227,8 +270,9 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   p.ldy = a.ldy;
   p.partial = nullptr;
   p.status = reinterpret_cast<DeviceStatus*>(device_status_ptr());
+  p.Mp = p.m_tiles * tm;
   if (splits > 1) {
-    const size_t need = (size_t)splits * a.M * a.N * sizeof(float);
+    const size_t need = (size_t)splits * a.N * p.Mp * sizeof(float);
     if (a.partial == nullptr || a.partial_bytes < need) {
       set_error("split-K workspace too small: need %zu bytes", need);
       return 2;
@@ -246,19 +290,25 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   } else {
     tw = tx;  // unused by bulk-copy decoders
   }
+  CUtensorMap tp = tx;  // split-K partials [splits][N][Mp] fp32, box {32 tokens, 128 rows}
+  if (splits > 1 && tm >= 32) {
+    rc = make_tmap_3d(&tp, p.partial, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)p.Mp, (uint64_t)a.N,
+                      (uint64_t)splits, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
   switch (a.fmt) {
-    case WF_INT8: rc = dispatch_tm<DecInt8>(a, tx, tw, p, tm, stream); break;
-    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(a, tx, tw, p, tm, stream); break;
-    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(a, tx, tw, p, tm, stream); break;
-    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(a, tx, tw, p, tm, stream); break;
-    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(a, tx, tw, p, tm, stream); break;
-    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(a, tx, tw, p, tm, stream); break;
+    case WF_INT8: rc = dispatch_tm<DecInt8>(a, tx, tw, tp, p, tm, stream); break;
+    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(a, tx, tw, tp, p, tm, stream); break;
+    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(a, tx, tw, tp, p, tm, stream); break;
+    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(a, tx, tw, tp, p, tm, stream); break;
+    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(a, tx, tw, tp, p, tm, stream); break;
+    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(a, tx, tw, tp, p, tm, stream); break;
     default: set_error("unknown weight format %d", a.fmt); return 2;
   }
   if (rc) return rc;
   if (splits > 1) {
-    launch_splitk_finalize(p.partial, splits, a.M, a.N, a.col_scale, a.col_scale_kind, a.w_row_exp, a.x_row_exp,
-                           nullptr, a.bias, a.bias_kind, a.y, a.y_dtype, a.ldy, stream);
+    launch_splitk_finalize(p.partial, splits, a.M, a.N, p.Mp, a.col_scale, a.col_scale_kind, a.w_row_exp,
+                           a.x_row_exp, nullptr, a.bias, a.bias_kind, a.y, a.y_dtype, a.ldy, stream);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       set_error("split-K finalize launch failed: %s", cudaGetErrorString(e));

@@ -42,7 +42,8 @@ struct GemmParams {
   void* y;
   int y_dtype;
   long long ldy;
-  float* partial;  // split-K partial sums [k_splits][M][N]; null when k_splits == 1
+  float* partial;  // split-K partial sums, n-major [k_splits][N][Mp]; null when k_splits == 1
+  int Mp;          // M rounded up to the token tile (row pitch of the partials)
   DeviceStatus* status;
 };
 
@@ -82,7 +83,7 @@ __device__ __forceinline__ void store_out(void* y, int dtype, long long idx, flo
 template <class Dec, int TM, int STAGES>
 __global__ void __launch_bounds__(448, 1)
 qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                 const GemmParams p) {
+                 const __grid_constant__ CUtensorMap tmap_p, const GemmParams p) {
   using Cfg = F16Cfg<TM, STAGES>;
   constexpr uint32_t kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -98,6 +99,10 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
   uint64_t* drain = acc_empty + 2;          // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Split-K epilogue staging: two 16 KB tiles (128 rows x 32 fp32, 128-byte swizzled) written by
+  // the epilogue warps and stored to the partials with one TMA tensor store each.
+  uint8_t* sepi = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(tmem_slot + 2) + 1023) & ~uintptr_t(1023));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -238,6 +243,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     uint32_t tile_i = 0;
+    uint32_t epi_chunk = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_i) {
       const int mt = t % p.m_tiles;
       const int nt = (t / p.m_tiles) % p.n_tiles;
@@ -257,37 +263,64 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       for (int c0 = 0; c0 < TM; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * Cfg::kAccCols + c0, v);
+        if (p.k_splits > 1) {
+          // n-major partials [split][N][Mp]: this thread's 32 tokens are one 128-byte row of a
+          // swizzled staging tile; one TMA store per chunk writes whole lines
+          tmem_wait_ld();
+          if constexpr (TM >= 32) {
+            const bool issuer = (warp == 2 + 4 * Cfg::kDecGroups) && lane == 0;
+            uint8_t* buf = sepi + (epi_chunk & 1) * 16384;
+            if (issuer) bulk_wait_read<1>();  // the store that last read this buffer is done
+            named_bar_sync(1, 128);
+            uint8_t* rowp = buf + r * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(rowp + ((j ^ (r & 7)) << 4)) =
+                  make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                              __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            fence_proxy_async_smem();
+            named_bar_sync(1, 128);
+            if (issuer) {
+              tma_store_3d(&tmap_p, buf, mt * TM + c0, nt * 128, ks);
+              bulk_commit();
+            }
+            ++epi_chunk;
+          } else {
+            if (n_ok) {
+              float4* dst = reinterpret_cast<float4*>(p.partial + ((size_t)ks * p.N + n) * p.Mp + mt * TM + c0);
+#pragma unroll
+              for (int j = 0; j < TM / 4; ++j)
+                dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                     __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            }
+          }
+          continue;
+        }
         // per-token power of two for the 32 columns of this chunk: lane j holds column j's
         const int mj = mt * TM + c0 + lane;
         const float rs_lane = (p.x_row_exp != nullptr && mj < p.M) ? exp2i(__ldg(&p.x_row_exp[mj])) : 1.f;
         tmem_wait_ld();
-        if (n_ok) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = mt * TM + c0 + j;
-            const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
-            if (m < p.M) {
-              float acc = __uint_as_float(v[j]);
-              if (p.k_splits > 1) {
-                p.partial[((size_t)ks * p.M + m) * p.N + n] = acc;
-              } else {
-                float o = __fmul_rn(__fmul_rn(acc, cs), rs);
-                o = __fadd_rn(o, bias);
-                store_out(p.y, p.y_dtype, (long long)m * p.ldy + n, o);
-              }
-            }
+        for (int j = 0; j < 32; ++j) {
+          const int m = mt * TM + c0 + j;
+          const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
+          if (n_ok && m < p.M) {
+            float o = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs);
+            o = __fadd_rn(o, bias);
+            store_out(p.y, p.y_dtype, (long long)m * p.ldy + n, o);
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) (void)__shfl_sync(0xffffffffu, rs_lane, j);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
+    if (warp == 2 + 4 * Cfg::kDecGroups && lane == 0) bulk_wait_all();  // partial stores complete
   }
 
+  // Warps 0 and 1 ran their loops on one elected lane; reconverge before the block barrier
+  // (barrier.sync is .aligned) and before the warp-wide TMEM dealloc.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -299,7 +332,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
 template <class Dec, int TM, int STAGES>
 constexpr int qgemm_f16_smem_bytes() {
   constexpr int kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
-  return 1024 /*align slack*/ + STAGES * (TM * 128 + kWStage) + (3 * STAGES + 5) * 8 + 16;
+  return 1024 /*align slack*/ + STAGES * (TM * 128 + kWStage) + 1024 /*barriers, aligned*/ + 2 * 16384;
 }
 
 }  // namespace qlin

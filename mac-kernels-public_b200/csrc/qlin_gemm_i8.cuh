@@ -336,6 +336,9 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     }
   }
 
+  // Warps 0 and 1 ran their loops on one elected lane; reconverge before the block barrier
+  // (barrier.sync is .aligned) and before the warp-wide TMEM dealloc.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -12,9 +12,10 @@ void launch_gguf_dequant(const uint8_t* raw, int qtype, long long total, void* o
 void launch_gguf_row_exp(const uint8_t* raw, int qtype, int N, int K, int n_pad, int32_t* row_exp, cudaStream_t s);
 void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_stages, int n_tiles, uint8_t* out,
                         uint32_t stage_bytes, int P, int S, cudaStream_t s);
-void launch_splitk_finalize(const float* partial, int splits, int M, int N, const void* col_scale, int cs_kind,
-                            const int32_t* w_row_exp, const int32_t* x_row_exp, const float* x_row_scale,
-                            const void* bias, int bias_kind, void* y, int y_dtype, long long ldy, cudaStream_t s);
+void launch_splitk_finalize(const float* partial, int splits, int M, int N, int Mp, const void* col_scale,
+                            int cs_kind, const int32_t* w_row_exp, const int32_t* x_row_exp,
+                            const float* x_row_scale, const void* bias, int bias_kind, void* y, int y_dtype,
+                            long long ldy, cudaStream_t s);
 
 // Weight formats of the f16 (weight-only) GEMM family.
 enum WFormat : int { WF_INT8 = 0, WF_Q8_0 = 8, WF_Q4_0 = 2, WF_Q4_K = 12, WF_Q6_K = 14, WF_IQ4_NL = 20 };
@@ -42,8 +43,8 @@ struct F16GemmArgs {
 
 // Returns 0 on success, a positive QLIN_* code on failure (message via set_error).
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream);
-size_t f16_gemm_partial_bytes(int M, int N, int K, int tm, int k_splits);
-void plan_f16(int M, int N, int K, int* tm, int* k_splits);
+size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits);
+void plan_f16(int M, int N, int K, int fmt, int* tm, int* k_splits);
 
 uint32_t gguf_stage_bytes(int qtype, int* P, int* S);
 int gguf_block_values(int qtype);

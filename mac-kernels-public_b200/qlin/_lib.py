@@ -7,7 +7,8 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libqlin.so")
+# QLIN_LIB selects another build of the same library (e.g. one compiled with different flags).
+LIB_PATH = os.environ.get("QLIN_LIB") or os.path.join(_HERE, "libqlin.so")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(f"{LIB_PATH} is missing: build it with `python mac-kernels-public_b200/build.py`")

@@ -1,0 +1,85 @@
+"""Named benchmark configurations, runnable on their own (for profiling and reproduction):
+
+    python -m qlin.cases cfg1_q8_0 --iters 3
+
+Synthetic seeded inputs with the configurations' shapes and value distributions:
+  cfg1_q8_0 / cfg1_q4_0   GGUF Q8_0 / Q4_0 linear, X fp16 [256, 3072], W [3072, 3072]
+  cfg2                    INT8 ConvRot weight-only linear, X [4096, 3072], W [12288, 3072], H-128
+  cfg3                    W4A8, X [4096, 12288], W 4-bit [3072, 12288], group 128
+  cfg4_fwd / cfg4_rev     W6A8, X [3240, 5120] / [3240, 13824], W 6-bit, group 64
+  cfg5_q4k / cfg5_q6k     MMDiT-block GGUF linears, X [4608, 3072] / [4608, 12288]
+"""
+import argparse
+import sys
+
+import torch
+
+import qlin
+
+
+def _gguf_blocks(qtype, n, k, gen, dev):
+    name, qk, ts = qlin.GGUF_TYPES[qtype]
+    nb = n * k // qk
+    raw = torch.randint(0, 256, (nb, ts), generator=gen, dtype=torch.int32).to(torch.uint8)
+    mag = {8: 0.02 / 127, 2: 0.02 / 7, 12: 5e-5, 14: 3e-5, 20: 3e-4}[qtype]
+    offs = {8: [0], 2: [0], 12: [0, 2], 14: [208], 20: [0]}[qtype]
+    for off in offs:
+        d = (torch.randn(nb, generator=gen).abs() * mag).to(torch.float16)
+        raw[:, off:off + 2] = d.view(torch.uint8).reshape(nb, 2)
+    return raw.reshape(n, -1).to(dev)
+
+
+def build(name, dev):
+    """Returns (callable running the op once, flops per call)."""
+    gen = torch.Generator().manual_seed(0)
+    if name.startswith("cfg1") or name.startswith("cfg5"):
+        qtype, m, k, n = {"cfg1_q8_0": (8, 256, 3072, 3072), "cfg1_q4_0": (2, 256, 3072, 3072),
+                          "cfg5_q4k": (12, 4608, 3072, 9216), "cfg5_q6k": (14, 4608, 12288, 3072)}[name]
+        x = torch.randn(m, k, generator=gen).to(torch.float16).to(dev)
+        raw = _gguf_blocks(qtype, n, k, gen, dev)
+        qlin.repack_gguf(raw, qtype, (n, k))
+        return (lambda: qlin.gguf_linear(x, raw, qtype, (n, k))), 2.0 * m * k * n
+    if name == "cfg2":
+        m, k, n = 4096, 3072, 12288
+        x = torch.randn(m, k, generator=gen)
+        x[:, torch.randperm(k, generator=gen)[: k // 100]] *= 20
+        x = x.to(torch.float16).to(dev)
+        q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int32).to(torch.int8).to(dev)
+        s = (torch.randn(n, generator=gen).abs() * 0.02 / 127).to(torch.float16).to(dev)
+        b = (torch.randn(n, generator=gen) * 0.01).to(torch.float16).to(dev)
+        return (lambda: qlin.int8_linear(x, q, s, b, torch.float16, convrot=True, convrot_groupsize=128)), 2.0 * m * k * n
+    m, k, n, bits, grp = {"cfg3": (4096, 12288, 3072, 4, 128), "cfg4_fwd": (3240, 5120, 13824, 6, 64),
+                          "cfg4_rev": (3240, 13824, 5120, 6, 64)}[name]
+    x = torch.randn(m, k, generator=gen).to(torch.float16).to(dev)
+    if bits == 4:
+        u = torch.randint(0, 16, (n, k), generator=gen, dtype=torch.int32)
+        w = (u[:, 0::2] | (u[:, 1::2] << 4)).to(torch.uint8)
+    else:
+        u = torch.randint(0, 64, (n, k), generator=gen, dtype=torch.int64)
+        word = u[:, 0::4] | (u[:, 1::4] << 6) | (u[:, 2::4] << 12) | (u[:, 3::4] << 18)
+        w = torch.stack([word & 0xFF, (word >> 8) & 0xFF, (word >> 16) & 0xFF], dim=-1).reshape(n, -1).to(torch.uint8)
+    w = w.to(dev)
+    s = (torch.randn(n, k // grp, generator=gen).abs() * 0.003).to(torch.float16).to(dev)
+    return (lambda: qlin.w4a8_linear(x, w, s, bits=bits, group_size=grp)), 2.0 * m * k * n
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("--iters", type=int, default=3)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    fn, flops = build(a.case, dev)
+    for _ in range(a.iters):
+        fn()
+    torch.cuda.synchronize()
+    code, where = qlin.device_status()
+    if code:
+        print(f"device wait timed out at {where:#x}", file=sys.stderr)
+        return 1
+    print(f"{a.case}: ran {a.iters} calls ({flops / 1e9:.1f} GFLOP each)")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
