@@ -282,6 +282,38 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
     return out, cfgs
 
 
+def run_mmdit(args, world, dev, flush, stream):
+    """Configuration 5: the MMDiT block linear stack (60 blocks of QKV / out / MLP-up Q4_K and
+    MLP-down Q6_K GGUF linears, 4608 tokens, hidden 3072), weights sharded along N over the ranks,
+    outputs all-gathered with NCCL into column slabs.  Returns whole-job TFLOP/s (strong scaling:
+    the total work is fixed) with the time taken as the max over ranks."""
+    from qlin.sharded import ShardedStack
+    chunks = args.mmdit_chunks or (1 if world == 1 else 4)  # chunks only pay off when a gather overlaps
+    st = ShardedStack(blocks=args.mmdit_blocks, tokens=4608, hidden=3072, chunks=chunks, device=dev)
+    x = torch.randn(4608, 3072, generator=torch.Generator().manual_seed(7)).to(torch.float16).to(dev)
+    for _ in range(2):
+        st.forward(x)
+    torch.cuda.synchronize()
+    st.capture(x)  # one CUDA graph for the whole forward, NCCL gathers included
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    times = timed_steps(st.replay, max(2, args.steps // 8), 1, flush, stream)
+    ms = statistics.mean(times)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    out = {"tflops": st.flops() / (ms * 1e-3) / 1e12, "ms_per_forward": ms, "blocks": args.mmdit_blocks,
+           "chunks": chunks, "n_gpus": world, "scaling": "strong", "timing": "cuda graph replay",
+           "config": "4608 tokens, hidden 3072, QKV/out/up Q4_K + down Q6_K, N-sharded, NCCL all-gather"}
+    st.release()  # graphs holding NCCL calls go before the process group does
+    del st
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank, world):
     import qlin
     from oracle import qlin_oracle as O
@@ -367,6 +399,10 @@ def run_ours(args, rank, world):
     formats["int8_convrot_g128"] = {"tflops": FLOPS / (ms * 1e-3) / 1e12, "ms": ms,
                                     "roofline_frac": roof_t / (ms * 1e-3), "bound": "tensor"}
 
+    mmdit = None
+    if not args.no_mmdit:
+        mmdit = run_mmdit(args, world, dev, flush, stream)
+
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = cpu_baseline()
@@ -384,7 +420,7 @@ def run_ours(args, rank, world):
                                 "note": "whole op (rotation prologue + GEMM) vs max(bytes/HBM, flops/peak)"},
                 "e2e": {"value": world * FLOPS / (t_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
                         "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
-                "cpu_baseline": base, "formats": formats, "configs": configs,
+                "cpu_baseline": base, "formats": formats, "configs": configs, "mmdit_stack": mmdit,
                 "int8_peak_tops_measured": int8_peak, "gpu_launches": 2 * args.steps,
                 "parity_max_abs_rel": err, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
@@ -398,6 +434,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-formats", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-mmdit", action="store_true")
+    ap.add_argument("--mmdit-blocks", type=int, default=60)
+    ap.add_argument("--mmdit-chunks", type=int, default=0)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

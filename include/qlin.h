@@ -82,6 +82,16 @@ int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
                      const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
                      int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The GGUF linear with the fp16 activation given as x_slabs column slabs, [x_slabs][m][k / x_slabs]
+ * (slab i holds columns i*k/x_slabs ...; rows ldx apart, slabs x_slab_stride elements apart) —
+ * the layout an all-gather of column shards produces, consumed in place by the N-sharded multi-GPU
+ * stack.  No counterpart in the reference (which runs on one GPU).  k / x_slabs must be a multiple
+ * of 64.  Workspace: qlin_gguf_linear_workspace(m, n, k, QLIN_F16, ldx). */
+int qlin_gguf_linear_slabs(const void* x, int64_t m, int64_t k, int64_t ldx, int x_slabs, int64_t x_slab_stride,
+                           const void* packed, const int32_t* row_exp, int qtype, int64_t n, const void* bias,
+                           int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
 /* The GGUF linear above with no workspace argument: the scratch (fp16 activation copy and split-K
  * partial sums) lives in a fixed 16 MiB array in device memory that the library reserves on every
  * device that loads it, until the process exits.  It has no counterpart in the reference; it is

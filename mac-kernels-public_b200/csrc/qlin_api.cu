@@ -312,6 +312,51 @@ int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
   return run_f16_gemm(a, stream);
 }
 
+int qlin_gguf_linear_slabs(const void* x, int64_t m, int64_t k, int64_t ldx, int x_slabs, int64_t x_slab_stride,
+                           const void* packed, const int32_t* row_exp, int qtype, int64_t n, const void* bias,
+                           int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                           void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (m < 0 || n < 0 || k <= 0 || x_slabs < 1 || k % x_slabs != 0 || ldx < k / x_slabs || ldy < n ||
+      (x_slabs > 1 && x_slab_stride < m * ldx)) {
+    set_error("bad slab sizes");
+    return QLIN_EINVAL;
+  }
+  if (m == 0 || n == 0) return QLIN_OK;
+  if (gguf_stage_bytes(qtype, nullptr, nullptr) == 0 || k % gguf_block_values(qtype) != 0 ||
+      out_kind_of(y_dtype) < 0 || bias_kind_of(bias, bias_dtype) < 0 || (k / x_slabs) % 64 != 0 || ldx % 8 != 0 ||
+      x_slab_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15)) {
+    set_error("unsupported slab operand (fp16 slabs of a multiple of 64 columns, 16-byte aligned)");
+    return QLIN_EDECLINE;
+  }
+  Carver ws{reinterpret_cast<uint8_t*>(workspace), workspace_bytes};
+  F16GemmArgs a{};
+  a.fmt = qtype;
+  a.x = x;
+  a.ldx = ldx;
+  a.x_slabs = x_slabs;
+  a.x_slab_stride = x_slab_stride;
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.w = packed;
+  a.w_row_exp = row_exp;
+  a.col_scale_kind = CS_EXP2;
+  a.bias = bias;
+  a.bias_kind = bias_kind_of(bias, bias_dtype);
+  a.y = y;
+  a.y_dtype = out_kind_of(y_dtype);
+  a.ldy = ldy;
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, qtype, 0, 0);
+  a.partial = reinterpret_cast<float*>(ws.take(pb));
+  a.partial_bytes = pb;
+  if (ws.off > ws.cap && pb > 0) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  return run_f16_gemm(a, stream);
+}
+
 // Same computation as qlin_gguf_linear, with the workspace taken from the library's static device
 // scratch instead of the caller.  Nothing is allocated, so it suits callers that cannot allocate
 // device memory at call time.  The first call on a device looks up the scratch address (make it

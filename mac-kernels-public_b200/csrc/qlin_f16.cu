@@ -113,6 +113,35 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return 0;
 }
 
+// 3-D tile map with explicit byte strides: dims {d0, d1, d2}, d0 contiguous.
+int make_tmap_3d_strided(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem, uint64_t d0,
+                         uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0,
+                         uint32_t b1, CUtensorMapSwizzle swz) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is unavailable");
+    return 3;
+  }
+  (void)elem;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || stride1_bytes % 16 != 0 || stride2_bytes % 16 != 0) {
+    set_error("TMA operand needs a 16-byte aligned base and strides (row pitch %llu, slab stride %llu bytes)",
+              (unsigned long long)stride1_bytes, (unsigned long long)stride2_bytes);
+    return 1;
+  }
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (3-D) failed (%d): %llu x %llu x %llu", (int)r, (unsigned long long)d0,
+              (unsigned long long)d1, (unsigned long long)d2);
+    return 3;
+  }
+  return 0;
+}
+
 uint32_t gguf_stage_bytes(int qtype, int* P, int* S) {
   int p = 0, s = 0;
   switch (qtype) {
@@ -280,8 +309,18 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
     p.partial = a.partial;
   }
   CUtensorMap tx, tw;
-  int rc = make_tmap_2d(&tx, a.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)a.K, (uint64_t)a.M,
-                        (uint64_t)a.ldx * 2, 64, (uint32_t)tm, CU_TENSOR_MAP_SWIZZLE_128B);
+  // Activation map: 3-D {K per slab, M, slabs}; an ordinary X is one slab.
+  const int slabs = a.x_slabs > 0 ? a.x_slabs : 1;
+  const long long k_slab = a.K / slabs;
+  if (slabs > 1 && (a.K % slabs != 0 || k_slab % 64 != 0)) {
+    set_error("slab width %lld must be a multiple of 64", k_slab);
+    return 1;
+  }
+  p.k_slab = (int)k_slab;
+  int rc = make_tmap_3d_strided(&tx, a.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k_slab, (uint64_t)a.M,
+                                (uint64_t)slabs, (uint64_t)a.ldx * 2,
+                                (uint64_t)(slabs > 1 ? a.x_slab_stride : (long long)a.ldx * a.M) * 2, 64, (uint32_t)tm,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (a.fmt == WF_INT8) {
     rc = make_tmap_2d(&tw, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, 64,

@@ -28,6 +28,8 @@ namespace qlin {
 struct GemmParams {
   int M, N, K;
   int num_k_stages;  // stages over the padded K
+  int k_slab;        // K columns per activation slab (the activation is [slabs][M][k_slab]; slabs = 1
+                     // for an ordinary row-major X).  A multiple of 64 when there is more than one slab.
   int m_tiles, n_tiles, k_splits;
   int stages_per_split;
   // weights
@@ -152,7 +154,11 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes + Dec::kStageBytes);
-          tma_load_2d(sx + s * Cfg::kXStageBytes, &tmap_x, &full[s], kst * 64, mt * TM);
+          {
+            const int k0 = kst * 64;
+            const int slab = k0 / p.k_slab;
+            tma_load_3d(sx + s * Cfg::kXStageBytes, &tmap_x, &full[s], k0 - slab * p.k_slab, mt * TM, slab);
+          }
           if constexpr (Dec::kTma) {
             tma_load_2d(sw + s * kWStage, &tmap_w, &full[s], kst * 64, nt * 128);
           } else {

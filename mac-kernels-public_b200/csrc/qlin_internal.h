@@ -24,6 +24,8 @@ struct F16GemmArgs {
   int fmt;
   const void* x;  // fp16 activations [M, ldx] (prologue output or caller's fp16 tensor)
   long long ldx;
+  int x_slabs = 1;             // > 1: X is [x_slabs][M][K / x_slabs] (e.g. an all-gather of column shards)
+  long long x_slab_stride = 0;  // elements between slabs
   int M, N, K;
   const void* w;  // INT8: raw int8 [N, K]; GGUF: repacked stages
   const int32_t* w_row_exp;

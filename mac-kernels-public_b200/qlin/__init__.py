@@ -21,7 +21,7 @@ import torch
 from . import _lib
 from ._lib import QlinDecline, QlinError, check, lib
 
-__all__ = ["int8_linear", "gguf_linear", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear",
+__all__ = ["int8_linear", "gguf_linear", "gguf_linear_slabs", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear",
            "quantize_int8_rowwise", "prologue_f16", "repack_gguf", "GGUF_TYPES", "QlinDecline", "QlinError",
            "device_status"]
 
@@ -182,6 +182,26 @@ def gguf_linear(x, weight, qtype, shape, bias=None, out_dtype=None, lora_down=No
                                None if ws is None else ws.data_ptr(), wsb, _stream(x.device)), "qlin_gguf_linear")
     if lora_down is not None:
         _lora_beside(y, x, lora_down, lora_up, lora_scale)
+    return y
+
+
+def gguf_linear_slabs(x_slabs, packed, row_exp, qtype, n, bias=None, out=None):
+    """GGUF linear on an fp16 activation stored as column slabs, x_slabs [S, M, K/S] (the layout
+    an all-gather of column shards produces).  `packed`, `row_exp` come from repack_gguf.
+    Returns (or fills) out [M, n] fp16."""
+    s_, m, ks = x_slabs.shape
+    k = s_ * ks
+    if x_slabs.dtype != torch.float16 or x_slabs.stride(2) != 1:
+        raise QlinDecline(1, "gguf_linear_slabs needs fp16 slabs with contiguous rows")
+    y = out if out is not None else torch.empty(m, n, dtype=torch.float16, device=x_slabs.device)
+    b = None if bias is None else bias.contiguous()
+    ws_bytes = lib.qlin_gguf_linear_workspace(m, n, k, 1, x_slabs.stride(1))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x_slabs.device)
+    check(lib.qlin_gguf_linear_slabs(x_slabs.data_ptr(), m, k, x_slabs.stride(1), s_, x_slabs.stride(0),
+                                     packed.data_ptr(), row_exp.data_ptr(), int(qtype), n,
+                                     None if b is None else b.data_ptr(), 0 if b is None else _DT[b.dtype],
+                                     y.data_ptr(), 1, y.stride(0), ws.data_ptr(), ws_bytes,
+                                     _stream(x_slabs.device)), "qlin_gguf_linear_slabs")
     return y
 
 

@@ -31,6 +31,8 @@ SIGNATURES = {
     "qlin_gguf_repack": (_i, [_p, _i, _i64, _i64, _p, _sz, _p, _i64, _p]),
     "qlin_gguf_linear_workspace": (_sz, [_i64, _i64, _i64, _i, _i64]),
     "qlin_gguf_linear": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p]),
+    "qlin_gguf_linear_slabs": (_i, [_p, _i64, _i64, _i64, _i, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _sz,
+                                    _p]),
     "qlin_gguf_linear_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p]),
     "qlin_gguf_dequantize": (_i, [_p, _i, _i64, _i64, _p, _i, _p]),
     "qlin_prologue_f16": (_i, [_p, _i, _i64, _i64, _i64, _i, _p, _i64, _p, _p]),
