@@ -282,14 +282,24 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
     return out, cfgs
 
 
+def qlin_status():
+    import qlin
+    return qlin.device_status()
+
+
 def run_mmdit(args, world, dev, flush, stream):
     """Configuration 5: the MMDiT block linear stack (60 blocks of QKV / out / MLP-up Q4_K and
     MLP-down Q6_K GGUF linears, 4608 tokens, hidden 3072), weights sharded along N over the ranks,
-    outputs all-gathered with NCCL into column slabs.  Returns whole-job TFLOP/s (strong scaling:
-    the total work is fixed) with the time taken as the max over ranks."""
+    outputs all-gathered into column slabs -- by the GEMM epilogues' stores into every rank's buffer
+    over NVLink ("peer", the default) or by NCCL all-gathers on a side stream ("nccl").  Returns
+    whole-job TFLOP/s (strong scaling: the total work is fixed) with the time taken as the max over
+    ranks."""
     from qlin.sharded import ShardedStack
-    chunks = args.mmdit_chunks or (1 if world == 1 else 4)  # chunks only pay off when a gather overlaps
-    st = ShardedStack(blocks=args.mmdit_blocks, tokens=4608, hidden=3072, chunks=chunks, device=dev)
+    transport = args.mmdit_transport
+    # chunks only pay off when a separate gather overlaps the next chunk's GEMM
+    chunks = args.mmdit_chunks or (4 if world > 1 and transport == "nccl" else 1)
+    st = ShardedStack(blocks=args.mmdit_blocks, tokens=4608, hidden=3072, chunks=chunks, device=dev,
+                      transport=transport)
     x = torch.randn(4608, 3072, generator=torch.Generator().manual_seed(7)).to(torch.float16).to(dev)
     for _ in range(2):
         st.forward(x)
@@ -306,8 +316,12 @@ def run_mmdit(args, world, dev, flush, stream):
         ms = float(t.item())
     out = {"tflops": st.flops() / (ms * 1e-3) / 1e12, "ms_per_forward": ms, "blocks": args.mmdit_blocks,
            "chunks": chunks, "n_gpus": world, "scaling": "strong", "timing": "cuda graph replay",
-           "config": "4608 tokens, hidden 3072, QKV/out/up Q4_K + down Q6_K, N-sharded, NCCL all-gather"}
-    st.release()  # graphs holding NCCL calls go before the process group does
+           "transport": st.transport if world > 1 else "none",
+           "config": "4608 tokens, hidden 3072, QKV/out/up Q4_K + down Q6_K, N-sharded, all-gathered outputs"}
+    code, where = qlin_status()
+    if code:
+        raise SystemExit(f"MMDiT stack: a kernel gave up a bounded wait (status {code}, where {where:#x})")
+    st.close()  # graphs holding NCCL calls go before the process group does; peer buffers after a barrier
     del st
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -437,6 +451,7 @@ def main():
     ap.add_argument("--no-mmdit", action="store_true")
     ap.add_argument("--mmdit-blocks", type=int, default=60)
     ap.add_argument("--mmdit-chunks", type=int, default=0)
+    ap.add_argument("--mmdit-transport", choices=("peer", "nccl"), default="peer")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -92,6 +92,39 @@ int qlin_gguf_linear_slabs(const void* x, int64_t m, int64_t k, int64_t ldx, int
                            int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Sharded linear fused with the all-gather of its output (one process per GPU of a node).
+ * No counterpart in the reference (which runs on one GPU); it replaces the slab linear above
+ * followed by an all-gather of the world ranks' [m, n] output shards into [world][m][n] slabs.
+ *
+ * Each rank computes its [m, n] shard and its epilogue stores every finished tile into all
+ * ranks' gathered buffers over NVLink: y_ranks[r] is this rank's slab inside rank r's buffer
+ * (row pitch ldy; a peer buffer mapped into this process with qlin_peer_import, or local for
+ * r == rank).  sync_ranks[r] is rank r's flag pad (qlin_peer_sync_bytes() bytes of a buffer
+ * from qlin_peer_alloc, zero at start; mapped likewise).  Before reading x the kernel waits until
+ * every rank finished its previous call of this function; every rank must therefore make the same
+ * sequence of calls.  The wait is bounded by timeout_ms (0: 10 s): on expiry the call's tiles are
+ * skipped and qlin_device_status reports QLIN_ETIMEOUT; the pads are then out of step and must be
+ * reallocated.  Output fp16/bf16 with n and ldy multiples of 8; m, n > 0.
+ * Workspace: qlin_gguf_linear_workspace(m, n, k, QLIN_F16, ldx).
+ * ------------------------------------------------------------------------------------------ */
+#define QLIN_PEER_HANDLE_BYTES 64
+int qlin_gguf_linear_allgather(const void* x, int64_t m, int64_t k, int64_t ldx, int x_slabs, int64_t x_slab_stride,
+                               const void* packed, const int32_t* row_exp, int qtype, int64_t n, const void* bias,
+                               int bias_dtype, int world, int rank, void* const* y_ranks, int y_dtype, int64_t ldy,
+                               void* const* sync_ranks, uint32_t timeout_ms, void* workspace, size_t workspace_bytes,
+                               void* stream);
+size_t qlin_peer_sync_bytes(void);
+/* Zero-filled device memory on the current device that other processes can map (cudaMalloc). */
+int qlin_peer_alloc(size_t bytes, void** ptr);
+int qlin_peer_free(void* ptr);
+/* handle: QLIN_PEER_HANDLE_BYTES bytes (a CUDA IPC memory handle of ptr's allocation, which must
+ * start at ptr: a qlin_peer_alloc pointer).  qlin_peer_import maps another process's buffer
+ * into this one (peer access enabled on first use); qlin_peer_close unmaps it. */
+int qlin_peer_export(const void* ptr, void* handle);
+int qlin_peer_import(const void* handle, void** ptr);
+int qlin_peer_close(void* ptr);
+
 /* The GGUF linear above with no workspace argument: the scratch (fp16 activation copy and split-K
  * partial sums) lives in a fixed 16 MiB array in device memory that the library reserves on every
  * device that loads it, until the process exits.  It has no counterpart in the reference; it is

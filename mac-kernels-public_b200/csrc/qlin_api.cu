@@ -11,6 +11,7 @@
 #include "qlin_internal.h"
 #include "qlin_ptx.cuh"
 #include "qlin_gemm_i8.cuh"
+#include "qlin_peer.cuh"
 
 namespace qlin {
 
@@ -131,6 +132,52 @@ static int noalloc_scratch(void** out) {
 }  // namespace qlin
 
 using namespace qlin;
+
+static int gguf_slabs_impl(const void* x, int64_t m, int64_t k, int64_t ldx, int x_slabs, int64_t x_slab_stride,
+                           const void* packed, const int32_t* row_exp, int qtype, int64_t n, const void* bias,
+                           int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                           void* stream_, const PeerOut* out) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (m < 0 || n < 0 || k <= 0 || x_slabs < 1 || k % x_slabs != 0 || ldx < k / x_slabs || ldy < n ||
+      (x_slabs > 1 && x_slab_stride < m * ldx)) {
+    set_error("bad slab sizes");
+    return QLIN_EINVAL;
+  }
+  if (m == 0 || n == 0) return QLIN_OK;
+  if (gguf_stage_bytes(qtype, nullptr, nullptr) == 0 || k % gguf_block_values(qtype) != 0 ||
+      out_kind_of(y_dtype) < 0 || bias_kind_of(bias, bias_dtype) < 0 || (k / x_slabs) % 64 != 0 || ldx % 8 != 0 ||
+      x_slab_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15)) {
+    set_error("unsupported slab operand (fp16 slabs of a multiple of 64 columns, 16-byte aligned)");
+    return QLIN_EDECLINE;
+  }
+  Carver ws{reinterpret_cast<uint8_t*>(workspace), workspace_bytes};
+  F16GemmArgs a{};
+  a.fmt = qtype;
+  a.x = x;
+  a.ldx = ldx;
+  a.x_slabs = x_slabs;
+  a.x_slab_stride = x_slab_stride;
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.w = packed;
+  a.w_row_exp = row_exp;
+  a.col_scale_kind = CS_EXP2;
+  a.bias = bias;
+  a.bias_kind = bias_kind_of(bias, bias_dtype);
+  a.y = y;
+  a.y_dtype = out_kind_of(y_dtype);
+  a.ldy = ldy;
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, qtype, 0, 0);
+  a.partial = reinterpret_cast<float*>(ws.take(pb));
+  a.partial_bytes = pb;
+  if (ws.off > ws.cap && pb > 0) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  a.out = out;
+  return run_f16_gemm(a, stream);
+}
 
 extern "C" {
 
@@ -315,46 +362,100 @@ int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
 int qlin_gguf_linear_slabs(const void* x, int64_t m, int64_t k, int64_t ldx, int x_slabs, int64_t x_slab_stride,
                            const void* packed, const int32_t* row_exp, int qtype, int64_t n, const void* bias,
                            int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
-                           void* stream_) {
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  if (m < 0 || n < 0 || k <= 0 || x_slabs < 1 || k % x_slabs != 0 || ldx < k / x_slabs || ldy < n ||
-      (x_slabs > 1 && x_slab_stride < m * ldx)) {
-    set_error("bad slab sizes");
+                           void* stream) {
+  return gguf_slabs_impl(x, m, k, ldx, x_slabs, x_slab_stride, packed, row_exp, qtype, n, bias, bias_dtype, y, y_dtype,
+                         ldy, workspace, workspace_bytes, stream, nullptr);
+}
+
+int qlin_gguf_linear_allgather(const void* x, int64_t m, int64_t k, int64_t ldx, int x_slabs, int64_t x_slab_stride,
+                               const void* packed, const int32_t* row_exp, int qtype, int64_t n, const void* bias,
+                               int bias_dtype, int world, int rank, void* const* y_ranks, int y_dtype, int64_t ldy,
+                               void* const* sync_ranks, uint32_t timeout_ms, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || y_ranks == nullptr || sync_ranks == nullptr) {
+    set_error("allgather: world must be 1..%d with 0 <= rank < world and per-rank pointer arrays", kMaxPeers);
     return QLIN_EINVAL;
   }
-  if (m == 0 || n == 0) return QLIN_OK;
-  if (gguf_stage_bytes(qtype, nullptr, nullptr) == 0 || k % gguf_block_values(qtype) != 0 ||
-      out_kind_of(y_dtype) < 0 || bias_kind_of(bias, bias_dtype) < 0 || (k / x_slabs) % 64 != 0 || ldx % 8 != 0 ||
-      x_slab_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15)) {
-    set_error("unsupported slab operand (fp16 slabs of a multiple of 64 columns, 16-byte aligned)");
+  if ((y_dtype != QLIN_F16 && y_dtype != QLIN_BF16) || n % 8 != 0 || ldy % 8 != 0) {
+    set_error("allgather: fp16/bf16 output with n and ldy multiples of 8");
     return QLIN_EDECLINE;
   }
-  Carver ws{reinterpret_cast<uint8_t*>(workspace), workspace_bytes};
-  F16GemmArgs a{};
-  a.fmt = qtype;
-  a.x = x;
-  a.ldx = ldx;
-  a.x_slabs = x_slabs;
-  a.x_slab_stride = x_slab_stride;
-  a.M = (int)m;
-  a.N = (int)n;
-  a.K = (int)k;
-  a.w = packed;
-  a.w_row_exp = row_exp;
-  a.col_scale_kind = CS_EXP2;
-  a.bias = bias;
-  a.bias_kind = bias_kind_of(bias, bias_dtype);
-  a.y = y;
-  a.y_dtype = out_kind_of(y_dtype);
-  a.ldy = ldy;
-  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, qtype, 0, 0);
-  a.partial = reinterpret_cast<float*>(ws.take(pb));
-  a.partial_bytes = pb;
-  if (ws.off > ws.cap && pb > 0) {
-    set_error("workspace too small: need %zu bytes", ws.off);
+  PeerOut po{};
+  po.ndst = world;
+  po.world = world;
+  po.self = rank;
+  po.wait = 1;
+  po.signal = 1;
+  po.timeout_ms = timeout_ms;
+  for (int r = 0; r < world; ++r) {
+    if (y_ranks[r] == nullptr || sync_ranks[r] == nullptr || (reinterpret_cast<uintptr_t>(y_ranks[r]) & 15) ||
+        (reinterpret_cast<uintptr_t>(sync_ranks[r]) & 63)) {
+      set_error("allgather: rank %d output (16-byte) or pad (64-byte) pointer missing or misaligned", r);
+      return QLIN_EINVAL;
+    }
+    po.dst[r] = y_ranks[r];
+    po.sync[r] = reinterpret_cast<PeerSync*>(sync_ranks[r]);
+  }
+  po.own = po.sync[rank];
+  if (m == 0 || n == 0) {
+    set_error("allgather: empty shapes are not supported (every rank must take part in every step)");
     return QLIN_EINVAL;
   }
-  return run_f16_gemm(a, stream);
+  return gguf_slabs_impl(x, m, k, ldx, x_slabs, x_slab_stride, packed, row_exp, qtype, n, bias, bias_dtype,
+                         y_ranks[rank], y_dtype, ldy, workspace, workspace_bytes, stream, &po);
+}
+
+size_t qlin_peer_sync_bytes(void) { return sizeof(PeerSync); }
+
+int qlin_peer_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) {
+    set_error("peer_alloc: null result pointer or zero size");
+    return QLIN_EINVAL;
+  }
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return check_cuda("cudaMalloc (peer buffer)");
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p);
+    return check_cuda("cudaMemset (peer buffer)");
+  }
+  *ptr = p;
+  return QLIN_OK;
+}
+
+int qlin_peer_free(void* ptr) {
+  if (ptr != nullptr && cudaFree(ptr) != cudaSuccess) return check_cuda("cudaFree (peer buffer)");
+  return QLIN_OK;
+}
+
+int qlin_peer_export(const void* ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr) {
+    set_error("peer_export: null pointer");
+    return QLIN_EINVAL;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return check_cuda("cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == QLIN_PEER_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return QLIN_OK;
+}
+
+int qlin_peer_import(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) {
+    set_error("peer_import: null pointer");
+    return QLIN_EINVAL;
+  }
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return check_cuda("cudaIpcOpenMemHandle");
+  return QLIN_OK;
+}
+
+int qlin_peer_close(void* ptr) {
+  if (ptr != nullptr && cudaIpcCloseMemHandle(ptr) != cudaSuccess) return check_cuda("cudaIpcCloseMemHandle");
+  return QLIN_OK;
 }
 
 // Same computation as qlin_gguf_linear, with the workspace taken from the library's static device

@@ -11,6 +11,7 @@
 #include <cstdint>
 
 #include "qlin_decode.cuh"
+#include "qlin_peer.cuh"
 #include "qlin_internal.h"
 
 namespace qlin {
@@ -569,7 +570,7 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
 __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int splits, int M, int N, int Mp,
                                        const void* col_scale, int col_scale_kind, const int32_t* w_row_exp,
                                        const int32_t* x_row_exp, const float* x_row_scale, const void* bias,
-                                       int bias_kind, void* y, int y_dtype, long long ldy) {
+                                       int bias_kind, void* y, int y_dtype, long long ldy, const PeerOut po) {
   __shared__ float tile[32][33];
   const int m0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
@@ -600,9 +601,21 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int sp
     else if (bias_kind == 3) b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
     o = __fadd_rn(o, b);
     const long long oi = (long long)m * ldy + n;
+    if (po.ndst > 0) {
+      // 2-byte output to every destination (this rank's slab in each rank's gathered buffer)
+      const uint16_t bits = y_dtype == 2 ? __bfloat16_as_ushort(__float2bfloat16_rn(o)) : __half_as_ushort(__float2half_rn(o));
+#pragma unroll
+      for (int d = 0; d < kMaxPeers; ++d)
+        if (d < po.ndst) reinterpret_cast<uint16_t*>(po.dst[d])[oi] = bits;
+      continue;
+    }
     if (y_dtype == 1) reinterpret_cast<__half*>(y)[oi] = __float2half_rn(o);
     else if (y_dtype == 2) reinterpret_cast<__nv_bfloat16*>(y)[oi] = __float2bfloat16_rn(o);
     else reinterpret_cast<float*>(y)[oi] = o;
+  }
+  if (po.signal) {
+    __syncthreads();
+    if (tx == 0 && ty == 0) peer_signal_last_cta(po);
   }
 }
 
@@ -698,11 +711,16 @@ void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_s
 void launch_splitk_finalize(const float* partial, int splits, int M, int N, int Mp, const void* col_scale,
                             int cs_kind, const int32_t* w_row_exp, const int32_t* x_row_exp,
                             const float* x_row_scale, const void* bias, int bias_kind, void* y, int y_dtype,
-                            long long ldy, cudaStream_t s) {
+                            long long ldy, cudaStream_t s, const PeerOut* out) {
   if (M == 0 || N == 0) return;
   dim3 grid((M + 31) / 32, (N + 31) / 32);
+  PeerOut po{};
+  if (out != nullptr) {
+    po = *out;
+    po.wait = 0;  // the GEMM that produced the partials waited
+  }
   splitk_finalize_kernel<<<grid, dim3(32, 8), 0, s>>>(partial, splits, M, N, Mp, col_scale, cs_kind, w_row_exp,
-                                                      x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy);
+                                                      x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy, po);
 }
 
 }  // namespace qlin

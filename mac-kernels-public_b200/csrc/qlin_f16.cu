@@ -274,6 +274,17 @@ static int dispatch_tm(const F16GemmArgs& a, const CUtensorMap& tx, const CUtens
   }
 }
 
+// Whole 16-byte pieces of 2-byte output rows can be stored from the shared-memory staging tile.
+// Tuning knob: QLIN_STAGED_OUT=0 keeps per-element stores for sweeps.
+static bool staged_output_ok(const F16GemmArgs& a) {
+  static const bool enabled = [] {
+    const char* e = getenv("QLIN_STAGED_OUT");
+    return !(e && atoi(e) == 0);
+  }();
+  return enabled && (a.y_dtype == OUT_F16 || a.y_dtype == OUT_BF16) && a.N % 8 == 0 && a.ldy % 8 == 0 &&
+         (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+}
+
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return 0;
   int tm = a.tm, splits = a.k_splits;
@@ -300,6 +311,16 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   p.partial = nullptr;
   p.status = reinterpret_cast<DeviceStatus*>(device_status_ptr());
   p.Mp = p.m_tiles * tm;
+  if (a.out != nullptr) {
+    p.out = *a.out;
+    if (splits > 1) {
+      p.out.ndst = 0;  // the GEMM writes partials; the finalize kernel stores the output and signals
+      p.out.signal = 0;
+    }
+  } else if (splits == 1 && staged_output_ok(a)) {
+    p.out.ndst = 1;
+    p.out.dst[0] = a.y;
+  }
   if (splits > 1) {
     const size_t need = (size_t)splits * a.N * p.Mp * sizeof(float);
     if (a.partial == nullptr || a.partial_bytes < need) {
@@ -347,7 +368,7 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   if (rc) return rc;
   if (splits > 1) {
     launch_splitk_finalize(p.partial, splits, a.M, a.N, p.Mp, a.col_scale, a.col_scale_kind, a.w_row_exp,
-                           a.x_row_exp, nullptr, a.bias, a.bias_kind, a.y, a.y_dtype, a.ldy, stream);
+                           a.x_row_exp, nullptr, a.bias, a.bias_kind, a.y, a.y_dtype, a.ldy, stream, a.out);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       set_error("split-K finalize launch failed: %s", cudaGetErrorString(e));

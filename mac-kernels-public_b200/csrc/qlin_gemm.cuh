@@ -21,6 +21,7 @@
 #include <cuda.h>
 
 #include "qlin_decode.cuh"
+#include "qlin_peer.cuh"
 
 namespace qlin {
 
@@ -47,6 +48,10 @@ struct GemmParams {
   float* partial;  // split-K partial sums, n-major [k_splits][N][Mp]; null when k_splits == 1
   int Mp;          // M rounded up to the token tile (row pitch of the partials)
   DeviceStatus* status;
+  // Staged 2-byte output: out.ndst > 0 writes each finished 32-token chunk through shared memory
+  // with 16-byte stores to every destination (this rank's slab in each rank's gathered buffer);
+  // out.wait / out.signal run the cross-rank flag protocol of qlin_peer.cuh.
+  PeerOut out;
 };
 
 template <int TM, int STAGES>
@@ -99,7 +104,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
   uint64_t* acc_full = empty + STAGES;      // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint64_t* drain = acc_empty + 2;          // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* epi_bar = drain + 1;            // [1] epilogue warps' barrier (bounded, unlike bar.sync)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Split-K epilogue staging: two 16 KB tiles (128 rows x 32 fp32, 128-byte swizzled) written by
   // the epilogue warps and stored to the partials with one TMA tensor store each.
@@ -121,7 +127,10 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(epi_bar, 4);
     *abort_flag = 0;
+    // Before any activation is read: every rank finished the previous output-writing kernel.
+    if (p.out.wait && !peer_wait(p.out, p.status, 6)) *abort_flag = 1;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -141,7 +150,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     // ----------------------------------------------------------------- producer
     if (elect_one()) {
       uint32_t it = 0;
-      bool ok = true;
+      bool ok = *abort_flag == 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const int mt = t % p.m_tiles;
         const int rest = t / p.m_tiles;
@@ -182,7 +191,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_f16_f32(128, TM);
       uint32_t it = 0, tile_i = 0;
-      bool ok = true;
+      bool ok = *abort_flag == 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tile_i) {
         const int ks = (t / p.m_tiles) / p.n_tiles;
         const int s0 = ks * p.stages_per_split;
@@ -221,7 +230,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     const int group = (warp - 2) >> 2;  // takes ring iterations it with it % kDecGroups == group
     const int r = quarter * 32 + lane;  // weight row within the tile == TMEM lane
     uint32_t it = 0;
-    bool ok = true;
+    bool ok = *abort_flag == 0;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       const int nt = (t / p.m_tiles) % p.n_tiles;
       const int ks = (t / p.m_tiles) / p.n_tiles;
@@ -249,8 +258,20 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     uint32_t tile_i = 0;
-    uint32_t epi_chunk = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tile_i) {
+    uint32_t epi_chunk = 0, epi_phase = 0;
+    // Barrier of the four epilogue warps.  A bounded mbarrier wait instead of a named barrier:
+    // if another role gives up, the warps leave on the abort flag instead of waiting for a warp
+    // that already left the loop.
+    auto epi_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(epi_bar);
+      const bool ok = mbar_wait(epi_bar, epi_phase & 1, abort_flag, p.status, 7);
+      ++epi_phase;
+      return ok;
+    };
+    bool epi_ok = true;
+    const int etid = threadIdx.x - 32 * (2 + 4 * Cfg::kDecGroups);  // 0..127
+    for (int t = blockIdx.x; t < num_tiles && epi_ok && *abort_flag == 0; t += gridDim.x, ++tile_i) {
       const int mt = t % p.m_tiles;
       const int nt = (t / p.m_tiles) % p.n_tiles;
       const int ks = (t / p.m_tiles) / p.n_tiles;
@@ -277,7 +298,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             const bool issuer = (warp == 2 + 4 * Cfg::kDecGroups) && lane == 0;
             uint8_t* buf = sepi + (epi_chunk & 1) * 16384;
             if (issuer) bulk_wait_read<1>();  // the store that last read this buffer is done
-            named_bar_sync(1, 128);
+            if (!(epi_ok = epi_sync())) break;
             uint8_t* rowp = buf + r * 128;
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -285,7 +306,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
                   make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
                               __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
             fence_proxy_async_smem();
-            named_bar_sync(1, 128);
+            if (!(epi_ok = epi_sync())) break;
             if (issuer) {
               tma_store_3d(&tmap_p, buf, mt * TM + c0, nt * 128, ks);
               bulk_commit();
@@ -303,11 +324,41 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           continue;
         }
         // per-token power of two for the 32 columns of this chunk: lane j holds column j's
+        constexpr int kCh = TM < 32 ? TM : 32;  // tokens of this tile in the chunk
         const int mj = mt * TM + c0 + lane;
-        const float rs_lane = (p.x_row_exp != nullptr && mj < p.M) ? exp2i(__ldg(&p.x_row_exp[mj])) : 1.f;
+        const float rs_lane = (p.x_row_exp != nullptr && mj < p.M && lane < kCh) ? exp2i(__ldg(&p.x_row_exp[mj])) : 1.f;
         tmem_wait_ld();
+        if (p.out.ndst > 0) {
+          // Stage the chunk as [kCh tokens][128 channels] 2-byte values, then copy whole 16-byte
+          // pieces of token rows to every destination.  Two buffers: the barrier after staging
+          // one also orders every thread's reads of the other before it is staged again.
+          uint16_t* buf = reinterpret_cast<uint16_t*>(sepi + (epi_chunk & 1) * 8192);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+          for (int j = 0; j < kCh; ++j) {
+            const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
+            float o = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs);
+            o = __fadd_rn(o, bias);
+            buf[j * 128 + r] = p.y_dtype == OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o))
+                                                     : __half_as_ushort(__float2half_rn(o));
+          }
+          if (!(epi_ok = epi_sync())) break;
+#pragma unroll
+          for (int i = etid; i < kCh * 16; i += 128) {
+            const int m = mt * TM + c0 + (i >> 4);
+            const int n0 = nt * 128 + (i & 15) * 8;
+            if (m < p.M && n0 < p.N) {
+              const uint4 val = reinterpret_cast<const uint4*>(buf)[i];
+              const long long off = (long long)m * p.ldy + n0;
+#pragma unroll
+              for (int d = 0; d < kMaxPeers; ++d)
+                if (d < p.out.ndst) reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out.dst[d]) + off)[0] = val;
+            }
+          }
+          ++epi_chunk;
+          continue;
+        }
+#pragma unroll
+        for (int j = 0; j < kCh; ++j) {
           const int m = mt * TM + c0 + j;
           const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
           if (n_ok && m < p.M) {
@@ -333,6 +384,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
+  if (p.out.signal && threadIdx.x == 0) peer_signal_last_cta(p.out);
 }
 
 template <class Dec, int TM, int STAGES>

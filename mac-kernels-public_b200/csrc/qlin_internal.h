@@ -6,6 +6,8 @@
 
 namespace qlin {
 
+struct PeerOut;
+
 int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int group, int mode, void* out,
                     int32_t* row_exp, float* row_scale, int perm, cudaStream_t stream);
 void launch_gguf_dequant(const uint8_t* raw, int qtype, long long total, void* out, int out_dtype, cudaStream_t s);
@@ -15,7 +17,8 @@ void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_s
 void launch_splitk_finalize(const float* partial, int splits, int M, int N, int Mp, const void* col_scale,
                             int cs_kind, const int32_t* w_row_exp, const int32_t* x_row_exp,
                             const float* x_row_scale, const void* bias, int bias_kind, void* y, int y_dtype,
-                            long long ldy, cudaStream_t s);
+                            long long ldy, cudaStream_t s,
+                            const PeerOut* out = nullptr);
 
 // Weight formats of the f16 (weight-only) GEMM family.
 enum WFormat : int { WF_INT8 = 0, WF_Q8_0 = 8, WF_Q4_0 = 2, WF_Q4_K = 12, WF_Q6_K = 14, WF_IQ4_NL = 20 };
@@ -41,6 +44,7 @@ struct F16GemmArgs {
   size_t partial_bytes;
   int tm;           // token tile (0 = auto)
   int k_splits;     // 0 = auto
+  const PeerOut* out = nullptr;  // peer destinations + flag protocol (null: plain output to y)
 };
 
 // Returns 0 on success, a positive QLIN_* code on failure (message via set_error).

@@ -21,7 +21,7 @@ import torch
 from . import _lib
 from ._lib import QlinDecline, QlinError, check, lib
 
-__all__ = ["int8_linear", "gguf_linear", "gguf_linear_slabs", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear",
+__all__ = ["int8_linear", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear",
            "quantize_int8_rowwise", "prologue_f16", "repack_gguf", "GGUF_TYPES", "QlinDecline", "QlinError",
            "device_status"]
 
@@ -203,6 +203,32 @@ def gguf_linear_slabs(x_slabs, packed, row_exp, qtype, n, bias=None, out=None):
                                      y.data_ptr(), 1, y.stride(0), ws.data_ptr(), ws_bytes,
                                      _stream(x_slabs.device)), "qlin_gguf_linear_slabs")
     return y
+
+
+def gguf_linear_allgather(x_slabs, packed, row_exp, qtype, n, y_ranks, sync_ranks, rank, bias=None,
+                          timeout_ms=0):
+    """gguf_linear_slabs whose [M, n] fp16 output shard is stored by the GEMM's epilogue into every
+    rank's gathered buffer: y_ranks[r] = device address of this rank's slab inside rank r's buffer
+    (row pitch n), sync_ranks[r] = address of rank r's flag pad (see qlin.peer.PeerBuffer).  Every
+    rank of the group must make the same sequence of these calls."""
+    import ctypes
+    s_, m, ks = x_slabs.shape
+    k = s_ * ks
+    if x_slabs.dtype != torch.float16 or x_slabs.stride(2) != 1:
+        raise QlinDecline(1, "gguf_linear_allgather needs fp16 slabs with contiguous rows")
+    world = len(y_ranks)
+    if len(sync_ranks) != world:
+        raise ValueError("one output slab and one flag pad per rank")
+    b = None if bias is None else bias.contiguous()
+    ws_bytes = lib.qlin_gguf_linear_workspace(m, n, k, 1, x_slabs.stride(1))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x_slabs.device)
+    ys = (ctypes.c_void_p * world)(*y_ranks)
+    syncs = (ctypes.c_void_p * world)(*sync_ranks)
+    check(lib.qlin_gguf_linear_allgather(x_slabs.data_ptr(), m, k, x_slabs.stride(1), s_, x_slabs.stride(0),
+                                         packed.data_ptr(), row_exp.data_ptr(), int(qtype), n,
+                                         None if b is None else b.data_ptr(), 0 if b is None else _DT[b.dtype],
+                                         world, rank, ys, 1, n, syncs, int(timeout_ms), ws.data_ptr(), ws_bytes,
+                                         _stream(x_slabs.device)), "qlin_gguf_linear_allgather")
 
 
 def dequantize_gguf(weight, qtype, shape, out_dtype=torch.float32):

@@ -33,6 +33,15 @@ SIGNATURES = {
     "qlin_gguf_linear": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p]),
     "qlin_gguf_linear_slabs": (_i, [_p, _i64, _i64, _i64, _i, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _sz,
                                     _p]),
+    "qlin_gguf_linear_allgather": (_i, [_p, _i64, _i64, _i64, _i, _i64, _p, _p, _i, _i64, _p, _i, _i, _i,
+                                        ctypes.POINTER(_p), _i, _i64, ctypes.POINTER(_p), ctypes.c_uint32, _p, _sz,
+                                        _p]),
+    "qlin_peer_sync_bytes": (_sz, []),
+    "qlin_peer_alloc": (_i, [_sz, ctypes.POINTER(_p)]),
+    "qlin_peer_free": (_i, [_p]),
+    "qlin_peer_export": (_i, [_p, _p]),
+    "qlin_peer_import": (_i, [_p, ctypes.POINTER(_p)]),
+    "qlin_peer_close": (_i, [_p]),
     "qlin_gguf_linear_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p]),
     "qlin_gguf_dequantize": (_i, [_p, _i, _i64, _i64, _p, _i, _p]),
     "qlin_prologue_f16": (_i, [_p, _i, _i64, _i64, _i64, _i, _p, _i64, _p, _p]),

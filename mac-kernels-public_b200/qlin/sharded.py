@@ -7,6 +7,13 @@ slabs [p][M][N/p]; the GEMM reads that layout in place through a 3-D TMA map, so
 is needed.  Tokens are split into chunks that flow through the layers independently: chunk c's
 all-gather (on a side stream) overlaps chunk c+1's GEMM.
 
+Two transports for the gathers:
+  "nccl"  the GEMM writes its local shard; an NCCL all-gather (side stream) assembles the slabs.
+  "peer"  qlin_gguf_linear_allgather: the GEMM's epilogue stores every finished tile straight
+          into all ranks' gathered buffers (CUDA-IPC mappings over NVLink), so the exchange
+          overlaps the GEMM tile by tile, and a flag protocol between the ranks' kernels replaces
+          the collective (no NCCL on the data path, one launch per linear).
+
 Per block (hidden 3072): QKV 3072->9216 (Q4_K), out 3072->3072 (Q4_K), MLP up 3072->12288
 (Q4_K), MLP down 12288->3072 (Q6_K).  Attention and the activation function are not part of the
 linear stack: the out projection reads the block input in place of the attention output, and the
@@ -49,7 +56,7 @@ class ShardedStack:
     qlin.gguf_linear_slabs (tests on CPU ranks pass a reference stand-in to check the plumbing)."""
 
     def __init__(self, blocks=60, tokens=4608, hidden=3072, chunks=4, group=None, device=None, seed=0, op=None,
-                 weights=None):
+                 weights=None, transport="nccl"):
         dist = torch.distributed
         self.group = group
         self.p = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -82,6 +89,12 @@ class ShardedStack:
                     del shard
                 layer[name] = (qtype, n, k, packed, row_exp)
             self.blocks.append(layer)
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport if self.p > 1 else "nccl"
+        if self.transport == "peer":
+            self._init_peer()
+            return
         # Per chunk: local output [mc, n/p] and gathered slabs [p, mc, n/p] per layer kind.
         kw = dict(dtype=torch.float16, device=self.device)
         self.local = {name: [torch.empty(self.mc, n // self.p, **kw) for _ in range(chunks)]
@@ -94,6 +107,37 @@ class ShardedStack:
         self.comm = torch.cuda.Stream(device=self.device) if multi else None
         self.done = {name: [torch.cuda.Event() for _ in range(chunks)] for name, _, _, _ in self.layers} if multi else None
         self.ready = {name: [torch.cuda.Event() for _ in range(chunks)] for name, _, _, _ in self.layers} if multi else None
+
+    def _init_peer(self):
+        """Gathered buffers every rank stores into, [chunks][p][mc][n/p] per layer kind, and the
+        ranks' flag pads."""
+        from .peer import PeerBuffer
+        if not self.cuda:
+            raise ValueError("the peer transport needs CUDA devices")
+        self.bufs, self.gathered, self.local = {}, {}, None
+        for name, _, n, _ in self.layers:
+            slab = self.mc * (n // self.p) * 2
+            self.bufs[name] = PeerBuffer(self.chunks * self.p * slab, self.group, self.device)
+            self.gathered[name] = [self.bufs[name].view((self.p, self.mc, n // self.p), torch.float16,
+                                                        offset=c * self.p * slab) for c in range(self.chunks)]
+        self.pads = PeerBuffer(256, self.group, self.device)
+        self.sync_ranks = [self.pads.ptr(j) for j in range(self.p)]
+        self.y_ranks = {name: [[self.bufs[name].ptr(j, (c * self.p + self.r) * self.mc * (n // self.p) * 2)
+                                for j in range(self.p)] for c in range(self.chunks)]
+                        for name, _, n, _ in self.layers}
+        self.comm = self.done = self.ready = None
+        torch.cuda.synchronize(self.device)
+        torch.distributed.barrier(group=self.group)
+
+    def close(self):
+        """Frees the peer buffers (after a barrier, so no rank still stores into them)."""
+        self.release()
+        if self.transport == "peer" and getattr(self, "pads", None) is not None:
+            torch.cuda.synchronize(self.device)
+            torch.distributed.barrier(group=self.group)
+            for b in list(self.bufs.values()) + [self.pads]:
+                b.close()
+            self.pads = None
 
     def capture(self, x):
         """Records forward(x) once into a CUDA graph (GEMM launches, events and NCCL all-gathers);
@@ -125,6 +169,8 @@ class ShardedStack:
     def forward(self, x):
         """x: [tokens, hidden] fp16 on this rank's device (the same on every rank).  Returns the
         last block's output as chunk slabs ([p, mc, hidden/p] each, or [1, mc, hidden] on one GPU)."""
+        if self.transport == "peer":
+            return self._forward_peer(x)
         multi = self.comm is not None
         comp = torch.cuda.current_stream(self.device) if self.cuda else None
         if multi:
@@ -168,3 +214,19 @@ class ShardedStack:
         if multi:
             comp.wait_stream(self.comm)
         return inp
+
+    def _forward_peer(self, x):
+        inp = [x[c * self.mc:(c + 1) * self.mc].unsqueeze(0) for c in range(self.chunks)]
+        for layer in self.blocks:
+            src = {"qkv": inp, "out": inp}
+            for name, _, _, _ in self.layers:
+                if name == "up":
+                    src["up"] = self.gathered["out"]
+                if name == "down":
+                    src["down"] = self.gathered["up"]
+                qtype, n, k, packed, row_exp = layer[name]
+                for c in range(self.chunks):
+                    qlin.gguf_linear_allgather(src[name][c], packed, row_exp, qtype, n // self.p,
+                                               self.y_ranks[name][c], self.sync_ranks, self.r)
+            inp = self.gathered["down"]
+        return list(inp)
