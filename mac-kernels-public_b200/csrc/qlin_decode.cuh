@@ -182,69 +182,82 @@ struct DecQ4Block : PlaneStage<2, 4> {
   }
 };
 
-// Small non-negative integer (< 2^23) as float, exactly, without the conversion unit.
-__device__ __forceinline__ float small_uint_to_float(uint32_t q) {
-  return __fsub_rn(__uint_as_float(0x4B000000u | q), 8388608.0f);
+// Packed fp16 arithmetic on words holding two fp16 values.
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, __half2 s, __half2 c) {
+  __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&a), s, c);
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// Q4_K: w = (d*sc)*q - dmin*m per 32-value sub-block (gguf/quants.py:504-522).  d*sc and dmin*m
-// are exact products; with 2^-e folded into both, fma(ds', q, -dm') rounds once exactly where
-// gguf-py's subtraction rounds.  Then one rounding to fp16.
+// Q4_K: w = (d*sc)*q - dmin*m per 32-value sub-block (gguf/quants.py:504-522), in packed fp16.
+// Nibbles become exact fp16 pairs through the 0x64 magic byte (1024 + q, minus 1024); the high
+// nibble of a byte is kept in place as 16*q and its scale divided by 16 (exact).  The products
+// d*sc*2^-e and dmin*m*2^-e are formed in fp32 and rounded once to fp16, then one fp16 fma per
+// value: each weight is within two fp16 rounding steps of the exact dequantized value.
 struct DecQ4_K : PlaneStage<2, 8> {
   static constexpr bool kTma = false;
   __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
     const uint2 sd = *reinterpret_cast<const uint2*>(side(st, r));
     const float d = __fmul_rn(half_bits_to_float(sd.x), rscale), dmin = __fmul_rn(half_bits_to_float(sd.x >> 16), rscale);
-    const float ds0 = __fmul_rn(d, (float)(sd.y & 0xFF)), ds1 = __fmul_rn(d, (float)((sd.y >> 8) & 0xFF));
-    const float dm0 = -__fmul_rn(dmin, (float)((sd.y >> 16) & 0xFF)), dm1 = -__fmul_rn(dmin, (float)(sd.y >> 24));
+    const __half2 ds0 = __float2half2_rn(__fmul_rn(d, (float)(sd.y & 0xFF)));
+    const __half2 ds1 = __float2half2_rn(__fmul_rn(__fmul_rn(d, (float)((sd.y >> 8) & 0xFF)), 0.0625f));
+    const __half2 dm0 = __float2half2_rn(-__fmul_rn(dmin, (float)((sd.y >> 16) & 0xFF)));
+    const __half2 dm1 = __float2half2_rn(-__fmul_rn(dmin, (float)(sd.y >> 24)));
+    constexpr uint32_t kMagic = 0x64006400u;  // fp16 (1024, 1024)
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const uint4 v = chunk(st, j, r);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        // bytes 16j+4t .. +3: low nibbles are values i, high nibbles values 32+i
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t x = w[t] >> (8 * 2 * h);  // bytes (2h, 2h+1) in the low half
-          const float q0 = small_uint_to_float(x & 0xF), q1 = small_uint_to_float((x >> 8) & 0xF);
-          const float p0 = small_uint_to_float((x >> 4) & 0xF), p1 = small_uint_to_float((x >> 12) & 0xF);
-          const int i = 16 * j + 4 * t + 2 * h;  // value index of q0 (even)
-          out[i / 2] = pack_f16x2(__fmaf_rn(ds0, q0, dm0), __fmaf_rn(ds0, q1, dm0));
-          out[16 + i / 2] = pack_f16x2(__fmaf_rn(ds1, p0, dm1), __fmaf_rn(ds1, p1, dm1));
-        }
+        // bytes (0,1) and (2,3) of the word under the magic byte: (1024 + byte) pairs
+        const uint32_t a = prmt(w[t], 0x64646464u, 0x5140u), b = prmt(w[t], 0x64646464u, 0x7362u);
+        // low nibbles: values 16j+4t.. of sub-block 2c; high nibbles (x16): sub-block 2c+1
+        out[8 * j + 2 * t + 0] = hfma2_u32(hsub2_u32(a & 0xFF0FFF0Fu, kMagic), ds0, dm0);
+        out[8 * j + 2 * t + 1] = hfma2_u32(hsub2_u32(b & 0xFF0FFF0Fu, kMagic), ds0, dm0);
+        out[16 + 8 * j + 2 * t + 0] = hfma2_u32(hsub2_u32(a & 0xFFF0FFF0u, kMagic), ds1, dm1);
+        out[16 + 8 * j + 2 * t + 1] = hfma2_u32(hsub2_u32(b & 0xFFF0FFF0u, kMagic), ds1, dm1);
       }
     }
   }
 };
 
-// Q6_K: w = (d*sc)*(q-32) per 16 values (gguf/quants.py:554-572); 2^-e folded into d*sc (exact).
+// Q6_K: w = (d*sc)*(q-32) per 16 values (gguf/quants.py:554-572), in packed fp16.  The 6-bit code
+// is assembled under the 0x64 magic byte (low nibble from the 32-byte plane, high two bits from
+// the 16-byte plane) and (1024 + q) - 1056 = q - 32 is exact; d*sc*2^-e is formed in fp32 and
+// rounded once to fp16, then one fp16 multiply per value.
 struct DecQ6_K : PlaneStage<3, 8> {
   static constexpr bool kTma = false;
   __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
     const uint2 sd = *reinterpret_cast<const uint2*>(side(st, r));
-    const float d = half_bits_to_float(sd.y);
-    float ds[4];
+    const float d = __fmul_rn(half_bits_to_float(sd.y), rscale);
+    __half2 ds[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) ds[t] = __fmul_rn(__fmul_rn(d, (float)(int8_t)((sd.x >> (8 * t)) & 0xFF)), rscale);
+    for (int t = 0; t < 4; ++t) ds[t] = __float2half2_rn(__fmul_rn(d, (float)(int8_t)((sd.x >> (8 * t)) & 0xFF)));
     const uint4 l0 = chunk(st, 0, r), l1 = chunk(st, 1, r), hv = chunk(st, 2, r);
     const uint32_t lo[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
     const uint32_t hi[4] = {hv.x, hv.y, hv.z, hv.w};
-    float vals[64];
+    constexpr uint32_t kBias = 0x64206420u;  // fp16 (1056, 1056) = 1024 + 32
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const uint32_t lb = (lo[i >> 2] >> (8 * (i & 3))) & 0xFF;
-      const int i16 = i & 15;
-      const uint32_t hb = (hi[i16 >> 2] >> (8 * (i16 & 3))) & 0xFF;
-      const uint32_t sh_a = (i < 16) ? 0 : 2;  // v[i]: i<16 -> bits 0-1, 16<=i<32 -> bits 2-3
-      const uint32_t qa = (lb & 0xF) | (((hb >> sh_a) & 3) << 4);
-      const uint32_t qb = (lb >> 4) | (((hb >> (sh_a + 4)) & 3) << 4);
-      // (q - 32) exactly: magic 2^23 + q minus (2^23 + 32)
-      vals[i] = __fmul_rn(ds[i >> 4], __fsub_rn(__uint_as_float(0x4B000000u | qa), 8388640.0f));
-      vals[i + 32] = __fmul_rn(ds[2 + (i >> 4)], __fsub_rn(__uint_as_float(0x4B000000u | qb), 8388640.0f));
+    for (int k = 0; k < 8; ++k) {
+      // l bytes 4k..4k+3: low nibbles are values 4k.., high nibbles values 32+4k..; their high
+      // bits sit in h bytes (4k..4k+3) mod 16 at bit 0 (values < 16), 2 (< 32), 4 (< 48), 6.
+      const uint32_t hw = hi[k & 3];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t a = prmt(lo[k], 0x64646464u, h ? 0x7362u : 0x5140u);  // [l, 0x64, l', 0x64]
+        const uint32_t hb = prmt(hw, 0u, h ? 0x4342u : 0x4140u);             // [h, 0, h', 0]
+        const uint32_t hl = (k < 4 ? (hb << 4) : (hb << 2)) & 0x00300030u;
+        const uint32_t hh = ((k < 4 ? hb : (hb >> 2)) & 0x00300030u) | 0x64006400u;
+        const uint32_t ql = (a & 0xFF0FFF0Fu) | hl;            // 1024 + v[4k+2h], v[4k+2h+1]
+        const uint32_t qh = ((a >> 4) & 0x000F000Fu) | hh;     // 1024 + v[32+4k+2h], ...
+        out[2 * k + h] = hmul2_u32(hsub2_u32(ql, kBias), ds[k >> 2]);
+        out[16 + 2 * k + h] = hmul2_u32(hsub2_u32(qh, kBias), ds[2 + (k >> 2)]);
+      }
     }
-#pragma unroll
-    for (int c = 0; c < 32; ++c) out[c] = pack_f16x2(vals[2 * c], vals[2 * c + 1]);
   }
 };
 

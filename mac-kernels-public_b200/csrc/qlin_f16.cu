@@ -233,11 +233,12 @@ size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits
   return k_splits > 1 ? (size_t)k_splits * N * mp * sizeof(float) : 0;
 }
 
-template <class Dec, int TM, int STAGES>
-static int launch_one(const F16GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp,
-                      const GemmParams& p, cudaStream_t stream) {
-  constexpr int smem = qgemm_f16_smem_bytes<Dec, TM, STAGES>();
-  auto kern = qgemm_f16_kernel<Dec, TM, STAGES>;
+template <class Dec, int TM, int STAGES, bool PAIR>
+static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const GemmParams& p,
+                      cudaStream_t stream) {
+  constexpr int smem = qgemm_f16_smem_bytes<Dec, TM, STAGES, PAIR>();
+  static_assert(smem <= 232448, "shared memory per CTA");
+  auto kern = qgemm_f16_kernel<Dec, TM, STAGES, PAIR>;
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -248,30 +249,66 @@ static int launch_one(const F16GemmArgs& a, const CUtensorMap& tx, const CUtenso
     }
     attr_done[dev] = true;
   }
-  const int tiles = p.m_tiles * p.n_tiles * p.k_splits;
-  const int grid = std::min(tiles, sm_count());
-  kern<<<grid, F16Cfg<TM, STAGES>::kThreads, smem, stream>>>(tx, tw, tp, p);
-  cudaError_t e = cudaGetLastError();
+  constexpr int kCtas = PAIR ? 2 : 1;
+  const int tiles = p.m_tiles * (p.n_tiles / kCtas) * p.k_splits;
+  const int grid = kCtas * std::min(tiles, sm_count() / kCtas);
+  cudaError_t e;
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(F16Cfg<TM, STAGES, PAIR>::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, tx, tw, tp, p);
+  } else {
+    kern<<<grid, F16Cfg<TM, STAGES, PAIR>::kThreads, smem, stream>>>(tx, tw, tp, p);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) {
     set_error("qgemm_f16 launch failed: %s", cudaGetErrorString(e));
     return 3;
   }
-  (void)a;
   return 0;
 }
 
+template <class Dec, int TM>
+static int launch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const GemmParams& p,
+                     bool pair, cudaStream_t stream) {
+  if constexpr (TM >= 128) {
+    if (pair) return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, true>(), true>(tx, tw, tp, p, stream);
+  }
+  return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, false>(), false>(tx, tw, tp, p, stream);
+}
+
 template <class Dec>
-static int dispatch_tm(const F16GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp,
-                       const GemmParams& p, int tm, cudaStream_t stream) {
+static int dispatch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const GemmParams& p,
+                       int tm, bool pair, cudaStream_t stream) {
   switch (tm) {
-    case 16: return launch_one<Dec, 16, 8>(a, tx, tw, tp, p, stream);
-    case 32: return launch_one<Dec, 32, 8>(a, tx, tw, tp, p, stream);
-    case 64: return launch_one<Dec, 64, 8>(a, tx, tw, tp, p, stream);
-    case 128: return launch_one<Dec, 128, 6>(a, tx, tw, tp, p, stream);
-    case 192: return launch_one<Dec, 192, 4>(a, tx, tw, tp, p, stream);
-    case 256: return launch_one<Dec, 256, 4>(a, tx, tw, tp, p, stream);
+    case 16: return launch_tm<Dec, 16>(tx, tw, tp, p, pair, stream);
+    case 32: return launch_tm<Dec, 32>(tx, tw, tp, p, pair, stream);
+    case 64: return launch_tm<Dec, 64>(tx, tw, tp, p, pair, stream);
+    case 128: return launch_tm<Dec, 128>(tx, tw, tp, p, pair, stream);
+    case 192: return launch_tm<Dec, 192>(tx, tw, tp, p, pair, stream);
+    case 256: return launch_tm<Dec, 256>(tx, tw, tp, p, pair, stream);
     default: set_error("unsupported token tile %d", tm); return 2;
   }
+}
+
+// Pairs of CTAs (cta_group::2 MMAs, half the activation tile per SM) for token tiles of 128 and
+// more, when the weight tiles pair up.  Tuning knob: QLIN_PAIR=0 keeps single-CTA MMAs for sweeps.
+static bool use_pair(int tm, int n_tiles) {
+  static const bool enabled = [] {
+    const char* e = getenv("QLIN_PAIR");
+    return !(e && atoi(e) == 0);
+  }();
+  return enabled && tm >= 128 && n_tiles % 2 == 0;
 }
 
 // Whole 16-byte pieces of 2-byte output rows can be stored from the shared-memory staging tile.
@@ -338,10 +375,11 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
     return 1;
   }
   p.k_slab = (int)k_slab;
+  const bool pair = use_pair(tm, p.n_tiles);
   int rc = make_tmap_3d_strided(&tx, a.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)k_slab, (uint64_t)a.M,
                                 (uint64_t)slabs, (uint64_t)a.ldx * 2,
-                                (uint64_t)(slabs > 1 ? a.x_slab_stride : (long long)a.ldx * a.M) * 2, 64, (uint32_t)tm,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
+                                (uint64_t)(slabs > 1 ? a.x_slab_stride : (long long)a.ldx * a.M) * 2, 64,
+                                (uint32_t)(pair ? tm / 2 : tm), CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (a.fmt == WF_INT8) {
     rc = make_tmap_2d(&tw, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, 64,
@@ -357,12 +395,12 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
     if (rc) return rc;
   }
   switch (a.fmt) {
-    case WF_INT8: rc = dispatch_tm<DecInt8>(a, tx, tw, tp, p, tm, stream); break;
-    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(a, tx, tw, tp, p, tm, stream); break;
-    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(a, tx, tw, tp, p, tm, stream); break;
-    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(a, tx, tw, tp, p, tm, stream); break;
-    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(a, tx, tw, tp, p, tm, stream); break;
-    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(a, tx, tw, tp, p, tm, stream); break;
+    case WF_INT8: rc = dispatch_tm<DecInt8>(tx, tw, tp, p, tm, pair, stream); break;
+    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, p, tm, pair, stream); break;
+    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(tx, tw, tp, p, tm, pair, stream); break;
+    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(tx, tw, tp, p, tm, pair, stream); break;
+    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(tx, tw, tp, p, tm, pair, stream); break;
+    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(tx, tw, tp, p, tm, pair, stream); break;
     default: set_error("unknown weight format %d", a.fmt); return 2;
   }
   if (rc) return rc;

@@ -15,7 +15,8 @@
 //   warps 2..9   decoders, two groups of four that take alternate pipeline stages: one weight
 //                row per thread, smem -> registers -> TMEM (A operand)
 //   warps 10..13 epilogue: TMEM -> registers, scales, bias, cast, global stores
-// Pipelines: STAGES-deep ring (full / a_full / empty) and a double-buffered accumulator
+// Pipelines: a STAGES-deep shared-memory ring (full / empty), a ring of decoded-weight slots in
+// TMEM (a_full / a_empty) and a double-buffered accumulator
 // (acc_full / acc_empty) so the epilogue of one tile overlaps the MMAs of the next.
 #pragma once
 #include <cuda.h>
@@ -54,15 +55,28 @@ struct GemmParams {
   PeerOut out;
 };
 
-template <int TM, int STAGES>
+// Two rings: STAGES shared-memory stages (activation tile + packed weights, filled by TMA) and
+// kASlots decoded-weight slots in TMEM (32 columns each).  TMEM holds the accumulators too, so
+// it bounds the slots; the shared-memory ring can run deeper and keep more loads in flight.
+//
+// PAIR: the CTAs of a 2-CTA cluster share cta_group::2 MMAs of 256 weight rows (128 decoded into
+// each CTA's TMEM) by TM tokens (TM/2 loaded into each CTA's shared memory), so each SM streams
+// half of the activation tile per MMA.  The even CTA issues the MMAs; decoders and epilogues of
+// both CTAs arrive on its barriers, and its commits arrive on the barriers of both.
+template <int TM, int STAGES, bool PAIR = false>
 struct F16Cfg {
+  static constexpr int kCtas = PAIR ? 2 : 1;
   static constexpr int kDecGroups = 2;
   static constexpr int kThreads = 32 * (2 + 4 * kDecGroups + 4);
-  static constexpr int kXStageBytes = TM * 128;  // TM rows x 64 fp16
-  static constexpr int kAccBufs = (2 * TM + STAGES * 32 <= 512) ? 2 : 1;
+  static constexpr int kXRows = TM / kCtas;              // activation rows this CTA loads per stage
+  static constexpr int kXStageBytes = kXRows * 128;      // kXRows rows x 64 fp16
+  static constexpr int kAccBufs = (2 * TM + 4 * 32 <= 512) ? 2 : 1;
   static constexpr int kAccCols = TM;
-  static constexpr int kACol0 = kAccBufs * TM;  // first TMEM column of the A stages
+  static constexpr int kACol0 = kAccBufs * TM;  // first TMEM column of the A slots
+  static constexpr int kASlotsMax = (512 - kAccBufs * TM) / 32;
+  static constexpr int kASlots = STAGES < kASlotsMax ? STAGES : (kASlotsMax < 8 ? kASlotsMax : 8);
   static constexpr uint32_t kTmemCols = 512;
+  static_assert(kASlots >= 2, "at least two decoded-weight slots");
 };
 
 __device__ __forceinline__ float load_bias(const void* bias, int kind, int n) {
@@ -87,21 +101,22 @@ __device__ __forceinline__ void store_out(void* y, int dtype, long long idx, flo
   else reinterpret_cast<float*>(y)[idx] = v;
 }
 
-template <class Dec, int TM, int STAGES>
+template <class Dec, int TM, int STAGES, bool PAIR>
 __global__ void __launch_bounds__(448, 1)
 qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                  const __grid_constant__ CUtensorMap tmap_p, const GemmParams p) {
-  using Cfg = F16Cfg<TM, STAGES>;
+  using Cfg = F16Cfg<TM, STAGES, PAIR>;
   constexpr uint32_t kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sx = smem;                                 // STAGES x kXStageBytes
   uint8_t* sw = sx + STAGES * Cfg::kXStageBytes;      // STAGES x kWStage
   uint64_t* bars = reinterpret_cast<uint64_t*>(sw + STAGES * kWStage);
-  uint64_t* full = bars;                    // [STAGES]
-  uint64_t* a_full = full + STAGES;         // [STAGES]
-  uint64_t* empty = a_full + STAGES;        // [STAGES]
-  uint64_t* acc_full = empty + STAGES;      // [2]
+  uint64_t* full = bars;                    // [STAGES] X + W landed
+  uint64_t* empty = full + STAGES;          // [STAGES] MMAs that read the stage completed
+  uint64_t* a_full = empty + STAGES;        // [kASlots] decoded weights written to TMEM
+  uint64_t* a_empty = a_full + Cfg::kASlots;  // [kASlots] MMAs that read the slot completed
+  uint64_t* acc_full = a_empty + Cfg::kASlots;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint64_t* drain = acc_empty + 2;          // [1]
   uint64_t* epi_bar = drain + 1;            // [1] epilogue warps' barrier (bounded, unlike bar.sync)
@@ -114,17 +129,44 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.m_tiles * p.n_tiles * p.k_splits;
+  // Tiles are (token tile, group of kCtas weight tiles, K split); a CTA of a pair takes weight
+  // tile 2 * group + rank.  Pairs (or single CTAs) walk the tiles persistently.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  const int n_groups = p.n_tiles / Cfg::kCtas;
+  const int num_tiles = p.m_tiles * n_groups * p.k_splits;
+  const int tile0 = blockIdx.x / Cfg::kCtas;
+  const int tile_step = gridDim.x / Cfg::kCtas;
+  auto tile_nt = [&](int t) { return ((t / p.m_tiles) % n_groups) * Cfg::kCtas + (int)rank; };
+  auto tile_ks = [&](int t) { return (t / p.m_tiles) / n_groups; };
+  // Arrivals that the MMA issuer waits for go to the even CTA's barriers; in a single CTA these
+  // are its own.
+  auto arrive_leader = [&](uint64_t* bar) {
+    if constexpr (PAIR) mbar_arrive_cluster(cluster_map(bar, 0));
+    else mbar_arrive(bar);
+  };
+  // MMA completion arrives on the barrier in every CTA of the pair.
+  auto commit_all = [&](uint64_t* bar) {
+    if constexpr (PAIR) {
+      tc_commit_pair(cluster_map(bar, 0));
+      tc_commit_pair(cluster_map(bar, 1));
+    } else {
+      tc_commit(bar);
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&a_full[s], 4);
       mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < Cfg::kASlots; ++a) {
+      mbar_init(&a_full[a], 4 * Cfg::kCtas);
+      mbar_init(&a_empty[a], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 4 * Cfg::kCtas);
     }
     mbar_init(drain, 1);
     mbar_init(epi_bar, 4);
@@ -134,8 +176,13 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_x);
@@ -143,6 +190,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers are initialized before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -151,11 +199,10 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     if (elect_one()) {
       uint32_t it = 0;
       bool ok = *abort_flag == 0;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = tile0; t < num_tiles && ok; t += tile_step) {
         const int mt = t % p.m_tiles;
-        const int rest = t / p.m_tiles;
-        const int nt = rest % p.n_tiles;
-        const int ks = rest / p.n_tiles;
+        const int nt = tile_nt(t);
+        const int ks = tile_ks(t);
         const int s0 = ks * p.stages_per_split;
         const int s1 = min(p.num_k_stages, s0 + p.stages_per_split);
         for (int kst = s0; kst < s1; ++kst, ++it) {
@@ -166,7 +213,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           {
             const int k0 = kst * 64;
             const int slab = k0 / p.k_slab;
-            tma_load_3d(sx + s * Cfg::kXStageBytes, &tmap_x, &full[s], k0 - slab * p.k_slab, mt * TM, slab);
+            tma_load_3d(sx + s * Cfg::kXStageBytes, &tmap_x, &full[s], k0 - slab * p.k_slab,
+                        mt * TM + (int)rank * Cfg::kXRows, slab);
           }
           if constexpr (Dec::kTma) {
             tma_load_2d(sw + s * kWStage, &tmap_w, &full[s], kst * 64, nt * 128);
@@ -188,12 +236,12 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA issuer
-    if (elect_one()) {
-      constexpr uint32_t idesc = idesc_f16_f32(128, TM);
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = idesc_f16_f32(128 * Cfg::kCtas, TM);
       uint32_t it = 0, tile_i = 0;
       bool ok = *abort_flag == 0;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tile_i) {
-        const int ks = (t / p.m_tiles) / p.n_tiles;
+      for (int t = tile0; t < num_tiles && ok; t += tile_step, ++tile_i) {
+        const int ks = tile_ks(t);
         const int s0 = ks * p.stages_per_split;
         const int s1 = min(p.num_k_stages, s0 + p.stages_per_split);
         const int b = (Cfg::kAccBufs == 2) ? (tile_i & 1) : 0;
@@ -203,22 +251,26 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         const uint32_t d_tmem = tmem_base + b * Cfg::kAccCols;
         for (int kst = s0; kst < s1; ++kst, ++it) {
           const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&a_full[s], ph, abort_flag, p.status, 3)) { ok = false; break; }
+          const int as = it % Cfg::kASlots;
+          if (!mbar_wait(&a_full[as], (it / Cfg::kASlots) & 1, abort_flag, p.status, 3)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_tmem = tmem_base + Cfg::kACol0 + s * 32;
+          const uint32_t a_tmem = tmem_base + Cfg::kACol0 + as * 32;
           const uint64_t b_desc = smem_desc_sw128(smem_u32(sx + s * Cfg::kXStageBytes));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            mma_f16_ts(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, (kst > s0 || kk > 0) ? 1u : 0u);
+            const uint32_t acc = (kst > s0 || kk > 0) ? 1u : 0u;
+            if constexpr (PAIR) mma_f16_ts_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, acc);
+            else mma_f16_ts(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, acc);
           }
-          tc_commit(&empty[s]);
+          commit_all(&empty[s]);
+          commit_all(&a_empty[as]);
         }
         if (!ok) break;
-        tc_commit(&acc_full[b]);
+        commit_all(&acc_full[b]);
       }
       // Wait until every MMA this thread issued has completed before TMEM is released.
-      tc_commit(drain);
+      if constexpr (PAIR) tc_commit_pair(cluster_map(drain, 0));
+      else tc_commit(drain);
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(smem_u32(drain), 0)) {
         if (globaltimer() - t0 > QLIN_WAIT_TIMEOUT_NS) break;
@@ -231,9 +283,9 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     const int r = quarter * 32 + lane;  // weight row within the tile == TMEM lane
     uint32_t it = 0;
     bool ok = *abort_flag == 0;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      const int nt = (t / p.m_tiles) % p.n_tiles;
-      const int ks = (t / p.m_tiles) / p.n_tiles;
+    for (int t = tile0; t < num_tiles && ok; t += tile_step) {
+      const int nt = tile_nt(t);
+      const int ks = tile_ks(t);
       const int s0 = ks * p.stages_per_split;
       const int s1 = min(p.num_k_stages, s0 + p.stages_per_split);
       const int n = nt * 128 + r;
@@ -246,11 +298,15 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         if (!mbar_wait(&full[s], ph, abort_flag, p.status, 4)) { ok = false; break; }
         uint32_t a[32];
         Dec::decode(sw + s * kWStage, r, rscale, a);
-        tmem_st32(tmem_base + ((uint32_t)(quarter * 32) << 16) + Cfg::kACol0 + s * 32, a);
+        // the slot's previous weights have been consumed by their MMAs
+        const int as = it % Cfg::kASlots;
+        if (!mbar_wait(&a_empty[as], ((it / Cfg::kASlots) & 1) ^ 1, abort_flag, p.status, 8)) { ok = false; break; }
+        tc_fence_after();
+        tmem_st32(tmem_base + ((uint32_t)(quarter * 32) << 16) + Cfg::kACol0 + as * 32, a);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[s]);
+        if (lane == 0) arrive_leader(&a_full[as]);
       }
     }
   } else {
@@ -271,10 +327,10 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     };
     bool epi_ok = true;
     const int etid = threadIdx.x - 32 * (2 + 4 * Cfg::kDecGroups);  // 0..127
-    for (int t = blockIdx.x; t < num_tiles && epi_ok && *abort_flag == 0; t += gridDim.x, ++tile_i) {
+    for (int t = tile0; t < num_tiles && epi_ok && *abort_flag == 0; t += tile_step, ++tile_i) {
       const int mt = t % p.m_tiles;
-      const int nt = (t / p.m_tiles) % p.n_tiles;
-      const int ks = (t / p.m_tiles) / p.n_tiles;
+      const int nt = tile_nt(t);
+      const int ks = tile_ks(t);
       const int b = (Cfg::kAccBufs == 2) ? (tile_i & 1) : 0;
       const uint32_t aph = (Cfg::kAccBufs == 2) ? ((tile_i >> 1) & 1) : (tile_i & 1);
       if (!mbar_wait(&acc_full[b], aph, abort_flag, p.status, 5)) break;
@@ -370,7 +426,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) arrive_leader(&acc_empty[b]);
     }
     if (warp == 2 + 4 * Cfg::kDecGroups && lane == 0) bulk_wait_all();  // partial stores complete
   }
@@ -380,17 +436,30 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  // A pair: the even CTA's MMAs (which write the odd CTA's TMEM and read its shared memory) have
+  // all completed once its issuer's drain wait returned; neither CTA frees TMEM or exits before.
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
   if (p.out.signal && threadIdx.x == 0) peer_signal_last_cta(p.out);
 }
 
-template <class Dec, int TM, int STAGES>
+template <class Dec, int TM, int STAGES, bool PAIR>
 constexpr int qgemm_f16_smem_bytes() {
   constexpr int kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
-  return 1024 /*align slack*/ + STAGES * (TM * 128 + kWStage) + 1024 /*barriers, aligned*/ + 2 * 16384;
+  return 1024 /*align slack*/ + STAGES * (F16Cfg<TM, STAGES, PAIR>::kXStageBytes + kWStage) +
+         1024 /*barriers, aligned*/ + 2 * 16384;
+}
+
+// Deepest shared-memory ring (at most 8 stages) that fits the 227 KB a CTA may use.
+template <class Dec, int TM, bool PAIR>
+constexpr int qgemm_f16_stages() {
+  constexpr int kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
+  constexpr int fit = (232448 - 1024 - 1024 - 2 * 16384) / ((PAIR ? TM / 2 : TM) * 128 + kWStage);
+  return fit < 8 ? fit : 8;
 }
 
 }  // namespace qlin

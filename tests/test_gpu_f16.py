@@ -87,6 +87,20 @@ def test_gguf_linear_matches_fp64(qlin, qtype, m):
     _check_status(qlin)
 
 
+@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+@pytest.mark.parametrize("m", [600, 1000])
+def test_gguf_linear_cta_pairs_match_fp64(qlin, qtype, m):
+    """Token tiles of 192 / 256 over an even number of 128-row weight tiles: the two-CTA
+    (cta_group::2) kernels, several tiles per CTA pair, a ragged last token tile."""
+    n, k = 512, 768 if qtype in (12, 14) else 640
+    x, raw, b, ref = _gguf_case(qtype, m, n, k, seed=m + qtype)
+    y = qlin.gguf_linear(x.cuda(), torch.from_numpy(raw).cuda(), qtype, (n, k), bias=b.cuda())
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.max_abs_rel(got, ref) <= 2e-3, O.max_abs_rel(got, ref)
+    _check_status(qlin)
+
+
 @pytest.mark.parametrize("qtype", [8, 12])
 @pytest.mark.parametrize("x_dtype,out_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float32),
                                                (torch.float32, torch.float16)])
@@ -126,9 +140,9 @@ def test_gguf_linear_nd_input_and_empty(qlin):
 
 
 @pytest.mark.parametrize("group", [0, 128, 256])
-@pytest.mark.parametrize("m", [1, 16, 100, 256])
-def test_int8_convrot_linear_matches_fp64(qlin, group, m):
-    n, k = 320, 1024
+@pytest.mark.parametrize("m,n", [(1, 320), (16, 320), (100, 320), (256, 320), (256, 512), (768, 1024)])
+def test_int8_convrot_linear_matches_fp64(qlin, group, m, n):
+    k = 1024
     x, q, s, b = O.cfg_int8_convrot(m, k, n, seed=m + group)
     ref = O.int8_convrot_linear_ref(x.float().numpy(), q.numpy(), s.float().numpy(), b.float().numpy(),
                                     group=group or 128, convrot=group > 0)
