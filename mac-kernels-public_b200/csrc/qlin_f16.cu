@@ -175,10 +175,39 @@ int gguf_type_size(int qtype) {
   }
 }
 
-// Token tile and K-split plan.  Small M: the smallest tile that holds M (<= 256) and K split
-// across CTAs until the grid covers the SMs.  Large M: 192-token tiles (decode cost per MMA
-// cycle drops by a third against 128, and the accumulator is still double-buffered in TMEM);
-// 256 for Q6_K, whose decode is the heaviest; 128 for INT8 when M splits evenly into 128s.
+// Pairs of CTAs (cta_group::2 MMAs, half the activation tile per SM) for token tiles of 128 and
+// more, when the weight tiles pair up.  Tuning knob: QLIN_PAIR=0 keeps single-CTA MMAs for sweeps.
+static bool use_pair(int tm, int n_tiles) {
+  static const bool enabled = [] {
+    const char* e = getenv("QLIN_PAIR");
+    return !(e && atoi(e) == 0);
+  }();
+  return enabled && tm >= 128 && n_tiles % 2 == 0;
+}
+
+// Modelled time of one plan (microseconds at the boost clock), from measured per-stage costs of
+// the persistent kernel on B200: a 64-deep K stage of one tile costs c(TM), the 256-token tile
+// (single-buffered accumulator) adds an exposed epilogue per tile, Q6_K decodes ~12% slower, and
+// a K split adds the finalize pass over the fp32 partials.
+static double plan_cost(int M, int N, int kst, int fmt, int tm, int splits, int sms) {
+  const int n_tiles = (N + 127) / 128;
+  const bool pair = use_pair(tm, n_tiles);
+  const long long units = (long long)((M + tm - 1) / tm) * (pair ? n_tiles / 2 : n_tiles) * splits;
+  const int slots = pair ? sms / 2 : sms;
+  const long long waves = (units + slots - 1) / slots;
+  double c = tm <= 64 ? 0.30 : tm == 128 ? 0.33 : tm == 192 ? 0.38 : 0.45;
+  if (!pair) c *= 1.03;
+  if (fmt == WF_Q6_K) c *= 1.12;
+  const double epi = tm == 256 ? 6.0 : 0.0;
+  const int per = (kst + splits - 1) / splits;
+  double t = (double)waves * (per * c + epi);
+  if (splits > 1) t += ((double)splits * N * M * 4 + (double)N * M * 2) / 5.0e6 + 3.0;
+  return t;
+}
+
+// Token tile and K-split plan.  M <= 256: the smallest tile that holds M and K split across
+// CTAs until the grid covers the SMs.  Larger M: the tile (128 / 192 / 256) and split with the
+// lowest modelled time, which weighs per-stage cost against wave quantization on the SMs.
 void plan_f16(int M, int N, int K, int fmt, int* tm_out, int* splits_out) {
   int tm = *tm_out;
   // Tuning knob: QLIN_TM forces the token tile (16, 32, 64, 128, 192 or 256) for sweeps.
@@ -188,16 +217,6 @@ void plan_f16(int M, int N, int K, int fmt, int* tm_out, int* splits_out) {
       return e ? atoi(e) : 0;
     }();
     if (forced == 16 || forced == 32 || forced == 64 || forced == 128 || forced == 192 || forced == 256) tm = forced;
-  }
-  if (tm == 0) {
-    if (M <= 16) tm = 16;
-    else if (M <= 32) tm = 32;
-    else if (M <= 64) tm = 64;
-    else if (M <= 128) tm = 128;
-    else if (M <= 256) tm = 256;  // one token tile; the grid is filled by splitting K
-    else if (fmt == WF_Q6_K) tm = 256;
-    else if (fmt == WF_INT8 && M % 128 == 0 && M % 192 != 0) tm = 128;
-    else tm = 192;
   }
   int splits = *splits_out;
   const int kst = (K + 63) / 64;
@@ -209,9 +228,34 @@ void plan_f16(int M, int N, int K, int fmt, int* tm_out, int* splits_out) {
     }();
     if (forced_splits > 0) splits = forced_splits;
   }
+  const int sms = sm_count();
+  if (tm == 0 && M > 256) {
+    double best = 1e30;
+    int best_tm = 192, best_splits = 1;
+    for (int cand : {128, 192, 256}) {
+      for (int sp = 1; sp <= 4; ++sp) {
+        if (splits != 0 && sp != splits) continue;
+        if (sp > 1 && kst / sp < 8) break;
+        const double t = plan_cost(M, N, kst, fmt, cand, sp, sms);
+        if (t < best) {
+          best = t;
+          best_tm = cand;
+          best_splits = sp;
+        }
+      }
+    }
+    tm = best_tm;
+    if (splits == 0) splits = best_splits;
+  }
+  if (tm == 0) {
+    if (M <= 16) tm = 16;
+    else if (M <= 32) tm = 32;
+    else if (M <= 64) tm = 64;
+    else if (M <= 128) tm = 128;
+    else tm = 256;  // one token tile; the grid is filled by splitting K
+  }
   if (splits == 0) {
     const int tiles = ((N + 127) / 128) * ((M + tm - 1) / tm);
-    const int sms = sm_count();
     splits = 1;
     if (tiles < sms) {
       splits = std::max(1, sms / std::max(tiles, 1));
@@ -301,15 +345,6 @@ static int dispatch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUten
   }
 }
 
-// Pairs of CTAs (cta_group::2 MMAs, half the activation tile per SM) for token tiles of 128 and
-// more, when the weight tiles pair up.  Tuning knob: QLIN_PAIR=0 keeps single-CTA MMAs for sweeps.
-static bool use_pair(int tm, int n_tiles) {
-  static const bool enabled = [] {
-    const char* e = getenv("QLIN_PAIR");
-    return !(e && atoi(e) == 0);
-  }();
-  return enabled && tm >= 128 && n_tiles % 2 == 0;
-}
 
 // Whole 16-byte pieces of 2-byte output rows can be stored from the shared-memory staging tile.
 // Tuning knob: QLIN_STAGED_OUT=0 keeps per-element stores for sweeps.
