@@ -102,6 +102,12 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return r;
 }
 
+// v * 2^-f, exactly as ldexpf(v, -f): one multiply by the power of two when 2^-f is a normal
+// float (every row whose max is a normal number), the library call otherwise.
+__device__ __forceinline__ float scale_pow2(float v, int f) {
+  return (f >= -127 && f <= 126) ? __fmul_rn(v, exp2i(-f)) : ldexpf(v, -f);
+}
+
 // Rounds a float to the input dtype (fp16 / bf16 / fp32) and back.
 __device__ __forceinline__ float round_to(float v, int dtype) {
   if (dtype == 1) return __half2float(__float2half_rn(v));
@@ -206,7 +212,7 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
         uint4 pk;
         uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) pw[e] = pack_f16x2(ldexpf(v8[2 * e], -f), ldexpf(v8[2 * e + 1], -f));
+        for (int e = 0; e < 4; ++e) pw[e] = pack_f16x2(scale_pow2(v8[2 * e], f), scale_pow2(v8[2 * e + 1], f));
         *reinterpret_cast<uint4*>(o + c) = pk;
       }
     } else {
@@ -217,7 +223,7 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
         if (rotate) block_hadamard<E>(v, rotate_kind, lane);
 #pragma unroll
         for (int e = 0; e < E; ++e)
-          if (c + e < Kp) o[c + e] = __float2half_rn(ldexpf(v[e], -f));
+          if (c + e < Kp) o[c + e] = __float2half_rn(scale_pow2(v[e], f));
       }
     }
   } else {
@@ -316,11 +322,11 @@ __global__ void __launch_bounds__(512) prologue_reg_kernel(const void* __restric
           uint32_t w[(E + 1) / 2];
 #pragma unroll
           for (int e = 0; e < E; e += 2)
-            w[e / 2] = pack_f16x2(ldexpf(v[i][e], -f), E > 1 ? ldexpf(v[i][e + 1 < E ? e + 1 : e], -f) : 0.f);
+            w[e / 2] = pack_f16x2(scale_pow2(v[i][e], f), E > 1 ? scale_pow2(v[i][e + 1 < E ? e + 1 : e], f) : 0.f);
           if constexpr (E == 8) *reinterpret_cast<uint4*>(o + c) = make_uint4(w[0], w[1], w[2], w[3]);
           else if constexpr (E == 4) *reinterpret_cast<uint2*>(o + c) = make_uint2(w[0], w[1]);
           else if constexpr (E == 2) *reinterpret_cast<uint32_t*>(o + c) = w[0];
-          else o[c] = __float2half_rn(ldexpf(v[i][0], -f));
+          else o[c] = __float2half_rn(scale_pow2(v[i][0], f));
         }
       }
     }
