@@ -8,6 +8,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <algorithm>
+#include <cstdlib>
 #include <cstdint>
 
 #include "qlin_decode.cuh"
@@ -626,6 +627,229 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int sp
 }
 
 // ---------------------------------------------------------------------------------------------
+// Tensor-core block-Hadamard prologue for fp16 / bf16 activations (fp16 output, per-row power of
+// two).  A group of G = 16 * A values factors as H_G = H_A (x) H_16 (index i = 16 a + b): the
+// 16-point factor runs on mma.sync (m16n8k16, fp32 accumulate, entries +-1 exact), the A-point
+// factor as butterflies on the accumulators, which hold all A chunks of the same (row, column)
+// position in one thread.  A CTA takes 16 rows: the tile is staged in shared memory once, pass 1
+// finds the row maxima, pass 2 recomputes the rotation, scales, rounds to fp16 in place and the
+// tile is stored with 16-byte writes.  KIND 0: Sylvester; KIND 1: H4 (x) H4 (x) H4 (G = 64).
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+template <int KIND>
+__device__ __forceinline__ float hadamard16_entry(int k, int n) {
+  if constexpr (KIND == 0) return (__popc(k & n) & 1) ? -1.f : 1.f;
+  const float a = ((n >> 2) == 3 - (k >> 2)) ? -1.f : 1.f;
+  const float b = ((n & 3) == 3 - (k & 3)) ? -1.f : 1.f;
+  return a * b;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack_pm1(float lo, float hi) {
+  if constexpr (BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    return pack_f16x2(lo, hi);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%10,%10,%10,%10};"
+                 : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+  } else {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%10,%10,%10,%10};"
+                 : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+  }
+}
+
+// Rotated values of group g for this lane: z[a][nb][c] = row (lane/4 + 8*(c>>1)),
+// column 16a + 8nb + 2*(lane%4) + (c&1) of the group, already normalized by 1/sqrt(G).
+template <int A, int KIND, bool BF16>
+__device__ __forceinline__ void rotate_group(const uint8_t* tile, int pitch, int g, int lane,
+                                             const uint32_t (&hb)[2][2], float (&z)[A][2][4]) {
+  const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+  for (int a = 0; a < A; ++a) {
+    const int col = g * 16 * A + 16 * a + (lane >> 4) * 8;
+    uint32_t fr[4];
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(fr[0]), "=r"(fr[1]), "=r"(fr[2]), "=r"(fr[3])
+                 : "r"(smem_u32(tile + row * pitch + col * 2)));
+    mma_16816<BF16>(z[a][0], fr, hb[0][0], hb[0][1]);
+    mma_16816<BF16>(z[a][1], fr, hb[1][0], hb[1][1]);
+  }
+  constexpr float kNorm = A == 2 ? 0.17677669529663687f : A == 4 ? 0.125f : 0.08838834764831845f;
+#pragma unroll
+  for (int nb = 0; nb < 2; ++nb) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if constexpr (KIND == 0) {
+#pragma unroll
+        for (int st = 1; st < A; st <<= 1) {
+#pragma unroll
+          for (int a = 0; a < A; ++a) {
+            if (a & st) continue;
+            const float u = z[a][nb][c], v = z[a + st][nb][c];
+            z[a][nb][c] = __fadd_rn(u, v);
+            z[a + st][nb][c] = __fsub_rn(u, v);
+          }
+        }
+      } else {
+        const float t = __fadd_rn(__fadd_rn(z[0][nb][c], z[1][nb][c]), __fadd_rn(z[2][nb][c], z[3][nb][c]));
+        float y[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) y[k] = __fsub_rn(t, __fmul_rn(2.f, z[3 - k][nb][c]));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) z[k][nb][c] = y[k];
+      }
+#pragma unroll
+      for (int a = 0; a < A; ++a) z[a][nb][c] = __fmul_rn(z[a][nb][c], kNorm);
+    }
+  }
+}
+
+template <int A, int KIND, bool BF16>
+__global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restrict__ x, long long ldx, int M, int K,
+                                                           __half* __restrict__ out, long long ldo,
+                                                           int32_t* __restrict__ row_exp) {
+  extern __shared__ __align__(16) uint8_t psm[];
+  const int pitch = K * 2 + 16;
+  uint8_t* tile = psm;
+  unsigned* rmax = reinterpret_cast<unsigned*>(psm + 16 * pitch);
+  const int row0 = blockIdx.x * 16;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid < 16) rmax[tid] = 0u;
+  const int cpr = K / 8;  // 16-byte chunks per row
+  for (int i = tid; i < 16 * cpr; i += 256) {
+    const int r = i / cpr, c = i - r * cpr;
+    uint8_t* dst = tile + r * pitch + c * 16;
+    if (row0 + r < M) cp_async16(dst, reinterpret_cast<const uint8_t*>(x) + ((long long)(row0 + r) * ldx + c * 8) * 2);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  // B fragments of H16 (symmetric): n-block nb, k rows 2(lane%4)+{0,1} and +8, column lane/4.
+  uint32_t hb[2][2];
+#pragma unroll
+  for (int nb = 0; nb < 2; ++nb) {
+    const int n = nb * 8 + (lane >> 2), k0 = 2 * (lane & 3);
+    hb[nb][0] = pack_pm1<BF16>(hadamard16_entry<KIND>(k0, n), hadamard16_entry<KIND>(k0 + 1, n));
+    hb[nb][1] = pack_pm1<BF16>(hadamard16_entry<KIND>(k0 + 8, n), hadamard16_entry<KIND>(k0 + 9, n));
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int groups = K / (16 * A);
+  // pass 1: row maxima
+  float m_lo = 0.f, m_hi = 0.f;
+  for (int g = warp; g < groups; g += 8) {
+    float z[A][2][4];
+    rotate_group<A, KIND, BF16>(tile, pitch, g, lane, hb, z);
+#pragma unroll
+    for (int a = 0; a < A; ++a)
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        m_lo = fmaxf(m_lo, fmaxf(fabsf(z[a][nb][0]), fabsf(z[a][nb][1])));
+        m_hi = fmaxf(m_hi, fmaxf(fabsf(z[a][nb][2]), fabsf(z[a][nb][3])));
+      }
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, o));
+    m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, o));
+  }
+  if ((lane & 3) == 0) {
+    atomicMax(&rmax[lane >> 2], __float_as_uint(m_lo));
+    atomicMax(&rmax[(lane >> 2) + 8], __float_as_uint(m_hi));
+  }
+  __syncthreads();
+  auto row_f = [&](int r) {
+    const float amax = __uint_as_float(rmax[r]);
+    int f = 0;
+    if (amax > 0.f && amax <= 3.402823466e38f) {
+      int ex;
+      frexpf(amax, &ex);
+      f = ex - 15;
+    }
+    return f;
+  };
+  const int f_lo = row_f(lane >> 2), f_hi = row_f((lane >> 2) + 8);
+  // pass 2: rotate again, scale, round to fp16 in place (each warp overwrites only its groups)
+  for (int g = warp; g < groups; g += 8) {
+    float z[A][2][4];
+    rotate_group<A, KIND, BF16>(tile, pitch, g, lane, hb, z);
+#pragma unroll
+    for (int a = 0; a < A; ++a)
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        const int col = g * 16 * A + 16 * a + 8 * nb + 2 * (lane & 3);
+        *reinterpret_cast<uint32_t*>(tile + (lane >> 2) * pitch + col * 2) =
+            pack_f16x2(scale_pow2(z[a][nb][0], f_lo), scale_pow2(z[a][nb][1], f_lo));
+        *reinterpret_cast<uint32_t*>(tile + ((lane >> 2) + 8) * pitch + col * 2) =
+            pack_f16x2(scale_pow2(z[a][nb][2], f_hi), scale_pow2(z[a][nb][3], f_hi));
+      }
+  }
+  __syncthreads();
+  if (tid < 16 && row0 + tid < M) row_exp[row0 + tid] = row_f(tid);
+  for (int i = tid; i < 16 * cpr; i += 256) {
+    const int r = i / cpr, c = i - r * cpr;
+    if (row0 + r < M)
+      *reinterpret_cast<uint4*>(out + (long long)(row0 + r) * ldo + c * 8) =
+          *reinterpret_cast<const uint4*>(tile + r * pitch + c * 16);
+  }
+}
+
+// Launches the tensor-core prologue when it applies (fp16 / bf16 input, fp16 output, groups of
+// 32 / 128 (Sylvester) or 64 (H4 (x) H4 (x) H4), whole groups, 16-byte aligned rows, the tile in
+// shared memory); returns false otherwise.
+static bool launch_prologue_mma(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int group, int kind,
+                                void* out, int32_t* row_exp, cudaStream_t stream) {
+  if ((x_dtype != 1 && x_dtype != 2) || K != Kp || K % group != 0 || K % 8 != 0 || ldx % 8 != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return false;
+  const size_t smem = 16 * ((size_t)K * 2 + 16) + 64;
+  if (smem > 200 * 1024) return false;
+  const bool bf = x_dtype == 2;
+  const dim3 grid((M + 15) / 16);
+  __half* o = reinterpret_cast<__half*>(out);
+#define QLIN_MMA_PRO(AA, KK, BB)                                                                           \
+  do {                                                                                                     \
+    auto kern = prologue_mma_kernel<AA, KK, BB>;                                                           \
+    static bool attr_done[64] = {false};                                                                   \
+    int dev = 0;                                                                                           \
+    cudaGetDevice(&dev);                                                                                   \
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {                                                         \
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024 + 64) !=      \
+          cudaSuccess)                                                                                     \
+        return false;                                                                                      \
+      attr_done[dev] = true;                                                                               \
+    }                                                                                                      \
+    kern<<<grid, 256, smem, stream>>>(x, ldx, M, K, o, Kp, row_exp);                                       \
+  } while (0)
+  if (group == 128 && kind == 0) {
+    if (bf) QLIN_MMA_PRO(8, 0, true); else QLIN_MMA_PRO(8, 0, false);
+  } else if (group == 32 && kind == 0) {
+    if (bf) QLIN_MMA_PRO(2, 0, true); else QLIN_MMA_PRO(2, 0, false);
+  } else if (group == 64 && kind == 1) {
+    if (bf) QLIN_MMA_PRO(4, 1, true); else QLIN_MMA_PRO(4, 1, false);
+  } else {
+    return false;
+  }
+#undef QLIN_MMA_PRO
+  return true;
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------------------------
 template <int E, int MODE, int BPW>
@@ -681,6 +905,11 @@ int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int
       default: return -1;
     }
   }
+  // Tuning knob: QLIN_FWHT_PROLOGUE=1 keeps the shuffle-butterfly rotation for comparisons.
+  static const bool fwht_only = getenv("QLIN_FWHT_PROLOGUE") != nullptr;
+  if (mode == 0 && rotate && !fwht_only &&
+      launch_prologue_mma(x, x_dtype, ldx, M, K, Kp, group, kind, out, row_exp, stream))
+    return 0;
 #define QLIN_PRO(EE)                                                                                       \
   do {                                                                                                     \
     if (mode == 0) launch_prologue_e<EE, 0>(x, x_dtype, ldx, M, K, Kp, kind, rotate, out, row_exp, row_scale, perm, stream); \
