@@ -386,7 +386,8 @@ def run_ours(args, rank, world):
                 "frac": achieved / peak, "frac_of_burst_peak": achieved / pk["tflops"], "traffic": traffic,
                 "algorithmic_bytes": q.numel() + 4 * N + M * K * 2 + M * N * 2,
                 "peak_source": pk["source"] + " sustained (kernel timed after 1 s of load)",
-                "kernel": "qgemm_f16_kernel<DecInt8,128,6>", "kernel_ms": t_gemm}
+                "kernel": "qgemm_f16_kernel<DecInt8> (planner: 192-token tiles, CTA pairs at this shape)",
+                "kernel_ms": t_gemm}
     algo_bytes = q.numel() + N * 2 + N * 2 + M * K * 2 + M * N * 2
     roof_t = roofline_time_s(FLOPS, algo_bytes, pk)
 
