@@ -65,18 +65,6 @@ __device__ __forceinline__ void ffma2_sub_magic(float s, float f0, float f1, flo
       : "f"(f0), "f"(f1), "f"(12582912.0f), "f"(s));
 }
 
-// Writes the bit pattern of 1.5*2^23 into COLS consecutive 32-bit TMEM columns of this warp's lanes.
-template <int COLS>
-__device__ __forceinline__ void tmem_fill_bias(uint32_t taddr) {
-  uint32_t r[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) r[i] = 0x4B400000u;
-  static_assert(COLS % 16 == 0, "whole 16-column stores");
-#pragma unroll
-  for (int c = 0; c + 32 <= COLS; c += 32) tmem_st32(taddr + c, r);
-  if constexpr (COLS % 32 != 0) tmem_st16(taddr + (COLS / 32) * 32, *reinterpret_cast<const uint32_t(*)[16]>(r));
-}
-
 template <int TM, int STAGES>
 struct I8Cfg {
   static constexpr int kDecGroups = 1;
@@ -140,18 +128,6 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (warp >= 2 + 4 * Cfg::kDecGroups && p.group <= 128) {
-    // Biased accumulators: every int32 buffer starts at the bit pattern of 1.5*2^23, so after the
-    // group's MMAs it holds the float 1.5*2^23 + P exactly (|P| < 2^22).
-    const int ew = warp - (2 + 4 * Cfg::kDecGroups);
-    const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
-    for (int b = 0; b < 2; ++b) tmem_fill_bias<TM / 2>(tmem_base + lanes + b * TM + (ew >> 2) * (TM / 2));
-    tmem_wait_st();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-
   if (warp == 0) {
     if (elect_one()) {
       uint32_t it = 0;
@@ -185,7 +161,6 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_s8_s32(128, TM);
-      const uint32_t first_acc = p.group <= 128 ? 1u : 0u;  // biased buffers: accumulate onto the bias
       uint32_t it = 0, g_all = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -205,7 +180,7 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
               b = g_all & 1;
               if (!mbar_wait(&acc_empty[b], ((g_all >> 1) & 1) ^ 1, abort_flag, p.status, 13)) { ok = false; break; }
               tc_fence_after();
-              accumulate = first_acc;
+              accumulate = 0;
             }
             mma_i8_ts(tmem_base + b * TM, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, accumulate);
             accumulate = 1;
@@ -276,8 +251,9 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       const __half* gscale = reinterpret_cast<const __half*>(p.scales) + (size_t)min(n, p.N - 1) * p.groups_per_row;
       float s_next = 0.f;
       if (n_ok) s_next = (p.scale_kind == I8S_GROUP_F16) ? __half2float(gscale[0]) : reinterpret_cast<const float*>(p.scales)[n];
-      // Exact int32 -> fp32 through the 1.5*2^23 magic number while |P| < 2^22 (groups of <= 128
-      // values of 8-bit x 8-bit products); larger groups use the conversion instruction.
+      // Exact int32 -> fp32 without the conversion unit while |P| < 2^22 (groups of <= 128 values of
+      // 8-bit x 8-bit products): the int32 bits plus the bit pattern of 1.5*2^23, read as a float,
+      // are 1.5*2^23 + P exactly; larger groups use the conversion instruction.
       const bool magic = p.group <= 128;
       for (int g = 0; g < groups_per_tile; ++g, ++g_all) {
         const float sg = s_next;
@@ -295,11 +271,10 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
             else tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < W; j += 2) ffma2_sub_magic(sg, __uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                         accf[c0 + j], accf[c0 + j + 1]);
+            for (int j = 0; j < W; j += 2)
+              ffma2_sub_magic(sg, __uint_as_float(v[j] + 0x4B400000u), __uint_as_float(v[j + 1] + 0x4B400000u),
+                              accf[c0 + j], accf[c0 + j + 1]);
           }
-          tmem_fill_bias<kHalf>(taddr);  // re-bias the buffer for the group that reuses it
-          tmem_wait_st();
         } else {
 #pragma unroll
           for (int c0 = 0; c0 < kHalf; c0 += 16) {
