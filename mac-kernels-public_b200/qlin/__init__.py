@@ -21,7 +21,7 @@ import torch
 from . import _lib
 from ._lib import QlinDecline, QlinError, check, lib
 
-__all__ = ["int8_linear", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear",
+__all__ = ["int8_linear", "int8_linear_streamed", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear",
            "quantize_int8_rowwise", "prologue_f16", "repack_gguf", "GGUF_TYPES", "QlinDecline", "QlinError",
            "device_status"]
 
@@ -111,6 +111,52 @@ def int8_linear(x, qdata, scale, bias=None, out_dtype=None, convrot=False, convr
     if lora_down is not None:
         _lora_beside(y, x, lora_down, lora_up, lora_scale)
     return y
+
+
+_STREAMS: dict = {}
+
+
+def int8_linear_streamed(x, qdata, scale, bias=None, out=None, out_dtype=torch.float16, convrot=False,
+                         convrot_groupsize=256, chunks=8):
+    """int8_linear for activations and outputs in host memory: x is a (pinned) CPU tensor [M, K], the
+    weights live on the GPU, and the result lands in `out` (a pinned CPU tensor [M, N], allocated if
+    None).  Rows are processed in `chunks` pieces so the host-to-device copy of one piece, the op on
+    the previous one and the device-to-host copy of the one before run at the same time (two copy
+    streams besides the current stream).  Stream-ordered: the copies start after the work already on
+    the current stream, and the current stream waits for the last copy back, so synchronize it (or
+    record an event on it) before reading `out`."""
+    if x.is_cuda or not qdata.is_cuda:
+        raise NotImplementedError("int8_linear_streamed takes host activations and device weights")
+    dev = qdata.device
+    n, k = qdata.shape
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=out_dtype, pin_memory=True)
+    y2 = out.view(m, n)
+    if m == 0:
+        return out
+    cur = torch.cuda.current_stream(dev)
+    if dev not in _STREAMS:
+        _STREAMS[dev] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    h2d, d2h = _STREAMS[dev]
+    h2d.wait_stream(cur)
+    d2h.wait_stream(cur)
+    rows = -(-m // max(1, chunks))
+    for r0 in range(0, m, rows):
+        r1 = min(m, r0 + rows)
+        with torch.cuda.stream(h2d):
+            xb = torch.empty(r1 - r0, k, dtype=x2.dtype, device=dev)
+            xb.copy_(x2[r0:r1], non_blocking=True)
+        cur.wait_stream(h2d)
+        xb.record_stream(cur)
+        yb = int8_linear(xb, qdata, scale, bias, out_dtype=y2.dtype, convrot=convrot, convrot_groupsize=convrot_groupsize)
+        d2h.wait_stream(cur)
+        with torch.cuda.stream(d2h):
+            y2[r0:r1].copy_(yb, non_blocking=True)
+        yb.record_stream(d2h)
+    cur.wait_stream(d2h)
+    return out
 
 
 def _lora_beside(y, x, down, up, scale):

@@ -214,3 +214,21 @@ def test_quantize_rows_int8_bit_exact(qlin, x_dtype):
     perm = np.array([0, 2, 4, 6, 1, 3, 5, 7])
     want = q_ref.numpy().reshape(m, -1, 8)[:, :, perm].reshape(m, -1)
     assert np.array_equal(qp.cpu().numpy()[:, :k], want)
+
+
+def test_int8_linear_streamed_from_host_memory(qlin):
+    """Host activations in, host outputs out, copies overlapped in chunks: the same rows as the
+    device path (per-row prologue, no K split at this shape)."""
+    m, n, k = 1000, 512, 1024
+    x, q, s, b = O.cfg_int8_convrot(m, k, n, seed=3)
+    want = qlin.int8_linear(x.cuda(), q.cuda(), s.cuda(), b.cuda(), torch.float16, convrot=True,
+                            convrot_groupsize=128).cpu()
+    xh = x.pin_memory()
+    for chunks in (1, 3, 8):
+        got = qlin.int8_linear_streamed(xh, q.cuda(), s.cuda(), b.cuda(), convrot=True, convrot_groupsize=128,
+                                        chunks=chunks)
+        torch.cuda.current_stream().synchronize()
+        assert got.device.type == "cpu" and got.shape == (m, n)
+        assert O.max_abs_rel(got.float().numpy(), want.float().numpy()) <= 1e-3
+    with pytest.raises(NotImplementedError):
+        qlin.int8_linear_streamed(x.cuda(), q.cuda(), s.cuda())
