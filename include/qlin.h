@@ -168,6 +168,17 @@ int qlin_w4a8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
                      int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* The kitchen's AsymW4A8Int8Layout weight (symmetric form) -> its int8 weight grid, bit-exact:
+ * grid[n, k] = clamp(rint(level[code] * s_rel[n, k / group]), -127, 127) in fp32, with
+ * level = codebook (1 << bits fp32 entries) or code - 2^(bits-1).  qdata int8 [n, k * bits / 8]
+ * in the kitchen's planar packing, s_rel float8_e4m3fn [n, k / group], out int8 [n, k].
+ * Replaces the decode of `dequantize_w4a8` / the kitchen's w4a8_int8_linear
+ * (modal/weight_error_app.py:326-336, bench/bench_w4a8_linear.py:98-99); the linear is then the
+ * INT8 ConvRot linear with s_channel as the per-channel scale (the reference backend is weight-only:
+ * docs/upstream/comfy-kitchen-mps-backend.md:42). */
+int qlin_kitchen_w4a8_grid(const void* qdata, int bits, const void* s_rel, const float* codebook, int group,
+                           int64_t n, int64_t k, int8_t* out, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Activation prologues (exposed for tests and for callers that reuse one prologue across
  * several linears sharing an input).

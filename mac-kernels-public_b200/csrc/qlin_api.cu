@@ -405,6 +405,23 @@ int qlin_gguf_linear_allgather(const void* x, int64_t m, int64_t k, int64_t ldx,
                          y_ranks[rank], y_dtype, ldy, workspace, workspace_bytes, stream, &po);
 }
 
+int qlin_kitchen_w4a8_grid(const void* qdata, int bits, const void* s_rel, const float* codebook, int group,
+                           int64_t n, int64_t k, int8_t* out, void* stream) {
+  if ((bits != 4 && bits != 6) || n < 0 || k < 0 || group < 16 || group % 16 != 0 || k % group != 0 ||
+      (bits == 6 && k % 32 != 0) || (n > 0 && k > 0 && (qdata == nullptr || s_rel == nullptr || out == nullptr))) {
+    set_error("kitchen grid: bits 4 or 6, group a multiple of 16 dividing k (k a multiple of 32 for 6 bits)");
+    return QLIN_EINVAL;
+  }
+  if ((reinterpret_cast<uintptr_t>(qdata) & 7) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (bits == 6 && ((k / 2) % 4 != 0 || (n > 1 && ((k * 6 / 8) % 8 != 0))))) {
+    set_error("kitchen grid: qdata rows must be 8-byte aligned and out 16-byte aligned");
+    return QLIN_EDECLINE;
+  }
+  launch_kitchen_grid(reinterpret_cast<const uint8_t*>(qdata), reinterpret_cast<const uint8_t*>(s_rel), codebook,
+                      bits, group, (int)n, (int)k, out, reinterpret_cast<cudaStream_t>(stream));
+  return check_cuda("kitchen grid launch");
+}
+
 size_t qlin_peer_sync_bytes(void) { return sizeof(PeerSync); }
 
 int qlin_peer_alloc(size_t bytes, void** ptr) {

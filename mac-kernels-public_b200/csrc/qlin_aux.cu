@@ -850,6 +850,50 @@ static bool launch_prologue_mma(const void* x, int x_dtype, long long ldx, int M
 }
 
 // ---------------------------------------------------------------------------------------------
+// Kitchen W4A8 / W6A8 (AsymW4A8Int8Layout, symmetric) -> its int8 weight grid, bit-exact:
+// grid = clamp(rint(level[code] * s_rel), +-127) in fp32 (`modal/weight_error_app.py:326-336`).
+// Codes: planar packing, K/2 bytes of nibble pairs (even column low), then for 6 bits K/4 bytes of
+// 2-bit high planes (column 4j+i at bits 2i..2i+1 of byte j).  s_rel: float8_e4m3fn per group.
+// One thread per 16 consecutive values of a row; the level table (<= 64 fp32) sits in shared memory.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float e4m3_to_float(uint32_t b) {
+  const uint32_t e = (b >> 3) & 0xF, m = b & 7;
+  float v = e == 0 ? (float)m * 0.001953125f                              // m/8 * 2^-6
+                   : __uint_as_float(((e + 120u) << 23) | (m << 20));     // (1 + m/8) * 2^(e-7)
+  if ((b & 0x7F) == 0x7F) v = __uint_as_float(0x7FC00000u);
+  return (b & 0x80) ? -v : v;
+}
+
+__global__ void kitchen_grid_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ s_rel,
+                                    const float* __restrict__ codebook, int bits, int group, int N, int K,
+                                    int8_t* __restrict__ out) {
+  __shared__ float levels[64];
+  const int nlev = 1 << bits;
+  if (threadIdx.x < nlev) levels[threadIdx.x] = codebook ? codebook[threadIdx.x] : (float)((int)threadIdx.x - nlev / 2);
+  __syncthreads();
+  const int gpr = K / 16;
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (long long)N * gpr) return;
+  const int row = (int)(t / gpr), c0 = (int)(t - (long long)row * gpr) * 16;
+  const long long pitch = (long long)K * bits / 8;
+  const uint8_t* qr = q + row * pitch;
+  const uint2 lo = *reinterpret_cast<const uint2*>(qr + c0 / 2);
+  uint32_t hi = 0;
+  if (bits == 6) hi = *reinterpret_cast<const uint32_t*>(qr + K / 2 + c0 / 4);
+  const float sc = e4m3_to_float(s_rel[(long long)row * (K / group) + c0 / group]);
+  uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t byte = ((i < 8 ? lo.x : lo.y) >> (8 * ((i >> 1) & 3))) & 0xFF;
+    uint32_t code = (i & 1) ? (byte >> 4) : (byte & 0xF);
+    if (bits == 6) code |= ((hi >> (2 * i)) & 3) << 4;
+    const float v = fminf(fmaxf(rintf(__fmul_rn(levels[code], sc)), -127.f), 127.f);
+    w[i >> 2] |= ((uint32_t)(int)v & 0xFF) << (8 * (i & 3));
+  }
+  *reinterpret_cast<uint4*>(out + (long long)row * K + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------------------------
 template <int E, int MODE, int BPW>
@@ -956,6 +1000,13 @@ void launch_splitk_finalize(const float* partial, int splits, int M, int N, int 
   }
   splitk_finalize_kernel<<<grid, dim3(32, 8), 0, s>>>(partial, splits, M, N, Mp, col_scale, cs_kind, w_row_exp,
                                                       x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy, po);
+}
+
+void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* codebook, int bits, int group, int N,
+                         int K, int8_t* out, cudaStream_t s) {
+  const long long threads = (long long)N * (K / 16);
+  if (threads == 0) return;
+  kitchen_grid_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(q, s_rel, codebook, bits, group, N, K, out);
 }
 
 }  // namespace qlin

@@ -20,6 +20,9 @@ void launch_splitk_finalize(const float* partial, int splits, int M, int N, int 
                             long long ldy, cudaStream_t s,
                             const PeerOut* out = nullptr);
 
+void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* codebook, int bits, int group, int N,
+                         int K, int8_t* out, cudaStream_t s);
+
 // Weight formats of the f16 (weight-only) GEMM family.
 enum WFormat : int { WF_INT8 = 0, WF_Q8_0 = 8, WF_Q4_0 = 2, WF_Q4_K = 12, WF_Q6_K = 14, WF_IQ4_NL = 20 };
 

@@ -21,7 +21,7 @@ import torch
 from . import _lib
 from ._lib import QlinDecline, QlinError, check, lib
 
-__all__ = ["int8_linear", "int8_linear_streamed", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear",
+__all__ = ["int8_linear", "int8_linear_streamed", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear", "dequantize_w4a8_int8_weight",
            "quantize_int8_rowwise", "prologue_f16", "repack_gguf", "GGUF_TYPES", "QlinDecline", "QlinError",
            "device_status"]
 
@@ -314,11 +314,19 @@ def quantize_int8_rowwise(x, rotate_group=0, perm=False):
 
 
 # ---------------------------------------------------------------------------------------------- W4A8 / W6A8
-def w4a8_linear(*args, **kwargs):  # defined in _w4a8 once the kind::i8 kernels are built
+def w4a8_linear(*args, **kwargs):
+    """Benchmark-configuration W4A8 / W6A8 (per-token int8 activations, kind::i8); see _w4a8."""
     from ._w4a8 import w4a8_linear as impl
     return impl(*args, **kwargs)
 
 
 def w4a8_int8_linear(*args, **kwargs):
+    """Kitchen AsymW4A8Int8Layout linear (weight-only, like the reference backend); see _w4a8."""
     from ._w4a8 import w4a8_int8_linear as impl
+    return impl(*args, **kwargs)
+
+
+def dequantize_w4a8_int8_weight(*args, **kwargs):
+    """Kitchen W4A8 / W6A8 decode-only entry point; see _w4a8."""
+    from ._w4a8 import dequantize_w4a8_int8_weight as impl
     return impl(*args, **kwargs)

@@ -44,6 +44,7 @@ SIGNATURES = {
     "qlin_peer_close": (_i, [_p]),
     "qlin_gguf_linear_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p]),
     "qlin_gguf_dequantize": (_i, [_p, _i, _i64, _i64, _p, _i, _p]),
+    "qlin_kitchen_w4a8_grid": (_i, [_p, _i, _p, _p, _i, _i64, _i64, _p, _p]),
     "qlin_prologue_f16": (_i, [_p, _i, _i64, _i64, _i64, _i, _p, _i64, _p, _p]),
     "qlin_quantize_rows_int8": (_i, [_p, _i, _i64, _i64, _i64, _i, _i, _p, _i64, _p, _p]),
     "qlin_w4a8_repacked_bytes": (_i, [_i, _i, _i64, _i64, ctypes.POINTER(_sz)]),

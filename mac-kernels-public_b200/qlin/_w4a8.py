@@ -79,7 +79,84 @@ def w4a8_linear(x, qweight, scales, bits=4, group_size=128, layout=0, bias=None,
     return y
 
 
+def _hadamard(g, device):
+    """The rotation's block matrix: H4 (x) ... (x) H4 for powers of four (the reference's
+    build_hadamard, modal/weight_error_app.py:90-98), else Sylvester; orthonormal."""
+    import math
+    h = torch.ones(1, 1, dtype=torch.float64)
+    if 4 ** round(math.log(g, 4)) == g:
+        h4 = torch.ones(4, 4, dtype=torch.float64) - 2 * torch.eye(4, dtype=torch.float64).flip(0)
+        while h.shape[0] < g:
+            h = torch.kron(h, h4)
+    else:
+        h2 = torch.tensor([[1.0, 1.0], [1.0, -1.0]], dtype=torch.float64)
+        while h.shape[0] < g:
+            h = torch.kron(h, h2)
+    return (h / math.sqrt(g)).to(device=device, dtype=torch.float32)
+
+
+_GRID_CACHE: dict = {}
+
+
+def kitchen_grid(qdata, s_rel, codebook=None, group_size=16):
+    """The int8 weight grid [N, K] of a kitchen W4A8 / W6A8 weight (cached per tensor version)."""
+    if not qdata.is_cuda or not s_rel.is_cuda:
+        raise NotImplementedError("qlin runs on CUDA tensors only (there is no CPU path)")
+    n = qdata.shape[0]
+    k = s_rel.shape[1] * group_size
+    bits = qdata.shape[1] * 8 // k
+    if bits not in (4, 6) or qdata.shape[1] * 8 != bits * k:
+        raise QlinDecline(1, "w4a8_int8_linear: qdata width matches neither 4 nor 6 bits")
+    key = (qdata.data_ptr(), qdata._version, s_rel.data_ptr(), s_rel._version,
+           None if codebook is None else (codebook.data_ptr(), codebook._version), group_size, n, k)
+    hit = _GRID_CACHE.get(key)
+    if hit is not None:
+        return hit
+    cb = None
+    if codebook is not None:
+        cb = codebook.to(device=qdata.device, dtype=torch.float32).contiguous()
+        if cb.numel() != 1 << bits:
+            raise QlinDecline(1, f"w4a8_int8_linear: a {bits}-bit codebook has {1 << bits} levels")
+    q = qdata.contiguous()
+    sr = s_rel.contiguous().view(torch.uint8)
+    out = torch.empty(n, k, dtype=torch.int8, device=qdata.device)
+    check(lib.qlin_kitchen_w4a8_grid(q.data_ptr(), bits, sr.data_ptr(), None if cb is None else cb.data_ptr(),
+                                     group_size, n, k, out.data_ptr(),
+                                     torch.cuda.current_stream(qdata.device).cuda_stream), "qlin_kitchen_w4a8_grid")
+    _GRID_CACHE[key] = out
+    try:
+        weakref.finalize(qdata, _GRID_CACHE.pop, key, None)
+    except TypeError:
+        pass
+    return out
+
+
 def w4a8_int8_linear(x, qdata, s_rel, s_channel, codebook=None, correction=None, bias=None, group_size=16,
                      convrot_groupsize=256, out_dtype=None, lora_down=None, lora_up=None, lora_scale=None):
-    """comfy-kitchen AsymW4A8Int8Layout linear (bench/bench_lora_fused_rank.py:42-44)."""
-    raise QlinDecline(1, "w4a8_int8_linear: the kitchen AsymW4A8Int8Layout path is not built yet")
+    """comfy-kitchen AsymW4A8Int8Layout linear (bench/bench_lora_fused_rank.py:42-44;
+    bench/bench_w4a8_linear.py:83), symmetric form.  Like the reference backend it is weight-only
+    (docs/upstream/comfy-kitchen-mps-backend.md:42): the stored codes decode once to the exact int8
+    grid, and the linear is the INT8 ConvRot linear with s_channel per output channel.  An
+    asymmetric `correction` declines (QlinDecline), as an unsupported layout does in the kitchen."""
+    if correction is not None:
+        raise QlinDecline(1, "w4a8_int8_linear: the asymmetric correction term is not supported")
+    from . import int8_linear
+    grid = kitchen_grid(qdata, s_rel, codebook, group_size)
+    return int8_linear(x, grid, s_channel.float().reshape(-1), bias, out_dtype=out_dtype,
+                       convrot=convrot_groupsize > 0, convrot_groupsize=convrot_groupsize,
+                       lora_down=lora_down, lora_up=lora_up, lora_scale=lora_scale)
+
+
+def dequantize_w4a8_int8_weight(qdata, s_rel, s_channel, codebook=None, correction=None, group_size=16,
+                                convrot_groupsize=256, output_dtype=torch.float32):
+    """Decode-only entry point (docs/upstream/comfy-kitchen-mps-backend.md:30): the weight in the
+    original basis, grid * s_channel un-rotated per block (modal/weight_error_app.py:326-339)."""
+    if correction is not None:
+        raise QlinDecline(1, "dequantize_w4a8_int8_weight: the asymmetric correction term is not supported")
+    grid = kitchen_grid(qdata, s_rel, codebook, group_size)
+    w = grid.float() * s_channel.float().reshape(-1, 1)
+    if convrot_groupsize:
+        g = convrot_groupsize
+        n, k = w.shape
+        w = (w.view(n, k // g, g) @ _hadamard(g, w.device)).view(n, k)
+    return w.to(output_dtype)

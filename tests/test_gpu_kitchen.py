@@ -1,0 +1,71 @@
+"""The kitchen's AsymW4A8Int8Layout (symmetric) on the GPU: the int8 weight grid bit-identical
+with the reference's own CPU port (golden fixtures from modal/weight_error_app.py:326-336), the
+decode-only entry point against the fixtures' decoded rows, and the linear against float64."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import qlin_oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "kitchen_w4a8.npz")
+
+
+@pytest.fixture(scope="module")
+def qlin():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import qlin as q
+    return q
+
+
+def _case(z, fmt):
+    q = torch.from_numpy(z[f"{fmt}_q"]).cuda()
+    s_rel = torch.from_numpy(z[f"{fmt}_s_rel"]).view(torch.float8_e4m3fn).cuda()
+    s_ch = torch.from_numpy(z[f"{fmt}_s_channel"]).cuda()
+    cb = torch.from_numpy(z["w4a8_codebook"]).cuda() if fmt == "w4a8" else None
+    return q, s_rel, s_ch, cb
+
+
+@pytest.mark.parametrize("fmt", ["w4a8", "w6a8"])
+def test_grid_bit_identical_with_reference_port(qlin, fmt):
+    z = np.load(GOLD)
+    q, s_rel, s_ch, cb = _case(z, fmt)
+    from qlin._w4a8 import kitchen_grid
+    grid = kitchen_grid(q, s_rel, cb, 16)
+    assert np.array_equal(grid.cpu().numpy(), z[f"{fmt}_grid"])
+
+
+@pytest.mark.parametrize("fmt", ["w4a8", "w6a8"])
+def test_dequantize_matches_reference_port(qlin, fmt):
+    z = np.load(GOLD)
+    q, s_rel, s_ch, cb = _case(z, fmt)
+    w = qlin.dequantize_w4a8_int8_weight(q, s_rel, s_ch, cb, None, 16, 256, torch.float32)
+    ref = z[f"{fmt}_deq16"]
+    assert np.abs(w[:16].cpu().numpy() - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("fmt,bits", [("w4a8", 4), ("w6a8", 6)])
+@pytest.mark.parametrize("m", [1, 40, 300])
+def test_linear_matches_fp64(qlin, fmt, bits, m):
+    z = np.load(GOLD)
+    q, s_rel, s_ch, cb = _case(z, fmt)
+    n, k = 96, 1024
+    g = torch.Generator().manual_seed(m)
+    x = torch.randn(m, k, generator=g).to(torch.float16)
+    b = (torch.randn(n, generator=g) * 0.01).to(torch.float16)
+    w = O.dequantize_kitchen_w4a8(z[f"{fmt}_q"], z[f"{fmt}_s_rel"], z[f"{fmt}_s_channel"], k, bits, 16,
+                                  None if cb is None else z["w4a8_codebook"], 256)
+    ref = O.linear_f64(x.float().numpy(), w, b.float().numpy())
+    y = qlin.w4a8_int8_linear(x.cuda(), q, s_rel, s_ch, cb, None, b.cuda(), 16, 256)
+    assert y.dtype == torch.float16
+    assert O.max_abs_rel(y.float().cpu().numpy(), ref) <= 2e-3
+
+
+def test_asymmetric_correction_declines(qlin):
+    z = np.load(GOLD)
+    q, s_rel, s_ch, cb = _case(z, "w4a8")
+    with pytest.raises(NotImplementedError):
+        qlin.w4a8_int8_linear(torch.randn(4, 1024, device="cuda", dtype=torch.float16), q, s_rel, s_ch, cb,
+                              torch.zeros(96, device="cuda"))
