@@ -268,6 +268,19 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
         nbytes = raw.numel() + 256 * 3072 * 2 * 2
         cfgs[name] = {"tflops": fl / (t * 1e-3) / 1e12, "us": t * 1e3,
                       "roofline_frac": roofline_time_s(fl, nbytes, pk) / (t * 1e-3), "timing": "cuda graph replay"}
+    # Small M (text tokens, adapter side paths): HBM-bound weight streaming.
+    xs_all, raw_np = O.cfg_gguf(16, 3072, 3072, qtype=8, seed=0)
+    raw = torch.from_numpy(raw_np).to(dev)
+    for m in (1, 16):
+        xs = xs_all[:m].to(dev)
+        fn = lambda: qlin.gguf_linear(xs, raw, 8, (3072, 3072))  # noqa: E731
+        t = statistics.mean(graph_steps(fn, steps, warmup, flush, stream))
+        fl = 2.0 * m * 3072 * 3072
+        nbytes = raw.numel() + m * 3072 * 2 * 2
+        cfgs[f"cfg1_small_gguf_q8_0_{m}x3072x3072"] = {
+            "us": t * 1e3, "weight_stream_gbs": raw.numel() / (t * 1e-3) / 1e9,
+            "roofline_frac": roofline_time_s(fl, nbytes, pk) / (t * 1e-3), "bound": "hbm",
+            "timing": "cuda graph replay, L2 flushed"}
     for (m, k, n, bits, grp), name in (((4096, 12288, 3072, 4, 128), "cfg3_w4a8_4096x12288x3072"),
                                        ((3240, 5120, 13824, 6, 64), "cfg4_w6a8_fwd_3240x5120x13824"),
                                        ((3240, 13824, 5120, 6, 64), "cfg4_w6a8_rev_3240x13824x5120")):

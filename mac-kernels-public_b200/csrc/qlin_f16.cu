@@ -359,6 +359,10 @@ static bool staged_output_ok(const F16GemmArgs& a) {
 
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return 0;
+  if (a.M <= 2) {
+    const int rc = run_gemv(a, stream);
+    if (rc >= 0) return rc;
+  }
   int tm = a.tm, splits = a.k_splits;
   plan_f16(a.M, a.N, a.K, a.fmt, &tm, &splits);
   GemmParams p{};

@@ -52,6 +52,8 @@ struct F16GemmArgs {
 
 // Returns 0 on success, a positive QLIN_* code on failure (message via set_error).
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream);
+// Small-M (M <= 2) weight-streaming kernel; -1 when it does not apply.
+int run_gemv(const F16GemmArgs& a, cudaStream_t stream);
 size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits);
 void plan_f16(int M, int N, int K, int fmt, int* tm, int* k_splits);
 
