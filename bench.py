@@ -471,6 +471,9 @@ def main():
     if world > 1 and args.impl == "ours":
         import datetime
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        # NCCL's own log lines (its version banner among them) go to a file: stdout carries only
+        # the JSON line of rank 0.
+        os.environ.setdefault("NCCL_DEBUG_FILE", f"/tmp/qlin_bench_nccl.{rank}.log")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
         if args.impl == "reference":

@@ -136,7 +136,7 @@ using namespace qlin;
 static int gguf_slabs_impl(const void* x, int64_t m, int64_t k, int64_t ldx, int x_slabs, int64_t x_slab_stride,
                            const void* packed, const int32_t* row_exp, int qtype, int64_t n, const void* bias,
                            int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
-                           void* stream_, const PeerOut* out) {
+                           void* stream_, const PeerOut* out, const PeerMaps* out_maps = nullptr) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (m < 0 || n < 0 || k <= 0 || x_slabs < 1 || k % x_slabs != 0 || ldx < k / x_slabs || ldy < n ||
       (x_slabs > 1 && x_slab_stride < m * ldx)) {
@@ -176,6 +176,7 @@ static int gguf_slabs_impl(const void* x, int64_t m, int64_t k, int64_t ldx, int
     return QLIN_EINVAL;
   }
   a.out = out;
+  a.out_maps = out_maps;
   return run_f16_gemm(a, stream);
 }
 
@@ -397,12 +398,23 @@ int qlin_gguf_linear_allgather(const void* x, int64_t m, int64_t k, int64_t ldx,
     po.sync[r] = reinterpret_cast<PeerSync*>(sync_ranks[r]);
   }
   po.own = po.sync[rank];
+  // Destination tensor maps for the TMA-store epilogue: {n, m} over each slab, boxes of 128
+  // channels x 32 tokens (the staged chunk).
+  PeerMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  po.tma = 1;
+  for (int r = 0; r < world && po.tma; ++r) {
+    if (make_tmap_2d(&maps.m[r], y_ranks[r], y_dtype == QLIN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     2, (uint64_t)n, (uint64_t)m, (uint64_t)ldy * 2, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE) != 0)
+      po.tma = 0;  // fall back to element stores
+  }
   if (m == 0 || n == 0) {
     set_error("allgather: empty shapes are not supported (every rank must take part in every step)");
     return QLIN_EINVAL;
   }
   return gguf_slabs_impl(x, m, k, ldx, x_slabs, x_slab_stride, packed, row_exp, qtype, n, bias, bias_dtype,
-                         y_ranks[rank], y_dtype, ldy, workspace, workspace_bytes, stream, &po);
+                         y_ranks[rank], y_dtype, ldy, workspace, workspace_bytes, stream, &po, &maps);
 }
 
 int qlin_kitchen_w4a8_grid(const void* qdata, int bits, const void* s_rel, const float* codebook, int group,

@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "qlin_gemm.cuh"
@@ -278,8 +279,8 @@ size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits
 }
 
 template <class Dec, int TM, int STAGES, bool PAIR>
-static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const GemmParams& p,
-                      cudaStream_t stream) {
+static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const PeerMaps& maps,
+                      const GemmParams& p, cudaStream_t stream) {
   constexpr int smem = qgemm_f16_smem_bytes<Dec, TM, STAGES, PAIR>();
   static_assert(smem <= 232448, "shared memory per CTA");
   auto kern = qgemm_f16_kernel<Dec, TM, STAGES, PAIR>;
@@ -310,9 +311,9 @@ static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtens
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, tx, tw, tp, p);
+    e = cudaLaunchKernelEx(&cfg, kern, tx, tw, tp, maps, p);
   } else {
-    kern<<<grid, F16Cfg<TM, STAGES, PAIR>::kThreads, smem, stream>>>(tx, tw, tp, p);
+    kern<<<grid, F16Cfg<TM, STAGES, PAIR>::kThreads, smem, stream>>>(tx, tw, tp, maps, p);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
@@ -323,24 +324,24 @@ static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtens
 }
 
 template <class Dec, int TM>
-static int launch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const GemmParams& p,
-                     bool pair, cudaStream_t stream) {
+static int launch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const PeerMaps& maps,
+                     const GemmParams& p, bool pair, cudaStream_t stream) {
   if constexpr (TM >= 128) {
-    if (pair) return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, true>(), true>(tx, tw, tp, p, stream);
+    if (pair) return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, true>(), true>(tx, tw, tp, maps, p, stream);
   }
-  return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, false>(), false>(tx, tw, tp, p, stream);
+  return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, false>(), false>(tx, tw, tp, maps, p, stream);
 }
 
 template <class Dec>
-static int dispatch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const GemmParams& p,
-                       int tm, bool pair, cudaStream_t stream) {
+static int dispatch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const PeerMaps& maps,
+                       const GemmParams& p, int tm, bool pair, cudaStream_t stream) {
   switch (tm) {
-    case 16: return launch_tm<Dec, 16>(tx, tw, tp, p, pair, stream);
-    case 32: return launch_tm<Dec, 32>(tx, tw, tp, p, pair, stream);
-    case 64: return launch_tm<Dec, 64>(tx, tw, tp, p, pair, stream);
-    case 128: return launch_tm<Dec, 128>(tx, tw, tp, p, pair, stream);
-    case 192: return launch_tm<Dec, 192>(tx, tw, tp, p, pair, stream);
-    case 256: return launch_tm<Dec, 256>(tx, tw, tp, p, pair, stream);
+    case 16: return launch_tm<Dec, 16>(tx, tw, tp, maps, p, pair, stream);
+    case 32: return launch_tm<Dec, 32>(tx, tw, tp, maps, p, pair, stream);
+    case 64: return launch_tm<Dec, 64>(tx, tw, tp, maps, p, pair, stream);
+    case 128: return launch_tm<Dec, 128>(tx, tw, tp, maps, p, pair, stream);
+    case 192: return launch_tm<Dec, 192>(tx, tw, tp, maps, p, pair, stream);
+    case 256: return launch_tm<Dec, 256>(tx, tw, tp, maps, p, pair, stream);
     default: set_error("unsupported token tile %d", tm); return 2;
   }
 }
@@ -387,11 +388,17 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   p.partial = nullptr;
   p.status = reinterpret_cast<DeviceStatus*>(device_status_ptr());
   p.Mp = p.m_tiles * tm;
+  PeerMaps maps;
+  memset(&maps, 0, sizeof(maps));
   if (a.out != nullptr) {
     p.out = *a.out;
     if (splits > 1) {
       p.out.ndst = 0;  // the GEMM writes partials; the finalize kernel stores the output and signals
       p.out.signal = 0;
+      p.out.tma = 0;
+    } else if (p.out.tma) {
+      if (a.out_maps == nullptr || tm < 32) p.out.tma = 0;
+      else maps = *a.out_maps;
     }
   } else if (splits == 1 && staged_output_ok(a)) {
     p.out.ndst = 1;
@@ -434,12 +441,12 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
     if (rc) return rc;
   }
   switch (a.fmt) {
-    case WF_INT8: rc = dispatch_tm<DecInt8>(tx, tw, tp, p, tm, pair, stream); break;
-    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, p, tm, pair, stream); break;
-    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(tx, tw, tp, p, tm, pair, stream); break;
-    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(tx, tw, tp, p, tm, pair, stream); break;
-    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(tx, tw, tp, p, tm, pair, stream); break;
-    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(tx, tw, tp, p, tm, pair, stream); break;
+    case WF_INT8: rc = dispatch_tm<DecInt8>(tx, tw, tp, maps, p, tm, pair, stream); break;
+    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, maps, p, tm, pair, stream); break;
+    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(tx, tw, tp, maps, p, tm, pair, stream); break;
+    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(tx, tw, tp, maps, p, tm, pair, stream); break;
+    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(tx, tw, tp, maps, p, tm, pair, stream); break;
+    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(tx, tw, tp, maps, p, tm, pair, stream); break;
     default: set_error("unknown weight format %d", a.fmt); return 2;
   }
   if (rc) return rc;

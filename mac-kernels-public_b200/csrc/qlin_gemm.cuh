@@ -104,7 +104,8 @@ __device__ __forceinline__ void store_out(void* y, int dtype, long long idx, flo
 template <class Dec, int TM, int STAGES, bool PAIR>
 __global__ void __launch_bounds__(448, 1)
 qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                 const __grid_constant__ CUtensorMap tmap_p, const GemmParams p) {
+                 const __grid_constant__ CUtensorMap tmap_p, const __grid_constant__ PeerMaps out_maps,
+                 const GemmParams p) {
   using Cfg = F16Cfg<TM, STAGES, PAIR>;
   constexpr uint32_t kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -386,9 +387,16 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         tmem_wait_ld();
         if (p.out.ndst > 0) {
           // Stage the chunk as [kCh tokens][128 channels] 2-byte values, then copy whole 16-byte
-          // pieces of token rows to every destination.  Two buffers: the barrier after staging
-          // one also orders every thread's reads of the other before it is staged again.
+          // pieces of token rows to every destination (or one TMA tensor store per destination).
+          // Two buffers: the barrier after staging one also orders every thread's reads of the
+          // other (or the TMA stores that read it, waited for by the issuer) before it is staged again.
           uint16_t* buf = reinterpret_cast<uint16_t*>(sepi + (epi_chunk & 1) * 8192);
+          const bool use_tma = TM >= 32 && p.out.tma;
+          const bool issuer = (warp == 2 + 4 * Cfg::kDecGroups) && lane == 0;
+          if (use_tma) {
+            if (issuer) bulk_wait_read<1>();  // the stores that last read this buffer are done with it
+            if (!(epi_ok = epi_sync())) break;
+          }
 #pragma unroll
           for (int j = 0; j < kCh; ++j) {
             const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
@@ -396,6 +404,18 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             o = __fadd_rn(o, bias);
             buf[j * 128 + r] = p.y_dtype == OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o))
                                                      : __half_as_ushort(__float2half_rn(o));
+          }
+          if (use_tma) {
+            fence_proxy_async_smem();
+            if (!(epi_ok = epi_sync())) break;
+            if (issuer) {
+#pragma unroll
+              for (int d = 0; d < kMaxPeers; ++d)
+                if (d < p.out.ndst) tma_store_2d(&out_maps.m[d], buf, nt * 128, mt * TM + c0);
+              bulk_commit();
+            }
+            ++epi_chunk;
+            continue;
           }
           if (!(epi_ok = epi_sync())) break;
 #pragma unroll
@@ -428,7 +448,10 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       __syncwarp();
       if (lane == 0) arrive_leader(&acc_empty[b]);
     }
-    if (warp == 2 + 4 * Cfg::kDecGroups && lane == 0) bulk_wait_all();  // partial stores complete
+    if (warp == 2 + 4 * Cfg::kDecGroups && lane == 0) {
+      bulk_wait_all();  // partial / output tensor stores complete
+      fence_proxy_async_global();
+    }
   }
 
   // Warps 0 and 1 ran their loops on one elected lane; reconverge before the block barrier

@@ -1,5 +1,6 @@
 // Host-side declarations shared by the library's translation units (not part of the ABI).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -7,6 +8,7 @@
 namespace qlin {
 
 struct PeerOut;
+struct PeerMaps;
 
 int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int Kp, int group, int mode, void* out,
                     int32_t* row_exp, float* row_scale, int perm, cudaStream_t stream);
@@ -48,6 +50,7 @@ struct F16GemmArgs {
   int tm;           // token tile (0 = auto)
   int k_splits;     // 0 = auto
   const PeerOut* out = nullptr;  // peer destinations + flag protocol (null: plain output to y)
+  const PeerMaps* out_maps = nullptr;  // destination tensor maps when out->tma
 };
 
 // Returns 0 on success, a positive QLIN_* code on failure (message via set_error).
@@ -69,6 +72,8 @@ int run_i8_gemm(int bits, const void* xq, long long kp, const float* sx, int M, 
                 long long ldy, cudaStream_t stream);
 
 void set_error(const char* fmt, ...);
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem, uint64_t cols, uint64_t rows,
+                 uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz);
 int sm_count();
 void* device_status_ptr();
 

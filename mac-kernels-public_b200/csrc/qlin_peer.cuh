@@ -18,6 +18,8 @@
 // The wait is bounded (timeout_ms, default 10 s): on expiry the kernel records a status word,
 // raises the CTA's abort flag and skips its tiles, so a missing rank shows up as an error code.
 #pragma once
+#include <cuda.h>
+
 #include "qlin_ptx.cuh"
 
 namespace qlin {
@@ -32,7 +34,14 @@ struct PeerSync {
 };
 static_assert(sizeof(PeerSync) == 64, "PeerSync is one 64-byte pad");
 
+// Tensor maps of the destinations (2-D {n, m} over each destination slab, box {128, 32}), for the
+// TMA-store epilogue; a __grid_constant__ kernel parameter.
+struct PeerMaps {
+  CUtensorMap m[kMaxPeers];
+};
+
 struct PeerOut {
+  int tma;       // 1: store each staged 32-token chunk with one TMA tensor store per destination
   int ndst;      // destinations of each output tile (0: plain per-element stores to GemmParams::y)
   int world;     // ranks taking part in the flag protocol (0: no waiting or signalling)
   int self;      // this rank's index in dst / sync
