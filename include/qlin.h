@@ -62,6 +62,20 @@ int qlin_int8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
                      const void* scale, int scale_dtype, const void* bias, int bias_dtype, int convrot_group,
                      void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The INT8 linear with an unmerged LoRA fused in: y = (linear) + lora_scale * t . up^T, where
+ * t = x . down^T [m, rank] is computed by the caller (a plain GEMM, e.g. cuBLAS) and passed with its
+ * row pitch ldt; up [n, rank] with pitch ldu (dtypes f32 / f16 / bf16), rank <= 256.  The LoRA
+ * term runs as extra K stages of the same tensor-core GEMM (bf16 operands, fp32 accumulator), so it
+ * is added before the output's single rounding.  Replaces the fused LoRA epilogue of the reference's
+ * backend (`lora_down`, `lora_up`, `lora_scale`; docs/upstream/comfy-kitchen-mps-backend.md:35,
+ * docs/findings.md:251-273). */
+size_t qlin_int8_linear_lora_workspace(int64_t m, int64_t n, int64_t k, int64_t rank);
+int qlin_int8_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q, int64_t n,
+                          const void* scale, int scale_dtype, const void* bias, int bias_dtype, int convrot_group,
+                          const void* lora_t, int lora_t_dtype, int64_t ldt, const void* lora_up, int lora_up_dtype,
+                          int64_t ldu, int64_t rank, float lora_scale, void* y, int y_dtype, int64_t ldy,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * GGUF block-format linear (Q4_0, Q8_0, Q4_K, Q6_K, IQ4_NL).
  * Replaces comfy-kitchen `gguf_linear(x, weight, qtype, shape, bias, out_dtype)` and its decode
@@ -81,6 +95,14 @@ size_t qlin_gguf_linear_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, 
 int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
                      const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
                      int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The GGUF linear with an unmerged LoRA fused in (as qlin_int8_linear_lora). */
+size_t qlin_gguf_linear_lora_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, int64_t ldx, int64_t rank);
+int qlin_gguf_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                          const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype,
+                          const void* lora_t, int lora_t_dtype, int64_t ldt, const void* lora_up, int lora_up_dtype,
+                          int64_t ldu, int64_t rank, float lora_scale, void* y, int y_dtype, int64_t ldy,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 /* The GGUF linear with the fp16 activation given as x_slabs column slabs, [x_slabs][m][k / x_slabs]
  * (slab i holds columns i*k/x_slabs ...; rows ldx apart, slabs x_slab_stride elements apart) —

@@ -180,6 +180,51 @@ static int gguf_slabs_impl(const void* x, int64_t m, int64_t k, int64_t ldx, int
   return run_f16_gemm(a, stream);
 }
 
+// Unmerged LoRA (y += scale * t . up^T with t = x . down^T computed by the caller) fused into the
+// linear as extra K stages; see GemmParams::main_k_stages.
+struct LoraArgs {
+  const void* t;
+  int t_dtype;
+  int64_t ldt;
+  const void* up;
+  int up_dtype;
+  int64_t ldu;
+  int64_t rank;
+  float scale;
+};
+
+static int64_t lora_k_of(const LoraArgs* l) { return l == nullptr ? 0 : round_up(l->rank, 64); }
+
+static size_t lora_bytes(int64_t m, int64_t n, const LoraArgs* l) {
+  const int64_t rk = lora_k_of(l);
+  return rk == 0 ? 0 : align256((size_t)m * rk * 2) + align256((size_t)round_up(n, 128) * rk * 2);
+}
+
+static int attach_lora(const LoraArgs* l, F16GemmArgs& a, Carver& ws, cudaStream_t stream) {
+  if (l == nullptr) return QLIN_OK;
+  if (l->rank <= 0 || l->rank > 256 || !is_float_dtype(l->t_dtype) || !is_float_dtype(l->up_dtype) ||
+      l->t == nullptr || l->up == nullptr || l->ldt < l->rank || l->ldu < l->rank) {
+    set_error("lora: rank 1..256, float t [m, rank] and up [n, rank]");
+    return QLIN_EDECLINE;
+  }
+  const int rk = (int)lora_k_of(l);
+  const int n_pad = (int)round_up(a.N, 128);
+  void* t_out = ws.take((size_t)a.M * rk * 2);
+  void* u_out = ws.take((size_t)n_pad * rk * 2);
+  if (ws.off > ws.cap) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  launch_lora_operands(l->t, l->t_dtype, l->ldt, a.M, l->up, l->up_dtype, l->ldu, a.N, n_pad, (int)l->rank, rk,
+                       l->scale, a.col_scale, a.col_scale_kind, a.w_row_exp, a.x_row_exp, t_out, u_out, stream);
+  const int rc = check_cuda("lora operand launch");
+  if (rc) return rc;
+  a.lora_t = t_out;
+  a.lora_u_ptr = u_out;
+  a.lora_k = rk;
+  return QLIN_OK;
+}
+
 extern "C" {
 
 const char* qlin_version(void) { return "qlin 0.1 (sm_100a, tcgen05)"; }
@@ -207,9 +252,10 @@ size_t qlin_int8_linear_workspace(int64_t m, int64_t n, int64_t k) {
   return f16_operand_bytes(m, k) + align256(f16_gemm_partial_bytes((int)m, (int)n, (int)k, WF_INT8, 0, 0));
 }
 
-int qlin_int8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q, int64_t n,
-                     const void* scale, int scale_dtype, const void* bias, int bias_dtype, int convrot_group, void* y,
-                     int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream_) {
+static int int8_linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
+                            int64_t n, const void* scale, int scale_dtype, const void* bias, int bias_dtype,
+                            int convrot_group, void* y, int y_dtype, int64_t ldy, void* workspace,
+                            size_t workspace_bytes, void* stream_, const LoraArgs* lora) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (m < 0 || n < 0 || k < 0 || ldx < k || ldy < n) {
     set_error("bad sizes m=%lld n=%lld k=%lld ldx=%lld ldy=%lld", (long long)m, (long long)n, (long long)k,
@@ -253,14 +299,41 @@ int qlin_int8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
   a.y = y;
   a.y_dtype = out_kind_of(y_dtype);
   a.ldy = ldy;
-  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, WF_INT8, 0, 0);
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(lora)), WF_INT8, 0, 0);
   a.partial = reinterpret_cast<float*>(ws.take(pb));
   a.partial_bytes = pb;
   if (ws.off > ws.cap && pb > 0) {
     set_error("workspace too small: need %zu bytes", ws.off);
     return QLIN_EINVAL;
   }
+  rc = attach_lora(lora, a, ws, stream);
+  if (rc) return rc;
   return run_f16_gemm(a, stream);
+}
+
+int qlin_int8_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q, int64_t n,
+                     const void* scale, int scale_dtype, const void* bias, int bias_dtype, int convrot_group, void* y,
+                     int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  return int8_linear_impl(x, x_dtype, m, k, ldx, q, n, scale, scale_dtype, bias, bias_dtype, convrot_group, y, y_dtype,
+                          ldy, workspace, workspace_bytes, stream, nullptr);
+}
+
+size_t qlin_int8_linear_lora_workspace(int64_t m, int64_t n, int64_t k, int64_t rank) {
+  LoraArgs l{};
+  l.rank = rank;
+  return f16_operand_bytes(m, k) +
+         align256(f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(&l)), WF_INT8, 0, 0)) +
+         lora_bytes(m, n, &l);
+}
+
+int qlin_int8_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q, int64_t n,
+                          const void* scale, int scale_dtype, const void* bias, int bias_dtype, int convrot_group,
+                          const void* lora_t, int lora_t_dtype, int64_t ldt, const void* lora_up, int lora_up_dtype,
+                          int64_t ldu, int64_t rank, float lora_scale, void* y, int y_dtype, int64_t ldy,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  const LoraArgs l{lora_t, lora_t_dtype, ldt, lora_up, lora_up_dtype, ldu, rank, lora_scale};
+  return int8_linear_impl(x, x_dtype, m, k, ldx, q, n, scale, scale_dtype, bias, bias_dtype, convrot_group, y, y_dtype,
+                          ldy, workspace, workspace_bytes, stream, &l);
 }
 
 // ------------------------------------------------------------------------------------------ GGUF
@@ -311,9 +384,10 @@ size_t qlin_gguf_linear_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, 
   return f16_operand_bytes(m, k) + align256(pb);
 }
 
-int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
-                     const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
-                     int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream_) {
+static int gguf_linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                            const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
+                            int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream_,
+                            const LoraArgs* lora) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (m < 0 || n < 0 || k < 0 || ldx < k || ldy < n) {
     set_error("bad sizes");
@@ -350,14 +424,44 @@ int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t l
   a.y = y;
   a.y_dtype = out_kind_of(y_dtype);
   a.ldy = ldy;
-  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)k, qtype, 0, 0);
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(lora)), qtype, 0, 0);
   a.partial = reinterpret_cast<float*>(ws.take(pb));
   a.partial_bytes = pb;
   if (ws.off > ws.cap && pb > 0) {
     set_error("workspace too small: need %zu bytes", ws.off);
     return QLIN_EINVAL;
   }
+  rc = attach_lora(lora, a, ws, stream);
+  if (rc) return rc;
   return run_f16_gemm(a, stream);
+}
+
+int qlin_gguf_linear(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                     const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
+                     int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  return gguf_linear_impl(x, x_dtype, m, k, ldx, packed, row_exp, qtype, n, bias, bias_dtype, y, y_dtype, ldy,
+                          workspace, workspace_bytes, stream, nullptr);
+}
+
+size_t qlin_gguf_linear_lora_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, int64_t ldx, int64_t rank) {
+  (void)x_dtype;
+  (void)ldx;
+  LoraArgs l{};
+  l.rank = rank;
+  size_t pb = 0;
+  for (int fmt : {WF_Q8_0, WF_Q6_K})
+    pb = std::max(pb, f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(&l)), fmt, 0, 0));
+  return f16_operand_bytes(m, k) + align256(pb) + lora_bytes(m, n, &l);
+}
+
+int qlin_gguf_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                          const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype,
+                          const void* lora_t, int lora_t_dtype, int64_t ldt, const void* lora_up, int lora_up_dtype,
+                          int64_t ldu, int64_t rank, float lora_scale, void* y, int y_dtype, int64_t ldy,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  const LoraArgs l{lora_t, lora_t_dtype, ldt, lora_up, lora_up_dtype, ldu, rank, lora_scale};
+  return gguf_linear_impl(x, x_dtype, m, k, ldx, packed, row_exp, qtype, n, bias, bias_dtype, y, y_dtype, ldy,
+                          workspace, workspace_bytes, stream, &l);
 }
 
 int qlin_gguf_linear_slabs(const void* x, int64_t m, int64_t k, int64_t ldx, int x_slabs, int64_t x_slab_stride,

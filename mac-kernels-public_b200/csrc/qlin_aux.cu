@@ -577,7 +577,8 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
 __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int splits, int M, int N, int Mp,
                                        const void* col_scale, int col_scale_kind, const int32_t* w_row_exp,
                                        const int32_t* x_row_exp, const float* x_row_scale, const void* bias,
-                                       int bias_kind, void* y, int y_dtype, long long ldy, const PeerOut po) {
+                                       int bias_kind, void* y, int y_dtype, long long ldy, const PeerOut po,
+                                       int lora) {
   __shared__ float tile[32][33];
   const int m0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
@@ -599,6 +600,7 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int sp
     if (col_scale_kind == 1) cs = __half2float(reinterpret_cast<const __half*>(col_scale)[n]);
     else if (col_scale_kind == 2) cs = reinterpret_cast<const float*>(col_scale)[n];
     else if (col_scale_kind == 3) cs = exp2i(w_row_exp[n]);
+    if (lora) cs = lora_safe_scale(cs);
     float o = __fmul_rn(tile[tx][i], cs);
     if (x_row_exp != nullptr) o = __fmul_rn(o, exp2i(x_row_exp[m]));
     if (x_row_scale != nullptr) o = __fmul_rn(o, x_row_scale[m]);
@@ -894,6 +896,37 @@ __global__ void kitchen_grid_kernel(const uint8_t* __restrict__ q, const uint8_t
 }
 
 // ---------------------------------------------------------------------------------------------
+// Fused-LoRA operands (bf16): T'[m][r] = t[m][r] * 2^-f[m] (the activation's row exponent, so the
+// GEMM epilogue's 2^f restores t) and U'[n][r] = up[n][r] * scale / cs[n] (the column scale the
+// epilogue applies), zero-padded to rk columns and n_pad rows.
+// ---------------------------------------------------------------------------------------------
+__global__ void lora_t_kernel(const void* __restrict__ t, int t_dtype, long long ldt, int M, int R, int rk,
+                              const int32_t* __restrict__ x_row_exp, __nv_bfloat16* __restrict__ out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)M * rk) return;
+  const int m = (int)(i / rk), r = (int)(i - (long long)m * rk);
+  float v = r < R ? load_x(t, t_dtype, (long long)m * ldt + r) : 0.f;
+  if (x_row_exp != nullptr) v = scale_pow2(v, x_row_exp[m]);
+  out[i] = __float2bfloat16_rn(v);
+}
+
+__global__ void lora_u_kernel(const void* __restrict__ up, int up_dtype, long long ldu, int N, int n_pad, int R,
+                              int rk, float scale, const void* __restrict__ cs, int cs_kind,
+                              const int32_t* __restrict__ w_row_exp, __nv_bfloat16* __restrict__ out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)n_pad * rk) return;
+  const int n = (int)(i / rk), r = (int)(i - (long long)n * rk);
+  float v = 0.f;
+  if (n < N && r < R) {
+    v = __fmul_rn(load_x(up, up_dtype, (long long)n * ldu + r), scale);
+    if (cs_kind == 1) v = __fdiv_rn(v, lora_safe_scale(__half2float(reinterpret_cast<const __half*>(cs)[n])));
+    else if (cs_kind == 2) v = __fdiv_rn(v, lora_safe_scale(reinterpret_cast<const float*>(cs)[n]));
+    else if (cs_kind == 3) v = scale_pow2(v, w_row_exp[n]);
+  }
+  out[i] = __float2bfloat16_rn(v);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------------------------
 template <int E, int MODE, int BPW>
@@ -990,7 +1023,7 @@ void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_s
 void launch_splitk_finalize(const float* partial, int splits, int M, int N, int Mp, const void* col_scale,
                             int cs_kind, const int32_t* w_row_exp, const int32_t* x_row_exp,
                             const float* x_row_scale, const void* bias, int bias_kind, void* y, int y_dtype,
-                            long long ldy, cudaStream_t s, const PeerOut* out) {
+                            long long ldy, cudaStream_t s, const PeerOut* out, int lora) {
   if (M == 0 || N == 0) return;
   dim3 grid((M + 31) / 32, (N + 31) / 32);
   PeerOut po{};
@@ -999,7 +1032,8 @@ void launch_splitk_finalize(const float* partial, int splits, int M, int N, int 
     po.wait = 0;  // the GEMM that produced the partials waited
   }
   splitk_finalize_kernel<<<grid, dim3(32, 8), 0, s>>>(partial, splits, M, N, Mp, col_scale, cs_kind, w_row_exp,
-                                                      x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy, po);
+                                                      x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy, po,
+                                                      lora);
 }
 
 void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* codebook, int bits, int group, int N,
@@ -1007,6 +1041,19 @@ void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* co
   const long long threads = (long long)N * (K / 16);
   if (threads == 0) return;
   kitchen_grid_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(q, s_rel, codebook, bits, group, N, K, out);
+}
+
+void launch_lora_operands(const void* t, int t_dtype, long long ldt, int M, const void* up, int up_dtype,
+                          long long ldu, int N, int n_pad, int R, int rk, float scale, const void* cs, int cs_kind,
+                          const int32_t* w_row_exp, const int32_t* x_row_exp, void* t_out, void* u_out,
+                          cudaStream_t s) {
+  const long long nt = (long long)M * rk, nu = (long long)n_pad * rk;
+  if (nt > 0)
+    lora_t_kernel<<<(unsigned)((nt + 255) / 256), 256, 0, s>>>(t, t_dtype, ldt, M, R, rk, x_row_exp,
+                                                               reinterpret_cast<__nv_bfloat16*>(t_out));
+  if (nu > 0)
+    lora_u_kernel<<<(unsigned)((nu + 255) / 256), 256, 0, s>>>(up, up_dtype, ldu, N, n_pad, R, rk, scale, cs, cs_kind,
+                                                               w_row_exp, reinterpret_cast<__nv_bfloat16*>(u_out));
 }
 
 }  // namespace qlin

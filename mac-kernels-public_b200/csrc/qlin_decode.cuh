@@ -55,6 +55,13 @@ __device__ __forceinline__ float exp2i(int e) {  // 2^e for -126 <= e <= 127
   return __int_as_float((e + 127) << 23);
 }
 
+// With a fused LoRA the accumulator holds base + LoRA / colscale, so a column scale of (nearly)
+// zero is raised to +-2^-100: the base term still vanishes in the output and the LoRA term stays
+// finite (the LoRA operand is divided by the same raised scale).
+__device__ __forceinline__ float lora_safe_scale(float cs) {
+  return fabsf(cs) >= 7.888609052210118e-31f ? cs : copysignf(7.888609052210118e-31f, cs);
+}
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFF)));
 }

@@ -279,7 +279,8 @@ size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits
 }
 
 template <class Dec, int TM, int STAGES, bool PAIR>
-static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const PeerMaps& maps,
+static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
+                      const PeerMaps& maps,
                       const GemmParams& p, cudaStream_t stream) {
   constexpr int smem = qgemm_f16_smem_bytes<Dec, TM, STAGES, PAIR>();
   static_assert(smem <= 232448, "shared memory per CTA");
@@ -311,9 +312,9 @@ static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtens
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, tx, tw, tp, maps, p);
+    e = cudaLaunchKernelEx(&cfg, kern, tx, tw, tp, tt, maps, p);
   } else {
-    kern<<<grid, F16Cfg<TM, STAGES, PAIR>::kThreads, smem, stream>>>(tx, tw, tp, maps, p);
+    kern<<<grid, F16Cfg<TM, STAGES, PAIR>::kThreads, smem, stream>>>(tx, tw, tp, tt, maps, p);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
@@ -324,24 +325,26 @@ static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtens
 }
 
 template <class Dec, int TM>
-static int launch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const PeerMaps& maps,
+static int launch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
+                      const PeerMaps& maps,
                      const GemmParams& p, bool pair, cudaStream_t stream) {
   if constexpr (TM >= 128) {
-    if (pair) return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, true>(), true>(tx, tw, tp, maps, p, stream);
+    if (pair) return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, true>(), true>(tx, tw, tp, tt, maps, p, stream);
   }
-  return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, false>(), false>(tx, tw, tp, maps, p, stream);
+  return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, false>(), false>(tx, tw, tp, tt, maps, p, stream);
 }
 
 template <class Dec>
-static int dispatch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const PeerMaps& maps,
+static int dispatch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
+                      const PeerMaps& maps,
                        const GemmParams& p, int tm, bool pair, cudaStream_t stream) {
   switch (tm) {
-    case 16: return launch_tm<Dec, 16>(tx, tw, tp, maps, p, pair, stream);
-    case 32: return launch_tm<Dec, 32>(tx, tw, tp, maps, p, pair, stream);
-    case 64: return launch_tm<Dec, 64>(tx, tw, tp, maps, p, pair, stream);
-    case 128: return launch_tm<Dec, 128>(tx, tw, tp, maps, p, pair, stream);
-    case 192: return launch_tm<Dec, 192>(tx, tw, tp, maps, p, pair, stream);
-    case 256: return launch_tm<Dec, 256>(tx, tw, tp, maps, p, pair, stream);
+    case 16: return launch_tm<Dec, 16>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 32: return launch_tm<Dec, 32>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 64: return launch_tm<Dec, 64>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 128: return launch_tm<Dec, 128>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 192: return launch_tm<Dec, 192>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 256: return launch_tm<Dec, 256>(tx, tw, tp, tt, maps, p, pair, stream);
     default: set_error("unsupported token tile %d", tm); return 2;
   }
 }
@@ -360,17 +363,20 @@ static bool staged_output_ok(const F16GemmArgs& a) {
 
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return 0;
-  if (a.M <= 2) {
+  if (a.M <= 2 && a.lora_k == 0) {
     const int rc = run_gemv(a, stream);
     if (rc >= 0) return rc;
   }
   int tm = a.tm, splits = a.k_splits;
-  plan_f16(a.M, a.N, a.K, a.fmt, &tm, &splits);
+  plan_f16(a.M, a.N, a.K + a.lora_k, a.fmt, &tm, &splits);
   GemmParams p{};
   p.M = a.M;
   p.N = a.N;
   p.K = a.K;
-  p.num_k_stages = (a.K + 63) / 64;
+  p.main_k_stages = (a.K + 63) / 64;
+  p.num_k_stages = p.main_k_stages + a.lora_k / 64;
+  p.lora_u = reinterpret_cast<const __nv_bfloat16*>(a.lora_u_ptr);
+  p.lora_k = a.lora_k;
   p.m_tiles = (a.M + tm - 1) / tm;
   p.n_tiles = (a.N + 127) / 128;
   p.k_splits = splits;
@@ -434,6 +440,12 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   } else {
     tw = tx;  // unused by bulk-copy decoders
   }
+  CUtensorMap tt = tx;  // LoRA low-rank activation T' [M][lora_k] bf16, box {64, token rows per CTA}
+  if (a.lora_k > 0) {
+    rc = make_tmap_2d(&tt, a.lora_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)a.lora_k, (uint64_t)a.M,
+                      (uint64_t)a.lora_k * 2, 64, (uint32_t)(pair ? tm / 2 : tm), CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
   CUtensorMap tp = tx;  // split-K partials [splits][N][Mp] fp32, box {32 tokens, 128 rows}
   if (splits > 1 && tm >= 32) {
     rc = make_tmap_3d(&tp, p.partial, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)p.Mp, (uint64_t)a.N,
@@ -441,18 +453,19 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
     if (rc) return rc;
   }
   switch (a.fmt) {
-    case WF_INT8: rc = dispatch_tm<DecInt8>(tx, tw, tp, maps, p, tm, pair, stream); break;
-    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, maps, p, tm, pair, stream); break;
-    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(tx, tw, tp, maps, p, tm, pair, stream); break;
-    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(tx, tw, tp, maps, p, tm, pair, stream); break;
-    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(tx, tw, tp, maps, p, tm, pair, stream); break;
-    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(tx, tw, tp, maps, p, tm, pair, stream); break;
+    case WF_INT8: rc = dispatch_tm<DecInt8>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
+    case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
+    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
+    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
+    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
+    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     default: set_error("unknown weight format %d", a.fmt); return 2;
   }
   if (rc) return rc;
   if (splits > 1) {
     launch_splitk_finalize(p.partial, splits, a.M, a.N, p.Mp, a.col_scale, a.col_scale_kind, a.w_row_exp,
-                           a.x_row_exp, nullptr, a.bias, a.bias_kind, a.y, a.y_dtype, a.ldy, stream, a.out);
+                           a.x_row_exp, nullptr, a.bias, a.bias_kind, a.y, a.y_dtype, a.ldy, stream, a.out,
+                           a.lora_k > 0);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       set_error("split-K finalize launch failed: %s", cudaGetErrorString(e));

@@ -48,6 +48,12 @@ struct GemmParams {
   long long ldy;
   float* partial;  // split-K partial sums, n-major [k_splits][N][Mp]; null when k_splits == 1
   int Mp;          // M rounded up to the token tile (row pitch of the partials)
+  // Unmerged LoRA fused as extra K stages: stages [main_k_stages, num_k_stages) multiply the bf16
+  // low-rank activation T' (tensor map tmap_t) by the bf16 up-projection U' [n_tiles*128][lora_k]
+  // into the same accumulator (main_k_stages == num_k_stages: no LoRA).
+  int main_k_stages;
+  const __nv_bfloat16* lora_u;
+  int lora_k;
   DeviceStatus* status;
   // Staged 2-byte output: out.ndst > 0 writes each finished 32-token chunk through shared memory
   // with 16-byte stores to every destination (this rank's slab in each rank's gathered buffer);
@@ -104,8 +110,8 @@ __device__ __forceinline__ void store_out(void* y, int dtype, long long idx, flo
 template <class Dec, int TM, int STAGES, bool PAIR>
 __global__ void __launch_bounds__(448, 1)
 qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                 const __grid_constant__ CUtensorMap tmap_p, const __grid_constant__ PeerMaps out_maps,
-                 const GemmParams p) {
+                 const __grid_constant__ CUtensorMap tmap_p, const __grid_constant__ CUtensorMap tmap_t,
+                 const __grid_constant__ PeerMaps out_maps, const GemmParams p) {
   using Cfg = F16Cfg<TM, STAGES, PAIR>;
   constexpr uint32_t kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -210,6 +216,12 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
+          if (kst >= p.main_k_stages) {  // LoRA stage: the low-rank activation only
+            mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes);
+            tma_load_2d(sx + s * Cfg::kXStageBytes, &tmap_t, &full[s], (kst - p.main_k_stages) * 64,
+                        mt * TM + (int)rank * Cfg::kXRows);
+            continue;
+          }
           mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes + Dec::kStageBytes);
           {
             const int k0 = kst * 64;
@@ -220,7 +232,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           if constexpr (Dec::kTma) {
             tma_load_2d(sw + s * kWStage, &tmap_w, &full[s], kst * 64, nt * 128);
           } else {
-            const uint8_t* src = p.w_stages + ((size_t)nt * p.num_k_stages + kst) * Dec::kStageBytes;
+            const uint8_t* src = p.w_stages + ((size_t)nt * p.main_k_stages + kst) * Dec::kStageBytes;
             bulk_load(sw + s * kWStage, src, Dec::kStageBytes, &full[s]);
           }
         }
@@ -238,7 +250,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA issuer
     if (leader && elect_one()) {
-      constexpr uint32_t idesc = idesc_f16_f32(128 * Cfg::kCtas, TM);
+      constexpr uint32_t idesc_main = idesc_f16_f32(128 * Cfg::kCtas, TM);
+      constexpr uint32_t idesc_lora = idesc_bf16_f32(128 * Cfg::kCtas, TM);
       uint32_t it = 0, tile_i = 0;
       bool ok = *abort_flag == 0;
       for (int t = tile0; t < num_tiles && ok; t += tile_step, ++tile_i) {
@@ -257,6 +270,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           tc_fence_after();
           const uint32_t a_tmem = tmem_base + Cfg::kACol0 + as * 32;
           const uint64_t b_desc = smem_desc_sw128(smem_u32(sx + s * Cfg::kXStageBytes));
+          const uint32_t idesc = kst < p.main_k_stages ? idesc_main : idesc_lora;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t acc = (kst > s0 || kk > 0) ? 1u : 0u;
@@ -298,7 +312,16 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         const uint32_t ph = (it / STAGES) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag, p.status, 4)) { ok = false; break; }
         uint32_t a[32];
-        Dec::decode(sw + s * kWStage, r, rscale, a);
+        if (kst < p.main_k_stages) {
+          Dec::decode(sw + s * kWStage, r, rscale, a);
+        } else {  // LoRA stage: 64 bf16 values of this row of U', as stored
+          const uint4* u = reinterpret_cast<const uint4*>(p.lora_u + (size_t)n * p.lora_k + (kst - p.main_k_stages) * 64);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 v = __ldg(u + j);
+            a[4 * j] = v.x; a[4 * j + 1] = v.y; a[4 * j + 2] = v.z; a[4 * j + 3] = v.w;
+          }
+        }
         // the slot's previous weights have been consumed by their MMAs
         const int as = it % Cfg::kASlots;
         if (!mbar_wait(&a_empty[as], ((it / Cfg::kASlots) & 1) ^ 1, abort_flag, p.status, 8)) { ok = false; break; }
@@ -341,6 +364,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       float cs = 1.f, bias = 0.f;
       if (p.k_splits == 1 && n_ok) {
         cs = load_colscale(p, n);
+        if (p.lora_k > 0) cs = lora_safe_scale(cs);
         bias = load_bias(p.bias, p.bias_kind, n);
       }
 #pragma unroll 1

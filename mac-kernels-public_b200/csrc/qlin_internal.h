@@ -20,8 +20,14 @@ void launch_splitk_finalize(const float* partial, int splits, int M, int N, int 
                             int cs_kind, const int32_t* w_row_exp, const int32_t* x_row_exp,
                             const float* x_row_scale, const void* bias, int bias_kind, void* y, int y_dtype,
                             long long ldy, cudaStream_t s,
-                            const PeerOut* out = nullptr);
+                            const PeerOut* out = nullptr, int lora = 0);
 
+// Fused-LoRA operands: T'[m][r] = bf16(t[m][r] * 2^-f[m]) and U'[n][r] = bf16(up[n][r] * scale / cs[n])
+// (cs: the linear's column scale; 2^e[n] for GGUF), zero past r = R and n = N.
+void launch_lora_operands(const void* t, int t_dtype, long long ldt, int M, const void* up, int up_dtype,
+                          long long ldu, int N, int n_pad, int R, int rk, float scale, const void* cs, int cs_kind,
+                          const int32_t* w_row_exp, const int32_t* x_row_exp, void* t_out, void* u_out,
+                          cudaStream_t s);
 void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* codebook, int bits, int group, int N,
                          int K, int8_t* out, cudaStream_t s);
 
@@ -51,6 +57,11 @@ struct F16GemmArgs {
   int k_splits;     // 0 = auto
   const PeerOut* out = nullptr;  // peer destinations + flag protocol (null: plain output to y)
   const PeerMaps* out_maps = nullptr;  // destination tensor maps when out->tma
+  // Fused unmerged LoRA: T' bf16 [M][lora_k] and U' bf16 [n_tiles * 128][lora_k] (lora_k a
+  // multiple of 64; 0 = none), prepared by launch_lora_operands.
+  const void* lora_t = nullptr;
+  const void* lora_u_ptr = nullptr;
+  int lora_k = 0;
 };
 
 // Returns 0 on success, a positive QLIN_* code on failure (message via set_error).

@@ -347,10 +347,13 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
 }
 
 // Instruction descriptor, dense, both operands K-major.
-//   c_format [4,6): 1 = f32, 2 = s32;  a/b format [7,10)/[10,13): f16 = 0 (kind::f16), s8 = 1 (kind::i8)
+//   c_format [4,6): 1 = f32, 2 = s32;  a/b format [7,10)/[10,13): f16 = 0, bf16 = 1 (kind::f16), s8 = 1 (kind::i8)
 //   n_dim [17,23) = N >> 3;  m_dim [24,29) = M >> 4
 __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n) {
   return (1u << 4) | (0u << 7) | (0u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_s8_s32(uint32_t m, uint32_t n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);

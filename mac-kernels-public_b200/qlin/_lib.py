@@ -27,10 +27,16 @@ SIGNATURES = {
     "qlin_device_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint32)]),
     "qlin_int8_linear_workspace": (_sz, [_i64, _i64, _i64]),
     "qlin_int8_linear": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i, _p, _i, _i, _p, _i, _i64, _p, _sz, _p]),
+    "qlin_int8_linear_lora_workspace": (_sz, [_i64, _i64, _i64, _i64]),
+    "qlin_int8_linear_lora": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i, _p, _i, _i, _p, _i, _i64, _p, _i, _i64,
+                                   _i64, ctypes.c_float, _p, _i, _i64, _p, _sz, _p]),
     "qlin_gguf_repacked_bytes": (_i, [_i, _i64, _i64, ctypes.POINTER(_sz), ctypes.POINTER(_i64)]),
     "qlin_gguf_repack": (_i, [_p, _i, _i64, _i64, _p, _sz, _p, _i64, _p]),
     "qlin_gguf_linear_workspace": (_sz, [_i64, _i64, _i64, _i, _i64]),
     "qlin_gguf_linear": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _sz, _p]),
+    "qlin_gguf_linear_lora_workspace": (_sz, [_i64, _i64, _i64, _i, _i64, _i64]),
+    "qlin_gguf_linear_lora": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _i, _i64,
+                                   _i64, ctypes.c_float, _p, _i, _i64, _p, _sz, _p]),
     "qlin_gguf_linear_slabs": (_i, [_p, _i64, _i64, _i64, _i, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _sz,
                                     _p]),
     "qlin_gguf_linear_allgather": (_i, [_p, _i64, _i64, _i64, _i, _i64, _p, _p, _i, _i64, _p, _i, _i, _i,

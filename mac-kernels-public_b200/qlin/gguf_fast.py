@@ -10,9 +10,10 @@ It returns None (stock path) for: weights that are not GGML-quantized with a sup
 patches, any patch that is not a plain LoRA (DoRA, other adapters), and inputs that are not on a
 CUDA device.  Plain LoRAs stay unmerged: call-local fp32 factors are built from the patches on
 every call (`_lora_for_call`; nothing is cached, so factors follow patch changes and never outlive
-the call), whole-layer LoRAs are stacked along the rank, row-slice LoRAs are applied to their
-output slice, and the base output is produced in fp32 so the LoRA terms join it before the single
-rounding to the input dtype.
+the call), whole-layer LoRAs are stacked along the rank and run inside the GEMM as extra K stages
+(up to rank 256; beside it otherwise), row-slice LoRAs are applied to their output slice beside a
+base output produced in fp32; either way the LoRA terms join the sum before the single rounding to
+the input dtype.
 """
 from __future__ import annotations
 
@@ -108,6 +109,11 @@ def linear(layer, x):
     shape = (int(w.tensor_shape[0]), int(w.tensor_shape[1]))
     has_lora = factors.stacked is not None or factors.sliced
     try:
+        if factors.stacked is not None and not factors.sliced:
+            # whole-layer LoRAs run inside the GEMM (extra K stages), added before the one rounding
+            down, up = factors.stacked
+            return qlin.gguf_linear(x, raw, int(qtype), shape, bias=bias, out_dtype=x.dtype, lora_down=down,
+                                    lora_up=up, lora_scale=1.0)
         y = qlin.gguf_linear(x, raw, int(qtype), shape, bias=bias,
                              out_dtype=torch.float32 if has_lora else x.dtype)
     except NotImplementedError:
