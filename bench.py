@@ -424,6 +424,16 @@ def run_ours(args, rank, world):
         formats, configs = format_sweep(dev, max(3, args.steps // 4), 3, flush, stream, pk, int8_peak)
     formats["int8_convrot_g128"] = {"tflops": FLOPS / (ms * 1e-3) / 1e12, "ms": ms,
                                     "roofline_frac": roof_t / (ms * 1e-3), "bound": "tensor"}
+    if not args.no_formats:
+        # unmerged rank-128 LoRA fused into the same GEMM (flops of the base linear only)
+        gl = torch.Generator().manual_seed(5)
+        down = (torch.randn(128, K, generator=gl) / K ** 0.5).half().to(dev)
+        up = (torch.randn(N, 128, generator=gl) * 0.02).half().to(dev)
+        fn = lambda: qlin.int8_linear(xd, qd, sd, bd, torch.float16, convrot=True, convrot_groupsize=GROUP,  # noqa: E731
+                                      lora_down=down, lora_up=up, lora_scale=1.0)
+        t = statistics.mean(timed_steps(fn, max(3, args.steps // 2), args.warmup, flush, stream))
+        formats["int8_convrot_g128_lora_r128_fused"] = {"tflops": FLOPS / (t * 1e-3) / 1e12, "ms": t,
+                                                         "overhead_vs_no_lora": t / ms - 1.0}
 
     mmdit = None
     if not args.no_mmdit:
