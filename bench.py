@@ -239,7 +239,7 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
     out, cfgs = {}, {}
     g = torch.Generator().manual_seed(1)
     x = torch.randn(M, K, generator=g).to(torch.float16).to(dev)
-    for qt, name in ((8, "gguf_q8_0"), (2, "gguf_q4_0"), (12, "gguf_q4_k"), (14, "gguf_q6_k"), (20, "gguf_iq4_nl")):
+    for qt, name in sorted((qt, "gguf_" + v[0].lower()) for qt, v in O.GGUF_TYPES.items()):
         raw = torch.from_numpy(O.random_gguf_blocks(qt, N, K, seed=qt)).to(dev)
         packed, _ = qlin.repack_gguf(raw, qt, (N, K))
         fn = lambda: qlin.gguf_linear(x, raw, qt, (N, K))  # noqa: E731

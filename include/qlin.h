@@ -35,7 +35,10 @@ enum qlin_status {
 enum qlin_dtype { QLIN_F32 = 0, QLIN_F16 = 1, QLIN_BF16 = 2, QLIN_I8 = 3, QLIN_U8 = 4, QLIN_I32 = 5, QLIN_E4M3 = 6 };
 
 /* ggml type ids accepted by the GGUF entry points. */
-enum qlin_gguf_type { QLIN_Q4_0 = 2, QLIN_Q8_0 = 8, QLIN_Q4_K = 12, QLIN_Q6_K = 14, QLIN_IQ4_NL = 20 };
+enum qlin_gguf_type {
+  QLIN_Q4_0 = 2, QLIN_Q4_1 = 3, QLIN_Q5_0 = 6, QLIN_Q5_1 = 7, QLIN_Q8_0 = 8, QLIN_Q2_K = 10, QLIN_Q3_K = 11,
+  QLIN_Q4_K = 12, QLIN_Q5_K = 13, QLIN_Q6_K = 14, QLIN_IQ4_NL = 20, QLIN_IQ4_XS = 23
+};
 
 const char* qlin_version(void);
 const char* qlin_last_error(void);
@@ -77,16 +80,21 @@ int qlin_int8_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int6
                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
- * GGUF block-format linear (Q4_0, Q8_0, Q4_K, Q6_K, IQ4_NL).
+ * GGUF block-format linear: the twelve types of the reference's kernel, Q4_0, Q4_1, Q5_0, Q5_1,
+ * Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_NL, IQ4_XS (docs/research/2026-10-03-gguf-on-metal.md:59).
  * Replaces comfy-kitchen `gguf_linear(x, weight, qtype, shape, bias, out_dtype)` and its decode
  * helpers `_decode` / `gguf_row_exp_<type>` (bench/bench_gguf_linear.py:120-127; design
  * docs/research/2026-10-03-gguf-on-metal.md:83-97 in the reference).
  *
  * qlin_gguf_repack turns raw ggml blocks [n rows of k/QK blocks] into the resident stage layout
  * (one time per weight) and writes the per-row exponents e (row_exp, length padded_n = n rounded
- * up to 128).  The linear decodes each value in fp32 exactly as gguf-py 0.19.0, multiplies it by
- * 2^-e and rounds once to fp16 for the tensor cores; the epilogue restores 2^e, adds bias in fp32
- * and rounds once to the output dtype.  Requires k to be a whole number of blocks per row.
+ * up to 128).  The linear feeds the tensor cores fp16 weights w * 2^-e, where w is gguf-py 0.19.0's
+ * fp32 value: exactly RN16(w * 2^-e) for Q8_0, Q4_0, Q5_0 and IQ4_NL; one fp16 fma of exact fp16
+ * factors (the exact value rounded once) for Q4_1 and Q5_1; within two fp16 rounding steps (block
+ * scale products rounded once to fp16, then one fp16 multiply or fma) for the K-quants and IQ4_XS.
+ * The epilogue restores 2^e, adds bias in fp32 and rounds once to the output dtype.
+ * qlin_gguf_dequantize is bit-exact with gguf-py for every type.  Requires k to be a whole number
+ * of blocks per row.
  * ------------------------------------------------------------------------------------------ */
 int qlin_gguf_repacked_bytes(int qtype, int64_t n, int64_t k, size_t* bytes, int64_t* padded_n);
 int qlin_gguf_repack(const void* raw, int qtype, int64_t n, int64_t k, void* packed, size_t packed_bytes,

@@ -374,12 +374,15 @@ int qlin_gguf_repack(const void* raw, int qtype, int64_t n, int64_t k, void* pac
   return check_cuda("gguf repack launch");
 }
 
+static constexpr int kGgufFormats[] = {WF_Q4_0, WF_Q4_1, WF_Q5_0, WF_Q5_1, WF_Q8_0, WF_Q2_K,
+                                       WF_Q3_K, WF_Q4_K, WF_Q5_K, WF_Q6_K, WF_IQ4_NL, WF_IQ4_XS};
+
 // Workspace of the GGUF linear for any of the supported types (the largest plan's partials).
 size_t qlin_gguf_linear_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, int64_t ldx) {
   (void)x_dtype;
   (void)ldx;
   size_t pb = 0;
-  for (int fmt : {WF_Q8_0, WF_Q6_K})
+  for (int fmt : kGgufFormats)
     pb = std::max(pb, f16_gemm_partial_bytes((int)m, (int)n, (int)k, fmt, 0, 0));
   return f16_operand_bytes(m, k) + align256(pb);
 }
@@ -449,7 +452,7 @@ size_t qlin_gguf_linear_lora_workspace(int64_t m, int64_t n, int64_t k, int x_dt
   LoraArgs l{};
   l.rank = rank;
   size_t pb = 0;
-  for (int fmt : {WF_Q8_0, WF_Q6_K})
+  for (int fmt : kGgufFormats)
     pb = std::max(pb, f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(&l)), fmt, 0, 0));
   return f16_operand_bytes(m, k) + align256(pb) + lora_bytes(m, n, &l);
 }

@@ -379,8 +379,104 @@ __device__ __forceinline__ float f16_at(const uint8_t* p) {
   return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
 }
 
+__host__ __device__ constexpr int gguf_qk(int qtype) {
+  return (qtype == GGUF_Q2_K || qtype == GGUF_Q3_K || qtype == GGUF_Q4_K || qtype == GGUF_Q5_K ||
+          qtype == GGUF_Q6_K || qtype == GGUF_IQ4_XS) ? 256 : 32;
+}
+
+__host__ __device__ constexpr int gguf_ts(int qtype) {
+  return qtype == GGUF_Q4_0 || qtype == GGUF_IQ4_NL ? 18 : qtype == GGUF_Q4_1 ? 20 : qtype == GGUF_Q5_0 ? 22
+       : qtype == GGUF_Q5_1 ? 24 : qtype == GGUF_Q8_0 ? 34 : qtype == GGUF_Q2_K ? 84 : qtype == GGUF_Q3_K ? 110
+       : qtype == GGUF_Q4_K ? 144 : qtype == GGUF_Q5_K ? 176 : qtype == GGUF_Q6_K ? 210 : 136;
+}
+
+__device__ __forceinline__ uint32_t u32_at(const uint8_t* p) {  // little-endian, any alignment
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+// 6-bit (scale, min) of sub-block `sub` from the 12 packed bytes of a Q4_K / Q5_K superblock
+// (`gguf/quants.py:478-500`).
+__device__ __forceinline__ void k4_scale_min(const uint8_t* sc, int sub, int& s, int& m) {
+  if (sub < 4) {
+    s = sc[sub] & 0x3F;
+    m = sc[sub + 4] & 0x3F;
+  } else {
+    s = (sc[sub + 4] & 0x0F) | ((sc[sub - 4] >> 2) & 0x30);
+    m = (sc[sub + 4] >> 4) | ((sc[sub] >> 2) & 0x30);
+  }
+}
+
+// Signed 6-bit scale of 16-value group i of a Q3_K superblock (`gguf/quants.py:456-463`).
+__device__ __forceinline__ int q3k_scale(const uint8_t* sc, int i) {
+  const int lo = i < 8 ? (sc[i] & 0xF) : (sc[i - 8] >> 4);
+  const int hi = (sc[8 + (i & 3)] >> (2 * (i >> 2))) & 3;
+  return (lo | (hi << 4)) - 32;
+}
+
+// Signed 6-bit scale of sub-block i of an IQ4_XS superblock (`gguf/quants.py:1363-1369`).
+__device__ __forceinline__ int iq4xs_scale(const uint8_t* b, int i) {
+  const int lo = (b[4 + (i >> 1)] >> (4 * (i & 1))) & 0xF;
+  const int hi = ((b[2] | (b[3] << 8)) >> (2 * i)) & 3;
+  return (lo | (hi << 4)) - 32;
+}
+
+// 2-bit code of value j (0..255) of a Q2_K / Q3_K code array (`gguf/quants.py:422-424`).
+__device__ __forceinline__ int crumb_at(const uint8_t* qs, int j) {
+  return (qs[32 * (j >> 7) + (j & 31)] >> (2 * ((j & 127) >> 5))) & 3;
+}
+
 __device__ float gguf_value(const uint8_t* __restrict__ raw, int qtype, long long idx) {
   switch (qtype) {
+    case GGUF_Q4_1:
+    case GGUF_Q5_0:
+    case GGUF_Q5_1: {
+      const int ts = gguf_ts(qtype);
+      const uint8_t* b = raw + (idx / 32) * ts;
+      const int j = (int)(idx % 32);
+      const int qs = ts - 16;
+      const uint8_t byte = b[qs + (j & 15)];
+      int q = (j < 16) ? (byte & 0xF) : (byte >> 4);
+      if (qtype != GGUF_Q4_1) q |= (int)((u32_at(b + qs - 4) >> j) & 1) << 4;
+      const float d = f16_at(b);
+      if (qtype == GGUF_Q5_0) return __fmul_rn(d, (float)(q - 16));
+      return __fadd_rn(__fmul_rn(d, (float)q), f16_at(b + 2));
+    }
+    case GGUF_Q2_K: {
+      const uint8_t* b = raw + (idx / 256) * 84;
+      const int j = (int)(idx % 256);
+      const int sc = b[j / 16];
+      const float dl = __fmul_rn(f16_at(b + 80), (float)(sc & 0xF));
+      const float ml = __fmul_rn(f16_at(b + 82), (float)(sc >> 4));
+      return __fsub_rn(__fmul_rn(dl, (float)crumb_at(b + 16, j)), ml);
+    }
+    case GGUF_Q3_K: {
+      const uint8_t* b = raw + (idx / 256) * 110;
+      const int j = (int)(idx % 256);
+      const int q = crumb_at(b + 32, j) - (((b[j & 31] >> (j >> 5)) & 1) ? 0 : 4);
+      const float dl = __fmul_rn(f16_at(b + 108), (float)q3k_scale(b + 96, j / 16));
+      return __fmul_rn(dl, (float)q);
+    }
+    case GGUF_Q5_K: {
+      const uint8_t* b = raw + (idx / 256) * 176;
+      const int j = (int)(idx % 256);
+      const int sub = j / 32, l = j % 32;
+      int s, m;
+      k4_scale_min(b + 4, sub, s, m);
+      const int q = ((b[48 + 32 * (sub / 2) + l] >> (4 * (sub & 1))) & 0xF) | (((b[16 + l] >> sub) & 1) << 4);
+      const float ds = __fmul_rn(f16_at(b), (float)s);
+      const float dm = __fmul_rn(f16_at(b + 2), (float)m);
+      return __fsub_rn(__fmul_rn(ds, (float)q), dm);
+    }
+    case GGUF_IQ4_XS: {
+      const uint8_t* b = raw + (idx / 256) * 136;
+      const int j = (int)(idx % 256);
+      const int sub = j / 32, l = j % 32;
+      const uint8_t byte = b[8 + 16 * sub + (l & 15)];
+      const int nib = (l < 16) ? (byte & 0xF) : (byte >> 4);
+      constexpr int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+      const float dl = __fmul_rn(f16_at(b), (float)iq4xs_scale(b, sub));
+      return __fmul_rn(dl, (float)kv[nib]);
+    }
     case GGUF_Q4_0:
     case GGUF_IQ4_NL: {
       const uint8_t* b = raw + (idx / 32) * 18;
@@ -400,15 +496,8 @@ __device__ float gguf_value(const uint8_t* __restrict__ raw, int qtype, long lon
       const uint8_t* b = raw + (idx / 256) * 144;
       const int j = (int)(idx % 256);
       const int sub = j / 32;
-      const uint8_t* sc = b + 4;
       int s, m;
-      if (sub < 4) {
-        s = sc[sub] & 0x3F;
-        m = sc[sub + 4] & 0x3F;
-      } else {
-        s = (sc[sub + 4] & 0x0F) | ((sc[sub - 4] >> 2) & 0x30);
-        m = (sc[sub + 4] >> 4) | ((sc[sub] >> 2) & 0x30);
-      }
+      k4_scale_min(b + 4, sub, s, m);
       const uint8_t byte = b[16 + (sub / 2) * 32 + (j % 32)];
       const int q = (sub & 1) ? (byte >> 4) : (byte & 0xF);
       const float ds = __fmul_rn(f16_at(b), (float)s);
@@ -442,6 +531,55 @@ __global__ void gguf_dequant_kernel(const uint8_t* __restrict__ raw, int qtype, 
   }
 }
 
+// Upper bound on |w| over one block, from its scales only (float64, as the oracle computes it).
+__device__ double gguf_block_bound(const uint8_t* b, int qtype) {
+  switch (qtype) {
+    case GGUF_Q4_0: return fabs((double)f16_at(b)) * 8.0;
+    case GGUF_Q4_1: return fabs((double)f16_at(b)) * 15.0 + fabs((double)f16_at(b + 2));
+    case GGUF_Q5_0: return fabs((double)f16_at(b)) * 16.0;
+    case GGUF_Q5_1: return fabs((double)f16_at(b)) * 31.0 + fabs((double)f16_at(b + 2));
+    case GGUF_Q8_0: return fabs((double)f16_at(b)) * 128.0;
+    case GGUF_IQ4_NL: return fabs((double)f16_at(b)) * 127.0;
+    case GGUF_Q2_K: {
+      const double d = fabs((double)f16_at(b + 80)), dmin = fabs((double)f16_at(b + 82));
+      double v = 0.0;
+      for (int t = 0; t < 16; ++t) v = fmax(v, d * (b[t] & 0xF) * 3.0 + dmin * (b[t] >> 4));
+      return v;
+    }
+    case GGUF_Q3_K: {
+      const double d = fabs((double)f16_at(b + 108));
+      double v = 0.0;
+      for (int t = 0; t < 16; ++t) v = fmax(v, d * abs(q3k_scale(b + 96, t)) * 4.0);
+      return v;
+    }
+    case GGUF_Q4_K:
+    case GGUF_Q5_K: {
+      const double d = fabs((double)f16_at(b)), dmin = fabs((double)f16_at(b + 2));
+      const double qmax = qtype == GGUF_Q4_K ? 15.0 : 31.0;
+      double v = 0.0;
+      for (int sub = 0; sub < 8; ++sub) {
+        int s, m;
+        k4_scale_min(b + 4, sub, s, m);
+        v = fmax(v, d * s * qmax + dmin * m);
+      }
+      return v;
+    }
+    case GGUF_Q6_K: {
+      const double d = fabs((double)f16_at(b + 208));
+      double v = 0.0;
+      for (int t = 0; t < 16; ++t) v = fmax(v, d * fabs((double)(int8_t)b[192 + t]) * 32.0);
+      return v;
+    }
+    case GGUF_IQ4_XS: {
+      const double d = fabs((double)f16_at(b));
+      double v = 0.0;
+      for (int sub = 0; sub < 8; ++sub) v = fmax(v, d * abs(iq4xs_scale(b, sub)) * 127.0);
+      return v;
+    }
+  }
+  return 0.0;
+}
+
 // Per-row exponent: e = frexp(bound).exp - 15 with bound an upper bound on |w| over the row's
 // blocks read from block scales only (float64, as the oracle computes it).
 __global__ void gguf_row_exp_kernel(const uint8_t* __restrict__ raw, int qtype, int N, int K, int n_pad,
@@ -451,36 +589,10 @@ __global__ void gguf_row_exp_kernel(const uint8_t* __restrict__ raw, int qtype, 
   if (row >= n_pad) return;
   double bound = 0.0;
   if (row < N) {
-    const int qk = (qtype == GGUF_Q4_K || qtype == GGUF_Q6_K) ? 256 : 32;
-    const int ts = qtype == GGUF_Q8_0 ? 34 : qtype == GGUF_Q4_K ? 144 : qtype == GGUF_Q6_K ? 210 : 18;
+    const int qk = gguf_qk(qtype), ts = gguf_ts(qtype);
     const int nb = K / qk;
     const uint8_t* r = raw + (long long)row * nb * ts;
-    for (int blk = lane; blk < nb; blk += 32) {
-      const uint8_t* b = r + (long long)blk * ts;
-      double v = 0.0;
-      if (qtype == GGUF_Q4_0) v = fabs((double)f16_at(b)) * 8.0;
-      else if (qtype == GGUF_Q8_0) v = fabs((double)f16_at(b)) * 128.0;
-      else if (qtype == GGUF_IQ4_NL) v = fabs((double)f16_at(b)) * 127.0;
-      else if (qtype == GGUF_Q4_K) {
-        const double d = fabs((double)f16_at(b)), dmin = fabs((double)f16_at(b + 2));
-        const uint8_t* sc = b + 4;
-        for (int sub = 0; sub < 8; ++sub) {
-          int s, m;
-          if (sub < 4) {
-            s = sc[sub] & 0x3F;
-            m = sc[sub + 4] & 0x3F;
-          } else {
-            s = (sc[sub + 4] & 0x0F) | ((sc[sub - 4] >> 2) & 0x30);
-            m = (sc[sub + 4] >> 4) | ((sc[sub] >> 2) & 0x30);
-          }
-          v = fmax(v, d * s * 15.0 + dmin * m);
-        }
-      } else if (qtype == GGUF_Q6_K) {
-        const double d = fabs((double)f16_at(b + 208));
-        for (int t = 0; t < 16; ++t) v = fmax(v, d * fabs((double)(int8_t)b[192 + t]) * 32.0);
-      }
-      bound = fmax(bound, v);
-    }
+    for (int blk = lane; blk < nb; blk += 32) bound = fmax(bound, gguf_block_bound(r + (long long)blk * ts, qtype));
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) bound = fmax(bound, __shfl_xor_sync(0xffffffffu, bound, o));
@@ -495,6 +607,19 @@ __global__ void gguf_row_exp_kernel(const uint8_t* __restrict__ raw, int qtype, 
   }
 }
 
+// H word of a stage layout from 32 per-value bits (bit v = the extra bit of value v): bit 8b + g
+// of H is the bit of value 4g + b.
+__device__ __forceinline__ uint32_t h_transpose(uint32_t bits) {
+  uint32_t h = 0;
+#pragma unroll
+  for (int v = 0; v < 32; ++v) h |= ((bits >> v) & 1u) << (8 * (v & 3) + (v >> 2));
+  return h;
+}
+
+__device__ __forceinline__ void put_u32(uint8_t* p, uint32_t v) {
+  for (int i = 0; i < 4; ++i) p[i] = (uint8_t)(v >> (8 * i));
+}
+
 // One-time repack of raw GGUF rows into the pipeline-stage layout documented in qlin_decode.cuh.
 // grid = (num_k_stages, n_tiles), block = 128 (one thread per weight row of the tile).
 __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, int N, int K, int num_k_stages,
@@ -503,66 +628,119 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
   const int n = nt * 128 + r;
   uint8_t* st = out + ((size_t)nt * num_k_stages + kst) * stage_bytes;
   uint8_t payload[64];
-  uint8_t side[8];
+  uint8_t side[16];
 #pragma unroll
   for (int i = 0; i < 64; ++i) payload[i] = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) side[i] = 0;
+  for (int i = 0; i < 16; ++i) side[i] = 0;
   const int k0 = kst * 64;
   if (n < N && k0 < K) {
-    if (qtype == GGUF_Q8_0 || qtype == GGUF_Q4_0 || qtype == GGUF_IQ4_NL) {
-      const int ts = qtype == GGUF_Q8_0 ? 34 : 18;
-      const int qsb = ts - 2;
+    const int ts = gguf_ts(qtype);
+    if (gguf_qk(qtype) == 32) {
       const uint8_t* row = raw + (long long)n * (K / 32) * ts;
       for (int blk = 0; blk < 2; ++blk) {
         const int kb = k0 / 32 + blk;
         if (kb * 32 >= K) break;
         const uint8_t* b = row + (long long)kb * ts;
-        side[2 * blk] = b[0];
-        side[2 * blk + 1] = b[1];
-        for (int i = 0; i < qsb; ++i) payload[blk * qsb + i] = b[2 + i];
-      }
-    } else if (qtype == GGUF_Q4_K) {
-      const uint8_t* b = raw + ((long long)n * (K / 256) + k0 / 256) * 144;
-      const int c = (k0 % 256) / 64;  // sub-blocks 2c, 2c+1
-      for (int i = 0; i < 32; ++i) payload[i] = b[16 + c * 32 + i];
-      const uint8_t* sc = b + 4;
-      int s[2], m[2];
-      for (int t = 0; t < 2; ++t) {
-        const int sub = 2 * c + t;
-        if (sub < 4) {
-          s[t] = sc[sub] & 0x3F;
-          m[t] = sc[sub + 4] & 0x3F;
-        } else {
-          s[t] = (sc[sub + 4] & 0x0F) | ((sc[sub - 4] >> 2) & 0x30);
-          m[t] = (sc[sub + 4] >> 4) | ((sc[sub] >> 2) & 0x30);
+        switch (qtype) {
+          case GGUF_Q8_0:
+          case GGUF_Q4_0:
+          case GGUF_IQ4_NL: {
+            const int qsb = ts - 2;
+            side[2 * blk] = b[0];
+            side[2 * blk + 1] = b[1];
+            for (int i = 0; i < qsb; ++i) payload[blk * qsb + i] = b[2 + i];
+            break;
+          }
+          case GGUF_Q4_1:
+            for (int i = 0; i < 4; ++i) side[4 * blk + i] = b[i];  // d, m
+            for (int i = 0; i < 16; ++i) payload[16 * blk + i] = b[4 + i];
+            break;
+          case GGUF_Q5_0:
+            side[2 * blk] = b[0];
+            side[2 * blk + 1] = b[1];
+            put_u32(side + 4 + 4 * blk, h_transpose(u32_at(b + 2)));
+            for (int i = 0; i < 16; ++i) payload[16 * blk + i] = b[6 + i];
+            break;
+          case GGUF_Q5_1:
+            for (int i = 0; i < 4; ++i) side[4 * blk + i] = b[i];  // d, m
+            put_u32(side + 8 + 4 * blk, h_transpose(u32_at(b + 4)));
+            for (int i = 0; i < 16; ++i) payload[16 * blk + i] = b[8 + i];
+            break;
         }
       }
-      side[0] = b[0];
-      side[1] = b[1];
-      side[2] = b[2];
-      side[3] = b[3];
-      side[4] = (uint8_t)s[0];
-      side[5] = (uint8_t)s[1];
-      side[6] = (uint8_t)m[0];
-      side[7] = (uint8_t)m[1];
-    } else if (qtype == GGUF_Q6_K) {
-      const uint8_t* b = raw + ((long long)n * (K / 256) + k0 / 256) * 210;
-      const int base = k0 % 256;  // stage covers values base .. base+63 of the superblock
-      uint8_t v[64];
-      for (int i = 0; i < 64; ++i) {
-        const int j = base + i;
-        const int h = j / 128, rr = j % 128;
-        const int lo = (b[64 * h + (rr % 64)] >> (4 * (rr / 64))) & 0xF;
-        const int hi = (b[128 + 32 * h + (rr % 32)] >> (2 * (rr / 32))) & 0x3;
-        v[i] = (uint8_t)(lo | (hi << 4));
+    } else {
+      const uint8_t* b = raw + ((long long)n * (K / 256) + k0 / 256) * ts;
+      const int c = (k0 % 256) / 64;  // the stage holds superblock values 64c .. 64c+63
+      switch (qtype) {
+        case GGUF_Q2_K:
+        case GGUF_Q3_K: {
+          const uint8_t* qs = b + (qtype == GGUF_Q2_K ? 16 : 32);
+          for (int i = 0; i < 64; ++i)  // word i/16, byte i%4, bits 2*((i%16)/4)
+            payload[4 * (i >> 4) + (i & 3)] |= (uint8_t)(crumb_at(qs, 64 * c + i) << (2 * ((i & 15) >> 2)));
+          if (qtype == GGUF_Q2_K) {
+            for (int i = 0; i < 4; ++i) side[i] = b[80 + i];  // d, dmin
+            for (int t = 0; t < 4; ++t) side[4 + t] = b[4 * c + t];
+          } else {
+            side[0] = b[108];
+            side[1] = b[109];
+            for (int t = 0; t < 4; ++t) side[2 + t] = (uint8_t)(int8_t)q3k_scale(b + 96, 4 * c + t);
+            for (int w = 0; w < 2; ++w) {
+              uint32_t bits = 0;
+              for (int l = 0; l < 32; ++l) bits |= (uint32_t)((b[l] >> (2 * c + w)) & 1) << l;
+              put_u32(side + 8 + 4 * w, h_transpose(bits));
+            }
+          }
+          break;
+        }
+        case GGUF_Q4_K:
+        case GGUF_Q5_K: {
+          const int qs = qtype == GGUF_Q4_K ? 16 : 48;
+          for (int i = 0; i < 32; ++i) payload[i] = b[qs + c * 32 + i];
+          int s0, m0, s1, m1;
+          k4_scale_min(b + 4, 2 * c, s0, m0);
+          k4_scale_min(b + 4, 2 * c + 1, s1, m1);
+          for (int i = 0; i < 4; ++i) side[i] = b[i];  // d, dmin
+          side[4] = (uint8_t)s0;
+          side[5] = (uint8_t)s1;
+          side[6] = (uint8_t)m0;
+          side[7] = (uint8_t)m1;
+          if (qtype == GGUF_Q5_K) {
+            for (int w = 0; w < 2; ++w) {  // sub-block 2c + w: bit (2c + w) of qh[l]
+              uint32_t bits = 0;
+              for (int l = 0; l < 32; ++l) bits |= (uint32_t)((b[16 + l] >> (2 * c + w)) & 1) << l;
+              put_u32(side + 8 + 4 * w, h_transpose(bits));
+            }
+          }
+          break;
+        }
+        case GGUF_Q6_K: {
+          const int base = 64 * c;
+          uint8_t v[64];
+          for (int i = 0; i < 64; ++i) {
+            const int j = base + i;
+            const int h = j / 128, rr = j % 128;
+            const int lo = (b[64 * h + (rr % 64)] >> (4 * (rr / 64))) & 0xF;
+            const int hi = (b[128 + 32 * h + (rr % 32)] >> (2 * (rr / 32))) & 0x3;
+            v[i] = (uint8_t)(lo | (hi << 4));
+          }
+          for (int i = 0; i < 32; ++i) payload[i] = (uint8_t)((v[i] & 0xF) | ((v[i + 32] & 0xF) << 4));
+          for (int i = 0; i < 16; ++i)
+            payload[32 + i] =
+                (uint8_t)((v[i] >> 4) | ((v[i + 16] >> 4) << 2) | ((v[i + 32] >> 4) << 4) | ((v[i + 48] >> 4) << 6));
+          for (int t = 0; t < 4; ++t) side[t] = b[192 + base / 16 + t];
+          side[4] = b[208];
+          side[5] = b[209];
+          break;
+        }
+        case GGUF_IQ4_XS:
+          for (int i = 0; i < 32; ++i) payload[i] = b[8 + 32 * c + i];  // sub-blocks 2c, 2c+1
+          side[0] = b[0];
+          side[1] = b[1];
+          side[2] = (uint8_t)(int8_t)iq4xs_scale(b, 2 * c);
+          side[3] = (uint8_t)(int8_t)iq4xs_scale(b, 2 * c + 1);
+          break;
       }
-      for (int i = 0; i < 32; ++i) payload[i] = (uint8_t)((v[i] & 0xF) | ((v[i + 32] & 0xF) << 4));
-      for (int i = 0; i < 16; ++i)
-        payload[32 + i] = (uint8_t)((v[i] >> 4) | ((v[i + 16] >> 4) << 2) | ((v[i + 32] >> 4) << 4) | ((v[i + 48] >> 4) << 6));
-      for (int t = 0; t < 4; ++t) side[t] = b[192 + base / 16 + t];
-      side[4] = b[208];
-      side[5] = b[209];
     }
   }
   for (int j = 0; j < P; ++j)

@@ -14,6 +14,18 @@
 //     Q4_K   P=2 (the 32-byte qs chunk of sub-blocks 2c, 2c+1)  S=8 (d, dmin fp16, sc0, sc1, m0, m1 u8)
 //     Q6_K   P=3 (32 B low nibbles: v[i] | v[i+32]<<4; 16 B high pairs: v[i], v[i+16], v[i+32],
 //            v[i+48] at bits 0,2,4,6)                  S=8 (sc0..sc3 int8, d fp16, pad)
+//     Q4_1   P=2 (qs of two blocks)                     S=8 (d0, m0, d1, m1 fp16)
+//     Q5_0   P=2 (qs of two blocks)                     S=12 (d0, d1 fp16, H0, H1)
+//     Q5_1   P=2 (qs of two blocks)                     S=16 (d0, m0, d1, m1 fp16, H0, H1)
+//     Q2_K   P=1 (2-bit codes: word u, byte b, bits 2s..2s+1 = value 16u+4s+b)
+//                                                       S=8 (d, dmin fp16, the 4 scale bytes)
+//     Q3_K   P=1 (low 2 bits, as Q2_K)                  S=16 (d fp16, 4 int8 scales sc-32, pad 2,
+//                                                              H0, H1: the hmask bits)
+//     Q5_K   P=2 (as Q4_K)                              S=16 (d, dmin fp16, sc0, sc1, m0, m1, H0, H1)
+//     IQ4_XS P=2 (qs of sub-blocks 2c, 2c+1, IQ4_NL order)  S=4 (d fp16, 2 int8 scales sc-32)
+//   "H" words carry one extra bit per value, transposed so that one shift and one mask place the
+//   bits of four consecutive values (4g .. 4g+3, g = 0..7 within the word) at the same bit of
+//   four bytes: bit 8b + g of H is the bit of value 4g + b.
 //   W4 nibbles (raw [N,K/2] via TMA box {64 B, 128 rows}, 64-byte swizzle): 128 values per stage.
 //   W6 planar (kitchen layout): low-nibble plane box {64 B, 128 rows} followed by the 2-bit plane
 //     box {32 B, 128 rows}, both 64-/32-byte swizzled.
@@ -25,7 +37,10 @@
 
 namespace qlin {
 
-enum GgufType : int { GGUF_Q4_0 = 2, GGUF_Q8_0 = 8, GGUF_Q4_K = 12, GGUF_Q6_K = 14, GGUF_IQ4_NL = 20 };
+enum GgufType : int {
+  GGUF_Q4_0 = 2, GGUF_Q4_1 = 3, GGUF_Q5_0 = 6, GGUF_Q5_1 = 7, GGUF_Q8_0 = 8, GGUF_Q2_K = 10, GGUF_Q3_K = 11,
+  GGUF_Q4_K = 12, GGUF_Q5_K = 13, GGUF_Q6_K = 14, GGUF_IQ4_NL = 20, GGUF_IQ4_XS = 23
+};
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
@@ -263,6 +278,205 @@ struct DecQ6_K : PlaneStage<3, 8> {
         const uint32_t qh = ((a >> 4) & 0x000F000Fu) | hh;     // 1024 + v[32+4k+2h], ...
         out[2 * k + h] = hmul2_u32(hsub2_u32(ql, kBias), ds[k >> 2]);
         out[16 + 2 * k + h] = hmul2_u32(hsub2_u32(qh, kBias), ds[2 + (k >> 2)]);
+      }
+    }
+  }
+};
+
+// The bits of values 4g .. 4g+3 of an H word (bit 8b + g = value 4g + b) moved to bit `kAt` of
+// bytes 0..3.
+template <int kAt>
+__device__ __forceinline__ uint32_t h_bits(uint32_t h, int g) {
+  return (g <= kAt ? (h << (kAt - g)) : (h >> (g - kAt))) & (0x01010101u << kAt);
+}
+
+// Q4_1: w = d*q + m per 32-value block (gguf/quants.py:275-288).  Nibbles under the magic byte as
+// in Q4_K (high nibbles in place, scale divided by 16); d*2^-e and m*2^-e are exact fp16 (normal
+// range), so one fp16 fma gives RN16((d*q + m) * 2^-e).
+struct DecQ4_1 : PlaneStage<2, 8> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint2 sd = *reinterpret_cast<const uint2*>(side(st, r));
+    constexpr uint32_t kMagic = 0x64006400u;
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const uint32_t dm = blk ? sd.y : sd.x;
+      const float d = __fmul_rn(half_bits_to_float(dm), rscale);
+      const __half2 d0 = __float2half2_rn(d), d1 = __float2half2_rn(__fmul_rn(d, 0.0625f));
+      const __half2 m = __float2half2_rn(__fmul_rn(half_bits_to_float(dm >> 16), rscale));
+      const uint4 v = chunk(st, blk, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t a = prmt(w[t], 0x64646464u, 0x5140u), b = prmt(w[t], 0x64646464u, 0x7362u);
+        out[16 * blk + 2 * t + 0] = hfma2_u32(hsub2_u32(a & 0xFF0FFF0Fu, kMagic), d0, m);
+        out[16 * blk + 2 * t + 1] = hfma2_u32(hsub2_u32(b & 0xFF0FFF0Fu, kMagic), d0, m);
+        out[16 * blk + 8 + 2 * t + 0] = hfma2_u32(hsub2_u32(a & 0xFFF0FFF0u, kMagic), d1, m);
+        out[16 * blk + 8 + 2 * t + 1] = hfma2_u32(hsub2_u32(b & 0xFFF0FFF0u, kMagic), d1, m);
+      }
+    }
+  }
+};
+
+// Q5_0 / Q5_1: the Q4 nibble plus a fifth bit from the block's qh word (gguf/quants.py:313-330,
+// 356-375), assembled under the magic byte.  Q5_0: (1024 + q) - 1040 = q - 16 exactly, times the
+// exact fp16 d*2^-e: RN16(d*(q-16)*2^-e), bit-exact.  Q5_1: one fp16 fma q*d' + m'.
+template <bool kMin>
+struct DecQ5Block : PlaneStage<2, kMin ? 16 : 12> {
+  using Base = PlaneStage<2, kMin ? 16 : 12>;
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint32_t* sd = reinterpret_cast<const uint32_t*>(Base::side(st, r));
+    uint32_t dw[2], hw[2];
+    if constexpr (kMin) {
+      const uint4 v = *reinterpret_cast<const uint4*>(sd);
+      dw[0] = v.x;
+      dw[1] = v.y;
+      hw[0] = v.z;
+      hw[1] = v.w;
+    } else {
+      dw[0] = sd[0] & 0xFFFF;
+      dw[1] = sd[0] >> 16;
+      hw[0] = sd[1];
+      hw[1] = sd[2];
+    }
+    const uint32_t bias = kMin ? 0x64006400u : 0x64106410u;  // fp16 1024 / 1040 = 1024 + 16
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const __half2 d = scale_pair(dw[blk] & 0xFFFF, rscale);
+      const __half2 m = kMin ? scale_pair(dw[blk] >> 16, rscale) : __half2{};
+      const uint4 v = Base::chunk(st, blk, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t qlo = (w[t] & 0x0F0F0F0Fu) | h_bits<4>(hw[blk], t);             // values 4t..
+        const uint32_t qhi = ((w[t] >> 4) & 0x0F0F0F0Fu) | h_bits<4>(hw[blk], 4 + t);  // 16+4t..
+        uint32_t a0, a1, b0, b1;
+        u8x4_to_f16x4(qlo, bias, a0, a1);
+        u8x4_to_f16x4(qhi, bias, b0, b1);
+        if constexpr (kMin) {
+          out[16 * blk + 2 * t + 0] = hfma2_u32(a0, d, m);
+          out[16 * blk + 2 * t + 1] = hfma2_u32(a1, d, m);
+          out[16 * blk + 8 + 2 * t + 0] = hfma2_u32(b0, d, m);
+          out[16 * blk + 8 + 2 * t + 1] = hfma2_u32(b1, d, m);
+        } else {
+          out[16 * blk + 2 * t + 0] = hmul2_u32(a0, d);
+          out[16 * blk + 2 * t + 1] = hmul2_u32(a1, d);
+          out[16 * blk + 8 + 2 * t + 0] = hmul2_u32(b0, d);
+          out[16 * blk + 8 + 2 * t + 1] = hmul2_u32(b1, d);
+        }
+      }
+    }
+  }
+};
+
+// Q2_K / Q3_K: 2-bit codes, 16-value groups with their own scale (gguf/quants.py:405-428,
+// 432-472).  Word u of the code chunk holds the group u (values 16u .. 16u+15); shifting it by 2s
+// and masking gives values 16u+4s .. 16u+4s+3, one per byte, under the magic byte.
+//   Q2_K: w = (d*sc)*q - dmin*m, scale and min in packed fp16 (each rounded once from fp32), one
+//         fp16 fma per value.
+//   Q3_K: q = code | hbit<<2, minus 4 (exact), times RN16(d*sc*2^-e): one fp16 multiply.
+template <bool kQ3>
+struct DecQ23_K : PlaneStage<1, kQ3 ? 16 : 8> {
+  using Base = PlaneStage<1, kQ3 ? 16 : 8>;
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint4 v = Base::chunk(st, 0, r);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    constexpr uint32_t kMagic = 0x64006400u;
+    if constexpr (kQ3) {
+      const uint4 sd = *reinterpret_cast<const uint4*>(Base::side(st, r));
+      const float d = __fmul_rn(half_bits_to_float(sd.x), rscale);
+      const uint32_t scs = (sd.x >> 16) | (sd.y << 16);  // four int8 scales
+      const uint32_t hw[2] = {sd.z, sd.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const __half2 dl = __float2half2_rn(__fmul_rn(d, (float)(int8_t)((scs >> (8 * u)) & 0xFF)));
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const int g = 4 * u + s;
+          const uint32_t x = ((w[u] >> (2 * s)) & 0x03030303u) | h_bits<2>(hw[g >> 3], g & 7);
+          uint32_t a0, a1;
+          u8x4_to_f16x4(x, 0x64046404u, a0, a1);  // fp16 1028 = 1024 + 4
+          out[8 * u + 2 * s + 0] = hmul2_u32(a0, dl);
+          out[8 * u + 2 * s + 1] = hmul2_u32(a1, dl);
+        }
+      }
+    } else {
+      const uint2 sd = *reinterpret_cast<const uint2*>(Base::side(st, r));
+      const float d = __fmul_rn(half_bits_to_float(sd.x), rscale);
+      const float dmin = __fmul_rn(half_bits_to_float(sd.x >> 16), rscale);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t sc = (sd.y >> (8 * u)) & 0xFF;
+        const __half2 dl = __float2half2_rn(__fmul_rn(d, (float)(sc & 0xF)));
+        const __half2 ml = __float2half2_rn(-__fmul_rn(dmin, (float)(sc >> 4)));
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const uint32_t x = (w[u] >> (2 * s)) & 0x03030303u;
+          const uint32_t a = prmt(x, 0x64646464u, 0x5140u), b = prmt(x, 0x64646464u, 0x7362u);
+          out[8 * u + 2 * s + 0] = hfma2_u32(hsub2_u32(a, kMagic), dl, ml);
+          out[8 * u + 2 * s + 1] = hfma2_u32(hsub2_u32(b, kMagic), dl, ml);
+        }
+      }
+    }
+  }
+};
+
+// Q5_K: Q4_K with a fifth bit per value (gguf/quants.py:526-549).  The 5-bit code is assembled
+// under the magic byte (the high nibble shifted down, the H bit ORed in at bit 4), then one fp16
+// fma with the fp16-rounded d*sc*2^-e and -dmin*m*2^-e, as for Q4_K.
+struct DecQ5_K : PlaneStage<2, 16> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint4 sd = *reinterpret_cast<const uint4*>(side(st, r));
+    const float d = __fmul_rn(half_bits_to_float(sd.x), rscale), dmin = __fmul_rn(half_bits_to_float(sd.x >> 16), rscale);
+    const __half2 ds0 = __float2half2_rn(__fmul_rn(d, (float)(sd.y & 0xFF)));
+    const __half2 ds1 = __float2half2_rn(__fmul_rn(d, (float)((sd.y >> 8) & 0xFF)));
+    const __half2 dm0 = __float2half2_rn(-__fmul_rn(dmin, (float)((sd.y >> 16) & 0xFF)));
+    const __half2 dm1 = __float2half2_rn(-__fmul_rn(dmin, (float)(sd.y >> 24)));
+    constexpr uint32_t kMagic = 0x64006400u;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 v = chunk(st, j, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t qlo = (w[t] & 0x0F0F0F0Fu) | h_bits<4>(sd.z, 4 * j + t);         // values 16j+4t..
+        const uint32_t qhi = ((w[t] >> 4) & 0x0F0F0F0Fu) | h_bits<4>(sd.w, 4 * j + t);  // 32+16j+4t..
+        const uint32_t a = prmt(qlo, 0x64646464u, 0x5140u), b = prmt(qlo, 0x64646464u, 0x7362u);
+        const uint32_t c = prmt(qhi, 0x64646464u, 0x5140u), e = prmt(qhi, 0x64646464u, 0x7362u);
+        out[8 * j + 2 * t + 0] = hfma2_u32(hsub2_u32(a, kMagic), ds0, dm0);
+        out[8 * j + 2 * t + 1] = hfma2_u32(hsub2_u32(b, kMagic), ds0, dm0);
+        out[16 + 8 * j + 2 * t + 0] = hfma2_u32(hsub2_u32(c, kMagic), ds1, dm1);
+        out[16 + 8 * j + 2 * t + 1] = hfma2_u32(hsub2_u32(e, kMagic), ds1, dm1);
+      }
+    }
+  }
+};
+
+// IQ4_XS: two IQ4_NL runs of 32 per stage with sub-block scales d*(sc-32) (gguf/quants.py:
+// 1352-1377).  The level is exact in fp16; d*sc*2^-e is formed in fp32 and rounded once to fp16,
+// then one fp16 multiply.
+struct DecIQ4_XS : PlaneStage<2, 4> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint32_t sd = *reinterpret_cast<const uint32_t*>(side(st, r));
+    const float d = __fmul_rn(half_bits_to_float(sd), rscale);
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const __half2 dl = __float2half2_rn(__fmul_rn(d, (float)(int8_t)((sd >> (16 + 8 * blk)) & 0xFF)));
+      const uint4 v = chunk(st, blk, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        uint32_t a0, a1, b0, b1;
+        s8x4_to_f16x4(DecQ4Block<true>::nl_levels(w[t] & 0x0F0F0F0Fu), a0, a1);
+        s8x4_to_f16x4(DecQ4Block<true>::nl_levels((w[t] >> 4) & 0x0F0F0F0Fu), b0, b1);
+        out[16 * blk + 2 * t + 0] = hmul2_u32(a0, dl);
+        out[16 * blk + 2 * t + 1] = hmul2_u32(a1, dl);
+        out[16 * blk + 8 + 2 * t + 0] = hmul2_u32(b0, dl);
+        out[16 * blk + 8 + 2 * t + 1] = hmul2_u32(b1, dl);
       }
     }
   }

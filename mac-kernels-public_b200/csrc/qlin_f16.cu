@@ -8,8 +8,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "qlin_gemm.cuh"
-#include "qlin_internal.h"
+#include "qlin_f16_launch.cuh"
 
 namespace qlin {
 
@@ -148,8 +147,15 @@ uint32_t gguf_stage_bytes(int qtype, int* P, int* S) {
   switch (qtype) {
     case WF_Q8_0: p = 4; s = 4; break;
     case WF_Q4_0:
-    case WF_IQ4_NL: p = 2; s = 4; break;
+    case WF_IQ4_NL:
+    case WF_IQ4_XS: p = 2; s = 4; break;
+    case WF_Q4_1:
     case WF_Q4_K: p = 2; s = 8; break;
+    case WF_Q5_0: p = 2; s = 12; break;
+    case WF_Q5_1:
+    case WF_Q5_K: p = 2; s = 16; break;
+    case WF_Q2_K: p = 1; s = 8; break;
+    case WF_Q3_K: p = 1; s = 16; break;
     case WF_Q6_K: p = 3; s = 8; break;
     default: return 0;
   }
@@ -160,18 +166,25 @@ uint32_t gguf_stage_bytes(int qtype, int* P, int* S) {
 
 int gguf_block_values(int qtype) {
   switch (qtype) {
-    case WF_Q8_0: case WF_Q4_0: case WF_IQ4_NL: return 32;
-    case WF_Q4_K: case WF_Q6_K: return 256;
+    case WF_Q4_0: case WF_Q4_1: case WF_Q5_0: case WF_Q5_1: case WF_Q8_0: case WF_IQ4_NL: return 32;
+    case WF_Q2_K: case WF_Q3_K: case WF_Q4_K: case WF_Q5_K: case WF_Q6_K: case WF_IQ4_XS: return 256;
     default: return 0;
   }
 }
 
 int gguf_type_size(int qtype) {
   switch (qtype) {
-    case WF_Q8_0: return 34;
     case WF_Q4_0: case WF_IQ4_NL: return 18;
+    case WF_Q4_1: return 20;
+    case WF_Q5_0: return 22;
+    case WF_Q5_1: return 24;
+    case WF_Q8_0: return 34;
+    case WF_Q2_K: return 84;
+    case WF_Q3_K: return 110;
     case WF_Q4_K: return 144;
+    case WF_Q5_K: return 176;
     case WF_Q6_K: return 210;
+    case WF_IQ4_XS: return 136;
     default: return 0;
   }
 }
@@ -186,6 +199,18 @@ static bool use_pair(int tm, int n_tiles) {
   return enabled && tm >= 128 && n_tiles % 2 == 0;
 }
 
+// Relative decode cost of a 64-deep stage per format (the 4-bit formats are the unit; Q6_K was
+// measured ~12% slower, the formats that insert a fifth / third bit or scale 16-value groups are
+// between the two).
+static double fmt_stage_cost(int fmt) {
+  switch (fmt) {
+    case WF_Q6_K: return 1.12;
+    case WF_Q5_0: case WF_Q5_1: case WF_Q5_K: case WF_Q3_K: return 1.06;
+    case WF_Q2_K: return 1.03;
+    default: return 1.0;
+  }
+}
+
 // Modelled time of one plan (microseconds at the boost clock), from measured per-stage costs of
 // the persistent kernel on B200: a 64-deep K stage of one tile costs c(TM), the 256-token tile
 // (single-buffered accumulator) adds an exposed epilogue per tile, Q6_K decodes ~12% slower, and
@@ -198,7 +223,7 @@ static double plan_cost(int M, int N, int kst, int fmt, int tm, int splits, int 
   const long long waves = (units + slots - 1) / slots;
   double c = tm <= 64 ? 0.30 : tm == 128 ? 0.33 : tm == 192 ? 0.38 : 0.45;
   if (!pair) c *= 1.03;
-  if (fmt == WF_Q6_K) c *= 1.12;
+  c *= fmt_stage_cost(fmt);
   const double epi = tm == 256 ? 6.0 : 0.0;
   const int per = (kst + splits - 1) / splits;
   double t = (double)waves * (per * c + epi);
@@ -278,76 +303,6 @@ size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits
   return k_splits > 1 ? (size_t)k_splits * N * mp * sizeof(float) : 0;
 }
 
-template <class Dec, int TM, int STAGES, bool PAIR>
-static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
-                      const PeerMaps& maps,
-                      const GemmParams& p, cudaStream_t stream) {
-  constexpr int smem = qgemm_f16_smem_bytes<Dec, TM, STAGES, PAIR>();
-  static_assert(smem <= 232448, "shared memory per CTA");
-  auto kern = qgemm_f16_kernel<Dec, TM, STAGES, PAIR>;
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
-      set_error("cudaFuncSetAttribute(max dynamic smem %d) failed", smem);
-      return 3;
-    }
-    attr_done[dev] = true;
-  }
-  constexpr int kCtas = PAIR ? 2 : 1;
-  const int tiles = p.m_tiles * (p.n_tiles / kCtas) * p.k_splits;
-  const int grid = kCtas * std::min(tiles, sm_count() / kCtas);
-  cudaError_t e;
-  if constexpr (PAIR) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(F16Cfg<TM, STAGES, PAIR>::kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, tx, tw, tp, tt, maps, p);
-  } else {
-    kern<<<grid, F16Cfg<TM, STAGES, PAIR>::kThreads, smem, stream>>>(tx, tw, tp, tt, maps, p);
-    e = cudaGetLastError();
-  }
-  if (e != cudaSuccess) {
-    set_error("qgemm_f16 launch failed: %s", cudaGetErrorString(e));
-    return 3;
-  }
-  return 0;
-}
-
-template <class Dec, int TM>
-static int launch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
-                      const PeerMaps& maps,
-                     const GemmParams& p, bool pair, cudaStream_t stream) {
-  if constexpr (TM >= 128) {
-    if (pair) return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, true>(), true>(tx, tw, tp, tt, maps, p, stream);
-  }
-  return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, false>(), false>(tx, tw, tp, tt, maps, p, stream);
-}
-
-template <class Dec>
-static int dispatch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
-                      const PeerMaps& maps,
-                       const GemmParams& p, int tm, bool pair, cudaStream_t stream) {
-  switch (tm) {
-    case 16: return launch_tm<Dec, 16>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 32: return launch_tm<Dec, 32>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 64: return launch_tm<Dec, 64>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 128: return launch_tm<Dec, 128>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 192: return launch_tm<Dec, 192>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 256: return launch_tm<Dec, 256>(tx, tw, tp, tt, maps, p, pair, stream);
-    default: set_error("unsupported token tile %d", tm); return 2;
-  }
-}
 
 
 // Whole 16-byte pieces of 2-byte output rows can be stored from the shared-memory staging tile.
@@ -457,9 +412,13 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
     case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
-    case WF_Q4_K: rc = dispatch_tm<DecQ4_K>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
-    case WF_Q6_K: rc = dispatch_tm<DecQ6_K>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
-    default: set_error("unknown weight format %d", a.fmt); return 2;
+    default:
+      rc = dispatch_f16_blk(a.fmt, tx, tw, tp, tt, maps, p, tm, pair, stream);
+      if (rc < 0) rc = dispatch_f16_kq(a.fmt, tx, tw, tp, tt, maps, p, tm, pair, stream);
+      if (rc < 0) {
+        set_error("unsupported weight format %d", a.fmt);
+        rc = 2;
+      }
   }
   if (rc) return rc;
   if (splits > 1) {

@@ -32,7 +32,10 @@ void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* co
                          int K, int8_t* out, cudaStream_t s);
 
 // Weight formats of the f16 (weight-only) GEMM family.
-enum WFormat : int { WF_INT8 = 0, WF_Q8_0 = 8, WF_Q4_0 = 2, WF_Q4_K = 12, WF_Q6_K = 14, WF_IQ4_NL = 20 };
+enum WFormat : int {
+  WF_INT8 = 0, WF_Q4_0 = 2, WF_Q4_1 = 3, WF_Q5_0 = 6, WF_Q5_1 = 7, WF_Q8_0 = 8, WF_Q2_K = 10, WF_Q3_K = 11,
+  WF_Q4_K = 12, WF_Q5_K = 13, WF_Q6_K = 14, WF_IQ4_NL = 20, WF_IQ4_XS = 23
+};
 
 struct F16GemmArgs {
   int fmt;

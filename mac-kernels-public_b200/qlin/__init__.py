@@ -26,8 +26,9 @@ __all__ = ["int8_linear", "int8_linear_streamed", "gguf_linear", "gguf_linear_sl
            "device_status"]
 
 # ggml type id -> (name, values per block, bytes per block)
-GGUF_TYPES = {2: ("Q4_0", 32, 18), 8: ("Q8_0", 32, 34), 12: ("Q4_K", 256, 144), 14: ("Q6_K", 256, 210),
-              20: ("IQ4_NL", 32, 18)}
+GGUF_TYPES = {2: ("Q4_0", 32, 18), 3: ("Q4_1", 32, 20), 6: ("Q5_0", 32, 22), 7: ("Q5_1", 32, 24),
+              8: ("Q8_0", 32, 34), 10: ("Q2_K", 256, 84), 11: ("Q3_K", 256, 110), 12: ("Q4_K", 256, 144),
+              13: ("Q5_K", 256, 176), 14: ("Q6_K", 256, 210), 20: ("IQ4_NL", 32, 18), 23: ("IQ4_XS", 256, 136)}
 GGUF_IDS = {v[0]: k for k, v in GGUF_TYPES.items()}
 _DT = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.int8: 3, torch.uint8: 4, torch.int32: 5,
        torch.float8_e4m3fn: 6}

@@ -7,9 +7,11 @@ its pinned third-party decoder (`gguf` 0.19.0, `gguf/quants.py`) define for:
     (reference `modal/weight_error_app.py:90-127`, a port of comfy-kitchen's eager quantizers);
   * the comfy-kitchen W4A8/W6A8 ("AsymW4A8Int8Layout") pack/unpack and int8-grid decode
     (`modal/weight_error_app.py:145-166, 326-339`);
-  * GGUF block decode for Q4_0, Q8_0, Q4_K, Q6_K, IQ4_NL (formula table
-    `docs/research/2026-10-03-gguf-on-metal.md:18-37`; third-party algorithm `gguf` 0.19.0
-    `gguf/quants.py` Q4_0 :220, Q8_0 :378, Q4_K :475, Q6_K :552, IQ4_NL :1330);
+  * GGUF block decode for the twelve types the reference's kernel covers: Q4_0, Q4_1, Q5_0, Q5_1,
+    Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_NL, IQ4_XS (formula table
+    `docs/research/2026-10-03-gguf-on-metal.md:18-37`, type list `:59`; third-party algorithm
+    `gguf` 0.19.0 `gguf/quants.py` Q4_0 :220, Q4_1 :275, Q5_0 :313, Q5_1 :356, Q8_0 :378,
+    Q2_K :405, Q3_K :432, Q4_K :475, Q5_K :526, Q6_K :552, IQ4_NL :1330, IQ4_XS :1352);
   * the simplified synthetic layouts the benchmark configurations use (uniform 4-bit group-128
     and 6-bit "four values per three bytes" group-64 weights with fp16 group scales, and the
     Sylvester Hadamard of size 128).  These have no counterpart in the reference; their
@@ -288,10 +290,17 @@ def int_group_partials(xq: np.ndarray, wq: np.ndarray, group: int) -> np.ndarray
 # type id -> (name, values per block, bytes per block); ids are enum ggml_type.
 GGUF_TYPES = {
     2: ("Q4_0", 32, 18),
+    3: ("Q4_1", 32, 20),
+    6: ("Q5_0", 32, 22),
+    7: ("Q5_1", 32, 24),
     8: ("Q8_0", 32, 34),
+    10: ("Q2_K", 256, 84),
+    11: ("Q3_K", 256, 110),
     12: ("Q4_K", 256, 144),
+    13: ("Q5_K", 256, 176),
     14: ("Q6_K", 256, 210),
     20: ("IQ4_NL", 32, 18),
+    23: ("IQ4_XS", 256, 136),
 }
 GGUF_IDS = {v[0]: k for k, v in GGUF_TYPES.items()}
 IQ4_NL_VALUES = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113],
@@ -313,11 +322,106 @@ def q4k_scale_min(scales12: np.ndarray):
     return sc.astype(np.float32), mn.astype(np.float32)
 
 
+def _nibbles32(qs16: np.ndarray) -> np.ndarray:
+    """[nb, 16] bytes -> [nb, 32] codes of a 32-value run: byte i holds value i in its low nibble
+    and value i + 16 in its high nibble (`gguf/quants.py:285-286`)."""
+    return np.concatenate([qs16 & 0xF, qs16 >> 4], axis=1)
+
+
+def _bits32(qh4: np.ndarray) -> np.ndarray:
+    """[nb, 4] bytes of a little-endian uint32 -> [nb, 32], element i = bit i (`gguf/quants.py:323-325`)."""
+    w = np.ascontiguousarray(qh4).view("<u4").astype(np.uint32)
+    return ((w >> np.arange(32, dtype=np.uint32)) & 1).astype(np.uint8)
+
+
+def _crumbs256(qs64: np.ndarray) -> np.ndarray:
+    """[nb, 64] bytes -> [nb, 256] 2-bit codes: value j of a 256-superblock sits in byte
+    32*(j // 128) + j % 32 at bits 2*((j % 128) // 32) (`gguf/quants.py:422-424`)."""
+    q = qs64.reshape(-1, 2, 1, 32)
+    return np.concatenate([(q >> s) & 3 for s in (0, 2, 4, 6)], axis=2).reshape(-1, 256)
+
+
+def q3k_scales(scales12: np.ndarray) -> np.ndarray:
+    """Sixteen signed 6-bit Q3_K scales (`gguf/quants.py:456-463`): low nibble of byte i (i < 8) or
+    high nibble of byte i - 8, plus bits 2*(i // 4) of byte 8 + i % 4 as bits 4-5, minus 32."""
+    s = scales12.astype(np.uint8).reshape(-1, 12)
+    lo = np.concatenate([s[:, 0:8] & 0xF, s[:, 0:8] >> 4], axis=1)
+    hi = np.concatenate([(s[:, 8:12] >> (2 * t)) & 3 for t in range(4)], axis=1)
+    return ((lo | (hi << 4)).astype(np.int16) - 32).astype(np.float32)
+
+
+def iq4xs_scales(block: np.ndarray) -> np.ndarray:
+    """Eight signed 6-bit IQ4_XS sub-block scales (`gguf/quants.py:1363-1369`): nibble i % 2 of
+    scales_l[i // 2] plus bits 2i..2i+1 of the uint16 scales_h as bits 4-5, minus 32."""
+    b = block.astype(np.uint8).reshape(-1, block.shape[-1])
+    sh = b[:, 2].astype(np.uint32) | (b[:, 3].astype(np.uint32) << 8)
+    sl = b[:, 4:8]
+    lo = np.stack([sl & 0xF, sl >> 4], axis=2).reshape(-1, 8).astype(np.uint32)
+    hi = (sh[:, None] >> (2 * np.arange(8, dtype=np.uint32))) & 3
+    return ((lo | (hi << 4)).astype(np.int16) - 32).astype(np.float32)
+
+
 def gguf_dequantize_blocks(blocks: np.ndarray, qtype: int) -> np.ndarray:
-    """uint8 blocks [nb, type_size] -> float32 [nb, block_values], bit-exact with gguf 0.19.0."""
+    """uint8 blocks [nb, type_size] -> float32 [nb, block_values], bit-exact with gguf 0.19.0.
+
+    Every product and sum below is one numpy float32 operation in the order gguf-py evaluates it
+    (no fused multiply-add), so the roundings are the same."""
     name, qk, ts = GGUF_TYPES[qtype]
     b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, ts)
     nb = b.shape[0]
+    if name in ("Q4_1", "Q5_0", "Q5_1"):
+        # Q4_1 d, m, qs[16] (`gguf/quants.py:275-288`); Q5_0 d, qh u32, qs[16] (:313-330);
+        # Q5_1 d, m, qh u32, qs[16] (:356-375).  w = d*q (+ m), Q5_0 with q - 16.
+        d = _f16(b[:, 0:2])
+        has_m = name != "Q5_0"
+        m = _f16(b[:, 2:4]) if has_m else None
+        qs_off = {"Q4_1": 4, "Q5_0": 6, "Q5_1": 8}[name]
+        q = _nibbles32(b[:, qs_off:qs_off + 16])
+        if name != "Q4_1":
+            q = q | (_bits32(b[:, qs_off - 4:qs_off]) << 4)
+        if name == "Q5_0":
+            return d * (q.astype(np.int8) - np.int8(16)).astype(np.float32)
+        return d * q.astype(np.float32) + m
+    if name == "Q2_K":
+        # scales[16], qs[64], d, dmin (`gguf/quants.py:405-428`): w = (d*(sc & 15))*q - dmin*(sc >> 4)
+        sc = b[:, 0:16]
+        d = _f16(b[:, 80:82])
+        dmin = _f16(b[:, 82:84])
+        dl = (d * (sc & 0xF).astype(np.float32)).reshape(nb, 16, 1)
+        ml = (dmin * (sc >> 4).astype(np.float32)).reshape(nb, 16, 1)
+        q = _crumbs256(b[:, 16:80]).reshape(nb, 16, 16).astype(np.float32)
+        return (dl * q - ml).reshape(nb, 256)
+    if name == "Q3_K":
+        # hmask[32], qs[64], scales[12], d (`gguf/quants.py:432-472`): w = (d*sc)*q with
+        # q = crumb - 4 where the hmask bit (bit j // 32 of hmask[j % 32]) is clear.
+        d = _f16(b[:, 108:110])
+        dl = (d * q3k_scales(b[:, 96:108])).reshape(nb, 16, 1)
+        lo = _crumbs256(b[:, 32:96])
+        hm = b[:, 0:32].reshape(nb, 1, 32)
+        hbit = np.concatenate([(hm >> i) & 1 for i in range(8)], axis=1).reshape(nb, 256)
+        q = (lo.astype(np.int8) - ((hbit ^ 1) << 2).astype(np.int8)).reshape(nb, 16, 16).astype(np.float32)
+        return (dl * q).reshape(nb, 256)
+    if name == "Q5_K":
+        # d, dmin, scales[12], qh[32], qs[128] (`gguf/quants.py:526-549`): Q4_K plus a fifth bit,
+        # bit s of qh[l] for value l of sub-block s.
+        d = _f16(b[:, 0:2])
+        dmin = _f16(b[:, 2:4])
+        sc, mn = q4k_scale_min(b[:, 4:16])
+        ds = (d * sc).reshape(nb, 8, 1)
+        dm = (dmin * mn).reshape(nb, 8, 1)
+        qs = b[:, 48:176].reshape(nb, 4, 1, 32)
+        lo = np.concatenate([qs & 0xF, qs >> 4], axis=2).reshape(nb, 8, 32)
+        qh = b[:, 16:48].reshape(nb, 1, 32)
+        hi = np.concatenate([(qh >> s) & 1 for s in range(8)], axis=1)
+        q = (lo | (hi << 4)).astype(np.float32)
+        return (ds * q - dm).reshape(nb, 256)
+    if name == "IQ4_XS":
+        # d, scales_h u16, scales_l[4], qs[128] (`gguf/quants.py:1352-1377`): sub-block i is an
+        # IQ4_NL run of 32 with scale d*sc_i.
+        d = _f16(b[:, 0:2])
+        dl = (d * iq4xs_scales(b)).reshape(nb, 8, 1)
+        nib = _nibbles32(b[:, 8:136].reshape(nb * 8, 16)).reshape(nb, 8, 32)
+        return (dl * IQ4_NL_VALUES[nib]).reshape(nb, 256)
     if name in ("Q4_0", "IQ4_NL"):
         d = _f16(b[:, 0:2])
         qs = b[:, 2:18]
@@ -368,8 +472,32 @@ def gguf_row_bound(raw: np.ndarray, qtype: int, n: int, k: int) -> np.ndarray:
     if k % qk:
         raise ValueError("row bound needs whole blocks per row")
     b = np.asarray(raw, dtype=np.uint8).reshape(n, k // qk, ts)
+    def f16abs(off):
+        return np.abs(_f16(b[..., off:off + 2])[..., 0].astype(np.float64))
+
     if name == "Q4_0":
         bound = np.abs(_f16(b[..., 0:2])[..., 0].astype(np.float64)) * 8
+    elif name == "Q4_1":
+        bound = f16abs(0) * 15 + f16abs(2)
+    elif name == "Q5_0":
+        bound = f16abs(0) * 16
+    elif name == "Q5_1":
+        bound = f16abs(0) * 31 + f16abs(2)
+    elif name == "Q2_K":
+        sc = b[..., 0:16]
+        bound = (f16abs(80)[..., None] * (sc & 0xF).astype(np.float64) * 3
+                 + f16abs(82)[..., None] * (sc >> 4).astype(np.float64)).max(axis=-1)
+    elif name == "Q3_K":
+        sc = np.abs(q3k_scales(b[..., 96:108].reshape(-1, 12)).reshape(n, k // qk, 16).astype(np.float64))
+        bound = (f16abs(108)[..., None] * sc * 4).max(axis=-1)
+    elif name == "Q5_K":
+        sc, mn = q4k_scale_min(b[..., 4:16].reshape(-1, 12))
+        sc = sc.reshape(n, k // qk, 8).astype(np.float64)
+        mn = mn.reshape(n, k // qk, 8).astype(np.float64)
+        bound = (f16abs(0)[..., None] * sc * 31 + f16abs(2)[..., None] * mn).max(axis=-1)
+    elif name == "IQ4_XS":
+        sc = np.abs(iq4xs_scales(b.reshape(-1, ts)).reshape(n, k // qk, 8).astype(np.float64))
+        bound = (f16abs(0)[..., None] * sc * 127).max(axis=-1)
     elif name == "Q8_0":
         bound = np.abs(_f16(b[..., 0:2])[..., 0].astype(np.float64)) * 128
     elif name == "IQ4_NL":
@@ -416,9 +544,7 @@ def random_gguf_blocks(qtype: int, n: int, k: int, seed: int = 0, scale: float |
     |N(0, scale)|-sized values, the way the reference's GGUF bench builds them
     (`bench/bench_gguf_linear.py:35-40,69-78`).  Returns uint8 [n, k/QK*type_size]."""
     name, qk, ts = GGUF_TYPES[qtype]
-    fields = {"Q4_0": ([0], 5e-3), "Q8_0": ([0], 3e-4), "Q4_K": ([0, 2], 5e-5),
-              "Q6_K": ([208], 3e-5), "IQ4_NL": ([0], 3e-4)}
-    offs, mag = fields[name]
+    offs, mag = GGUF_SCALE_FIELDS[name]
     if scale is not None:
         mag = scale
     rng = np.random.default_rng(seed)
@@ -426,7 +552,17 @@ def random_gguf_blocks(qtype: int, n: int, k: int, seed: int = 0, scale: float |
     raw = rng.integers(0, 256, size=(nb, ts), dtype=np.uint8)
     for off in offs:
         raw[:, off:off + 2] = np.abs(rng.standard_normal(nb) * mag + mag).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    if name in ("Q4_1", "Q5_1"):  # the block minimum m is signed (negative for most real blocks)
+        m = -np.abs(rng.standard_normal(nb) * 8 * mag).astype(np.float16)
+        raw[:, 2:4] = m.view(np.uint8).reshape(nb, 2)
     return raw.reshape(n, (k // qk) * ts)
+
+
+# name -> (byte offsets of the fp16 block scales that `random_gguf_blocks` overwrites, magnitude)
+GGUF_SCALE_FIELDS = {"Q4_0": ([0], 5e-3), "Q4_1": ([0], 1.5e-3), "Q5_0": ([0], 1.5e-3), "Q5_1": ([0], 7e-4),
+                     "Q8_0": ([0], 3e-4), "Q2_K": ([80, 82], 4e-4), "Q3_K": ([108], 2e-4),
+                     "Q4_K": ([0, 2], 5e-5), "Q5_K": ([0, 2], 3e-5), "Q6_K": ([208], 3e-5),
+                     "IQ4_NL": ([0], 3e-4), "IQ4_XS": ([0], 1e-5)}
 
 
 def baseline_gguf_blocks(qtype: int, n: int, k: int, seed: int = 0) -> np.ndarray:

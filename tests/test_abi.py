@@ -31,10 +31,19 @@ def test_version_and_host_side_declines_without_gpu():
     size = ctypes.c_size_t(0)
     npad = ctypes.c_int64(0)
     # unsupported GGUF type and a K that is not whole blocks decline on the host
-    assert lib.qlin_gguf_repacked_bytes(3, 10, 256, ctypes.byref(size), ctypes.byref(npad)) == 1
+    for unsupported in (9, 15, 16, 21):  # Q8_1, Q8_K, IQ2_XXS, IQ3_S
+        assert lib.qlin_gguf_repacked_bytes(unsupported, 10, 256, ctypes.byref(size), ctypes.byref(npad)) == 1
     assert lib.qlin_gguf_repacked_bytes(12, 10, 300, ctypes.byref(size), ctypes.byref(npad)) == 1
     assert lib.qlin_gguf_repacked_bytes(12, 130, 512, ctypes.byref(size), ctypes.byref(npad)) == 0
     assert npad.value == 256 and size.value == 2 * 8 * 128 * 40
+    # every supported type: bytes per 64-value stage of a 128-row tile (16 B planes + side record)
+    stage = {2: 36, 3: 40, 6: 44, 7: 48, 8: 68, 10: 24, 11: 32, 12: 40, 13: 48, 14: 56, 20: 36, 23: 36}
+    for qtype, per_row in stage.items():
+        qk = 256 if qtype in (10, 11, 12, 13, 14, 23) else 32
+        assert lib.qlin_gguf_repacked_bytes(qtype, 10, 4 * qk, ctypes.byref(size), ctypes.byref(npad)) == 0
+        assert size.value == (4 * qk // 64) * 128 * per_row, qtype
+    assert lib.qlin_gguf_repacked_bytes(3, 10, 96, ctypes.byref(size), ctypes.byref(npad)) == 0  # 3 blocks
+    assert size.value == 2 * 128 * 40
     assert b"block" in lib.qlin_last_error() or lib.qlin_last_error() == b""
     # workspace queries are pure host arithmetic
     assert lib.qlin_int8_linear_workspace(4096, 12288, 3072) >= 4096 * 3072 * 2

@@ -79,7 +79,7 @@ def test_lora_factors_follow_patch_kinds():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+@pytest.mark.parametrize("qtype", sorted(O.GGUF_TYPES))
 @pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 8e-3), (torch.float16, 3e-3)])
 def test_fast_path_matches_stock(qtype, dtype, tol):
     from qlin import gguf_fast

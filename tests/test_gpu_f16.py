@@ -24,14 +24,17 @@ def _check_status(qlin):
     assert code == 0, f"a kernel timed out waiting (where={where:#x})"
 
 
-@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+ALL_TYPES = sorted(O.GGUF_TYPES)
+
+
+@pytest.mark.parametrize("qtype", ALL_TYPES)
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
 def test_gguf_dequantize_bit_exact(qlin, qtype, out_dtype):
     name, qk, ts = O.GGUF_TYPES[qtype]
     raw = O.random_gguf_blocks(qtype, 40, 768 if qk == 256 else 544, seed=qtype)
     n, k = 40, (768 if qk == 256 else 544)
     flat = raw.reshape(-1, ts)
-    offs = {"Q4_0": [0], "Q8_0": [0], "IQ4_NL": [0], "Q4_K": [0, 2], "Q6_K": [208]}[name]
+    offs = O.GGUF_SCALE_FIELDS[name][0]
     for i, v in enumerate([0.0, 65504.0, -65504.0, 2.0 ** -24, -(2.0 ** -20), 6.1e-5]):
         for off in offs:
             flat[i, off:off + 2] = np.array([v], dtype=np.float16).view(np.uint8)
@@ -45,14 +48,15 @@ def test_gguf_dequantize_bit_exact(qlin, qtype, out_dtype):
     _check_status(qlin)
 
 
-def test_gguf_dequantize_rows_straddling_blocks(qlin):
-    raw = O.random_gguf_blocks(12, 3, 1024, seed=5)  # 12 superblocks
-    ref = O.gguf_dequantize(raw, 12, 6, 512)
-    got = qlin.dequantize_gguf(torch.from_numpy(raw).cuda(), 12, (6, 512), torch.float32).cpu().numpy()
+@pytest.mark.parametrize("qtype", [11, 12, 13, 23])
+def test_gguf_dequantize_rows_straddling_blocks(qlin, qtype):
+    raw = O.random_gguf_blocks(qtype, 3, 1024, seed=5)  # 12 superblocks
+    ref = O.gguf_dequantize(raw, qtype, 6, 512)
+    got = qlin.dequantize_gguf(torch.from_numpy(raw).cuda(), qtype, (6, 512), torch.float32).cpu().numpy()
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+@pytest.mark.parametrize("qtype", ALL_TYPES)
 def test_gguf_repack_row_exponents(qlin, qtype):
     n, k = 200, 1024
     raw = O.random_gguf_blocks(qtype, n, k, seed=11 + qtype)
@@ -74,7 +78,7 @@ def _gguf_case(qtype, m, n, k, seed, x_dtype=torch.float16, bias=True, scale=Non
     return x, raw, b, ref
 
 
-@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+@pytest.mark.parametrize("qtype", ALL_TYPES)
 @pytest.mark.parametrize("m", [1, 7, 16, 33, 130, 300])
 def test_gguf_linear_matches_fp64(qlin, qtype, m):
     n, k = 384, 1024
@@ -87,12 +91,12 @@ def test_gguf_linear_matches_fp64(qlin, qtype, m):
     _check_status(qlin)
 
 
-@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+@pytest.mark.parametrize("qtype", ALL_TYPES)
 @pytest.mark.parametrize("m", [600, 1000])
 def test_gguf_linear_cta_pairs_match_fp64(qlin, qtype, m):
     """Token tiles of 192 / 256 over an even number of 128-row weight tiles: the two-CTA
     (cta_group::2) kernels, several tiles per CTA pair, a ragged last token tile."""
-    n, k = 512, 768 if qtype in (12, 14) else 640
+    n, k = 512, 768 if O.GGUF_TYPES[qtype][1] == 256 else 640
     x, raw, b, ref = _gguf_case(qtype, m, n, k, seed=m + qtype)
     y = qlin.gguf_linear(x.cuda(), torch.from_numpy(raw).cuda(), qtype, (n, k), bias=b.cuda())
     got = y.float().cpu().numpy()
@@ -101,11 +105,11 @@ def test_gguf_linear_cta_pairs_match_fp64(qlin, qtype, m):
     _check_status(qlin)
 
 
-@pytest.mark.parametrize("qtype", [8, 12])
+@pytest.mark.parametrize("qtype", [8, 12, 3, 7, 13, 23])
 @pytest.mark.parametrize("x_dtype,out_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float32),
                                                (torch.float32, torch.float16)])
 def test_gguf_linear_dtypes_and_ragged_n(qlin, qtype, x_dtype, out_dtype):
-    m, n, k = 45, 200, 768 if qtype == 12 else 800
+    m, n, k = 45, 200, 768 if O.GGUF_TYPES[qtype][1] == 256 else 800
     x, raw, b, ref = _gguf_case(qtype, m, n, k, seed=7, x_dtype=x_dtype)
     y = qlin.gguf_linear(x.cuda(), torch.from_numpy(raw).cuda(), qtype, (n, k), bias=b.cuda(), out_dtype=out_dtype)
     assert y.dtype == out_dtype

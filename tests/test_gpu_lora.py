@@ -47,7 +47,7 @@ def test_int8_linear_fused_lora(qlin, m, n, rank, dtype):
     assert code == 0, where
 
 
-@pytest.mark.parametrize("qtype", [8, 12, 14])
+@pytest.mark.parametrize("qtype", [8, 12, 14, 3, 13, 11])
 @pytest.mark.parametrize("m", [20, 700])
 def test_gguf_linear_fused_lora(qlin, qtype, m):
     n, k, rank = 512, 768, 64

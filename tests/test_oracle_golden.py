@@ -66,7 +66,21 @@ def test_gguf_decode_matches_golden_ggml_vectors(case, fmt, qtype):
     assert sha(w) == f["deq"]
 
 
-@pytest.mark.parametrize("qtype", [2, 8, 12, 14, 20])
+ALL_TYPES = sorted(O.GGUF_TYPES)
+
+
+@pytest.mark.parametrize("qtype", ALL_TYPES)
+def test_gguf_decode_matches_committed_gguf_py_vectors(qtype):
+    """Bit-exact against gguf-py's own decode of the same blocks (tests/golden/gguf_types.npz,
+    made by tests/golden/make_gguf_types.py), edge scales included."""
+    name, qk, ts = O.GGUF_TYPES[qtype]
+    z = np.load(os.path.join(GOLD, "gguf_types.npz"))
+    raw, want = z[f"{name}__raw"], z[f"{name}__f32"]
+    got = O.gguf_dequantize(raw, qtype, *want.shape)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("qtype", ALL_TYPES)
 def test_gguf_decode_matches_gguf_py(qtype):
     gguf = pytest.importorskip("gguf")
     from gguf import quants
@@ -74,7 +88,7 @@ def test_gguf_decode_matches_gguf_py(qtype):
     # Extreme scales: zero, +-65504, subnormal, in the first blocks.
     name, qk, ts = O.GGUF_TYPES[qtype]
     flat = raw.reshape(-1, ts)
-    offs = {"Q4_0": [0], "Q8_0": [0], "IQ4_NL": [0], "Q4_K": [0, 2], "Q6_K": [208]}[name]
+    offs = O.GGUF_SCALE_FIELDS[name][0]
     for i, v in enumerate([0.0, 65504.0, -65504.0, 2.0 ** -24, -(2.0 ** -20)]):
         for off in offs:
             flat[i, off:off + 2] = np.array([v], dtype=np.float16).view(np.uint8)
@@ -84,12 +98,13 @@ def test_gguf_decode_matches_gguf_py(qtype):
     assert np.array_equal(got.view(np.uint32), want.astype(np.float32).view(np.uint32))
 
 
-def test_gguf_rows_straddling_blocks():
+@pytest.mark.parametrize("qtype", [12, 11, 23])
+def test_gguf_rows_straddling_blocks(qtype):
     gguf = pytest.importorskip("gguf")
     from gguf import quants
-    raw = O.random_gguf_blocks(12, 4, 768, seed=3)  # 12 superblocks
-    want = quants.dequantize(raw.reshape(-1), gguf.GGMLQuantizationType(12)).reshape(-1)
-    got = O.gguf_dequantize(raw, 12, 6, 512)  # 6 rows of 512: rows start mid-block
+    raw = O.random_gguf_blocks(qtype, 4, 768, seed=3)  # 12 superblocks
+    want = quants.dequantize(raw.reshape(-1), gguf.GGMLQuantizationType(qtype)).reshape(-1)
+    got = O.gguf_dequantize(raw, qtype, 6, 512)  # 6 rows of 512: rows start mid-block
     assert np.array_equal(got.reshape(-1), want)
 
 
@@ -150,7 +165,7 @@ def test_grouped_a8_reference_is_exact_on_integer_inputs():
 
 
 def test_row_exponent_bounds_decoded_rows():
-    for qtype in (2, 8, 12, 14, 20):
+    for qtype in ALL_TYPES:
         raw = O.random_gguf_blocks(qtype, 8, 512, seed=qtype + 10)
         w = O.gguf_dequantize(raw, qtype, 8, 512)
         bound = O.gguf_row_bound(raw, qtype, 8, 512)
