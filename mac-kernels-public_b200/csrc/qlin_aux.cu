@@ -620,6 +620,18 @@ __device__ __forceinline__ void put_u32(uint8_t* p, uint32_t v) {
   for (int i = 0; i < 4; ++i) p[i] = (uint8_t)(v >> (8 * i));
 }
 
+// A run of 32 IQ4 codes (ggml order: byte i holds value i in its low nibble, value i+16 in its
+// high nibble) -> 4 words in selector order: word t = codes of values 4t..4t+3 in bits 0-15 and
+// 16+4t..16+4t+3 in bits 16-31, value 4t+k in nibble k.
+__device__ __forceinline__ void iq4_selector_order(const uint8_t* qs, uint8_t* out) {
+  for (int t = 0; t < 4; ++t) {
+    uint32_t w = 0;
+    for (int k = 0; k < 4; ++k)
+      w |= ((uint32_t)(qs[4 * t + k] & 0xF) << (4 * k)) | ((uint32_t)(qs[4 * t + k] >> 4) << (16 + 4 * k));
+    put_u32(out + 4 * t, w);
+  }
+}
+
 // One-time repack of raw GGUF rows into the pipeline-stage layout documented in qlin_decode.cuh.
 // grid = (num_k_stages, n_tiles), block = 128 (one thread per weight row of the tile).
 __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, int N, int K, int num_k_stages,
@@ -644,14 +656,18 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
         const uint8_t* b = row + (long long)kb * ts;
         switch (qtype) {
           case GGUF_Q8_0:
-          case GGUF_Q4_0:
-          case GGUF_IQ4_NL: {
+          case GGUF_Q4_0: {
             const int qsb = ts - 2;
             side[2 * blk] = b[0];
             side[2 * blk + 1] = b[1];
             for (int i = 0; i < qsb; ++i) payload[blk * qsb + i] = b[2 + i];
             break;
           }
+          case GGUF_IQ4_NL:
+            side[2 * blk] = b[0];
+            side[2 * blk + 1] = b[1];
+            iq4_selector_order(b + 2, payload + 16 * blk);
+            break;
           case GGUF_Q4_1:
             for (int i = 0; i < 4; ++i) side[4 * blk + i] = b[i];  // d, m
             for (int i = 0; i < 16; ++i) payload[16 * blk + i] = b[4 + i];
@@ -734,7 +750,8 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
           break;
         }
         case GGUF_IQ4_XS:
-          for (int i = 0; i < 32; ++i) payload[i] = b[8 + 32 * c + i];  // sub-blocks 2c, 2c+1
+          iq4_selector_order(b + 8 + 32 * c, payload);  // sub-blocks 2c, 2c+1
+          iq4_selector_order(b + 8 + 32 * c + 16, payload + 16);
           side[0] = b[0];
           side[1] = b[1];
           side[2] = (uint8_t)(int8_t)iq4xs_scale(b, 2 * c);

@@ -10,7 +10,9 @@
 //     [P][128 rows][16 B], followed by a side record of S bytes per row, [128 rows][S B].
 //     Q8_0   P=4 (qs of two blocks)                     S=4 (d0, d1 fp16)
 //     Q4_0   P=2 (qs of two blocks, ggml nibble order)   S=4 (d0, d1 fp16)
-//     IQ4_NL P=2 (as Q4_0)                               S=4
+//     IQ4_NL P=2 (two runs of 32 in "selector order": word t of a run holds the nibbles of values
+//            4t..4t+3 in bits 0-15 and 16+4t..16+4t+3 in bits 16-31, value 4t+k in nibble k)
+//                                                       S=4 (d0, d1 fp16)
 //     Q4_K   P=2 (the 32-byte qs chunk of sub-blocks 2c, 2c+1)  S=8 (d, dmin fp16, sc0, sc1, m0, m1 u8)
 //     Q6_K   P=3 (32 B low nibbles: v[i] | v[i+32]<<4; 16 B high pairs: v[i], v[i+16], v[i+32],
 //            v[i+48] at bits 0,2,4,6)                  S=8 (sc0..sc3 int8, d fp16, pad)
@@ -22,7 +24,7 @@
 //     Q3_K   P=1 (low 2 bits, as Q2_K)                  S=16 (d fp16, 4 int8 scales sc-32, pad 2,
 //                                                              H0, H1: the hmask bits)
 //     Q5_K   P=2 (as Q4_K)                              S=16 (d, dmin fp16, sc0, sc1, m0, m1, H0, H1)
-//     IQ4_XS P=2 (qs of sub-blocks 2c, 2c+1, IQ4_NL order)  S=4 (d fp16, 2 int8 scales sc-32)
+//     IQ4_XS P=2 (sub-blocks 2c, 2c+1, selector order as IQ4_NL)  S=4 (d fp16, 2 int8 scales sc-32)
 //   "H" words carry one extra bit per value, transposed so that one shift and one mask place the
 //   bits of four consecutive values (4g .. 4g+3, g = 0..7 within the word) at the same bit of
 //   four bytes: bit 8b + g of H is the bit of value 4g + b.
@@ -161,49 +163,6 @@ struct DecQ8_0 : PlaneStage<4, 4> {
   }
 };
 
-// Q4_0 / IQ4_NL: block of 32 values, byte i holds value i (low nibble) and value i+16 (high).
-// Q4_0 value = nib - 8 (exact fp16 via the magic number with offset 1032); IQ4_NL value = the
-// non-linear level (gguf/quants.py:1331) looked up with prmt over four registers of int8 levels.
-template <bool kNL>
-struct DecQ4Block : PlaneStage<2, 4> {
-  static constexpr bool kTma = false;
-  // nibbles (one per byte, 0..15) -> int8 levels of IQ4_NL, one per byte
-  __device__ __forceinline__ static uint32_t nl_levels(uint32_t x) {
-    const uint32_t t = x & 0x07070707u;
-    const uint32_t u = t | (t >> 4);
-    const uint32_t sel = (u & 0xFFu) | ((u >> 8) & 0xFF00u);
-    const uint32_t lo = prmt(0xBFAD9881u, 0xF6EADDCFu, sel);  // levels 0..7: -127 -104 -83 -65 -49 -35 -22 -10
-    const uint32_t hi = prmt(0x26190D01u, 0x71594535u, sel);  // levels 8..15: 1 13 25 38 53 69 89 113
-    const uint32_t m = ((x >> 3) & 0x01010101u) * 0xFFu;      // bytes whose nibble is >= 8
-    return (hi & m) | (lo & ~m);
-  }
-  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
-    const uint32_t dd = *reinterpret_cast<const uint32_t*>(side(st, r));
-#pragma unroll
-    for (int blk = 0; blk < 2; ++blk) {
-      const __half2 d = scale_pair(blk ? (dd >> 16) : (dd & 0xFFFF), rscale);
-      const uint4 v = chunk(st, blk, r);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const uint32_t nlo = w[t] & 0x0F0F0F0Fu, nhi = (w[t] >> 4) & 0x0F0F0F0Fu;  // values 4t.., 16+4t..
-        uint32_t a0, a1, b0, b1;
-        if constexpr (kNL) {
-          s8x4_to_f16x4(nl_levels(nlo), a0, a1);
-          s8x4_to_f16x4(nl_levels(nhi), b0, b1);
-        } else {
-          u8x4_to_f16x4(nlo, 0x64086408u, a0, a1);  // fp16 1032 = 1024 + 8
-          u8x4_to_f16x4(nhi, 0x64086408u, b0, b1);
-        }
-        out[16 * blk + 2 * t + 0] = hmul2_u32(a0, d);
-        out[16 * blk + 2 * t + 1] = hmul2_u32(a1, d);
-        out[16 * blk + 8 + 2 * t + 0] = hmul2_u32(b0, d);
-        out[16 * blk + 8 + 2 * t + 1] = hmul2_u32(b1, d);
-      }
-    }
-  }
-};
-
 // Packed fp16 arithmetic on words holding two fp16 values.
 __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
   __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
@@ -213,6 +172,79 @@ __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, __half2 s, __half2 c) 
   __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&a), s, c);
   return *reinterpret_cast<uint32_t*>(&r);
 }
+
+// Q4_0: block of 32 values, byte i holds value i (low nibble) and value i+16 (high); value =
+// nib - 8 (exact fp16 via the magic number with offset 1032), times the exact fp16 d*2^-e.
+struct DecQ4_0 : PlaneStage<2, 4> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(side(st, r));
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      const __half2 d = scale_pair(blk ? (dd >> 16) : (dd & 0xFFFF), rscale);
+      const uint4 v = chunk(st, blk, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        uint32_t a0, a1, b0, b1;
+        u8x4_to_f16x4(w[t] & 0x0F0F0F0Fu, 0x64086408u, a0, a1);         // values 4t..; 1032 = 1024 + 8
+        u8x4_to_f16x4((w[t] >> 4) & 0x0F0F0F0Fu, 0x64086408u, b0, b1);  // values 16+4t..
+        out[16 * blk + 2 * t + 0] = hmul2_u32(a0, d);
+        out[16 * blk + 2 * t + 1] = hmul2_u32(a1, d);
+        out[16 * blk + 8 + 2 * t + 0] = hmul2_u32(b0, d);
+        out[16 * blk + 8 + 2 * t + 1] = hmul2_u32(b1, d);
+      }
+    }
+  }
+};
+
+// The IQ4 non-linear levels (gguf/quants.py:1331) of four 4-bit codes -> two exact fp16 pairs.
+// f holds the codes of four consecutive values in its nibbles 0-3 ("selector order", written by
+// the repack).  Two prmt lookups over the levels + 128 as bytes (codes 0-7, 8-15), a third picks
+// per byte by bit 3 of the code, and the bytes go under the 0x64 magic byte: (1024 + L + 128) -
+// 1152 = L exactly.
+__device__ __forceinline__ void iq4_levels_f16(uint32_t f, uint32_t& lo, uint32_t& hi) {
+  const uint32_t sel = f & 0x7777u;
+  const uint32_t l = prmt(0x3F2D1801u, 0x766A5D4Fu, sel);  // -127 -104 -83 -65 -49 -35 -22 -10, + 128
+  const uint32_t h = prmt(0xA6998D81u, 0xF1D9C5B5u, sel);  // 1 13 25 38 53 69 89 113, + 128
+  const uint32_t v = prmt(l, h, ((f >> 1) & 0x4444u) | 0x3210u);
+  const uint32_t bias = 0x64806480u;  // fp16 (1152, 1152)
+  lo = hsub2_u32(prmt(v, 0x64646464u, 0x5140u), bias);
+  hi = hsub2_u32(prmt(v, 0x64646464u, 0x7362u), bias);
+}
+
+// IQ4_NL (one fp16 scale per run of 32, exact: RN16(d*L*2^-e)) and IQ4_XS (sub-block scale
+// d*(sc-32) formed in fp32, rounded once to fp16; gguf/quants.py:1352-1377): two runs of 32 per
+// stage in selector order, one fp16 multiply per value.
+template <bool kXS>
+struct DecIQ4 : PlaneStage<2, 4> {
+  static constexpr bool kTma = false;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
+    const uint32_t sd = *reinterpret_cast<const uint32_t*>(side(st, r));
+#pragma unroll
+    for (int blk = 0; blk < 2; ++blk) {
+      __half2 d;
+      if constexpr (kXS) {
+        const float dx = __fmul_rn(half_bits_to_float(sd), rscale);
+        d = __float2half2_rn(__fmul_rn(dx, (float)(int8_t)((sd >> (16 + 8 * blk)) & 0xFF)));
+      } else {
+        d = scale_pair(blk ? (sd >> 16) : (sd & 0xFFFF), rscale);
+      }
+      const uint4 v = chunk(st, blk, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        uint32_t a0, a1, b0, b1;
+        iq4_levels_f16(w[t], a0, a1);        // values 4t .. 4t+3
+        iq4_levels_f16(w[t] >> 16, b0, b1);  // values 16+4t .. 16+4t+3
+        out[16 * blk + 2 * t + 0] = hmul2_u32(a0, d);
+        out[16 * blk + 2 * t + 1] = hmul2_u32(a1, d);
+        out[16 * blk + 8 + 2 * t + 0] = hmul2_u32(b0, d);
+        out[16 * blk + 8 + 2 * t + 1] = hmul2_u32(b1, d);
+      }
+    }
+  }
+};
 
 // Q4_K: w = (d*sc)*q - dmin*m per 32-value sub-block (gguf/quants.py:504-522), in packed fp16.
 // Nibbles become exact fp16 pairs through the 0x64 magic byte (1024 + q, minus 1024); the high
@@ -450,33 +482,6 @@ struct DecQ5_K : PlaneStage<2, 16> {
         out[8 * j + 2 * t + 1] = hfma2_u32(hsub2_u32(b, kMagic), ds0, dm0);
         out[16 + 8 * j + 2 * t + 0] = hfma2_u32(hsub2_u32(c, kMagic), ds1, dm1);
         out[16 + 8 * j + 2 * t + 1] = hfma2_u32(hsub2_u32(e, kMagic), ds1, dm1);
-      }
-    }
-  }
-};
-
-// IQ4_XS: two IQ4_NL runs of 32 per stage with sub-block scales d*(sc-32) (gguf/quants.py:
-// 1352-1377).  The level is exact in fp16; d*sc*2^-e is formed in fp32 and rounded once to fp16,
-// then one fp16 multiply.
-struct DecIQ4_XS : PlaneStage<2, 4> {
-  static constexpr bool kTma = false;
-  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
-    const uint32_t sd = *reinterpret_cast<const uint32_t*>(side(st, r));
-    const float d = __fmul_rn(half_bits_to_float(sd), rscale);
-#pragma unroll
-    for (int blk = 0; blk < 2; ++blk) {
-      const __half2 dl = __float2half2_rn(__fmul_rn(d, (float)(int8_t)((sd >> (16 + 8 * blk)) & 0xFF)));
-      const uint4 v = chunk(st, blk, r);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        uint32_t a0, a1, b0, b1;
-        s8x4_to_f16x4(DecQ4Block<true>::nl_levels(w[t] & 0x0F0F0F0Fu), a0, a1);
-        s8x4_to_f16x4(DecQ4Block<true>::nl_levels((w[t] >> 4) & 0x0F0F0F0Fu), b0, b1);
-        out[16 * blk + 2 * t + 0] = hmul2_u32(a0, dl);
-        out[16 * blk + 2 * t + 1] = hmul2_u32(a1, dl);
-        out[16 * blk + 8 + 2 * t + 0] = hmul2_u32(b0, dl);
-        out[16 * blk + 8 + 2 * t + 1] = hmul2_u32(b1, dl);
       }
     }
   }

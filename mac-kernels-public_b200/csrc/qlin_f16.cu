@@ -410,8 +410,8 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   switch (a.fmt) {
     case WF_INT8: rc = dispatch_tm<DecInt8>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
-    case WF_Q4_0: rc = dispatch_tm<DecQ4Block<false>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
-    case WF_IQ4_NL: rc = dispatch_tm<DecQ4Block<true>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
+    case WF_Q4_0: rc = dispatch_tm<DecQ4_0>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
+    case WF_IQ4_NL: rc = dispatch_tm<DecIQ4<false>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     default:
       rc = dispatch_f16_blk(a.fmt, tx, tw, tp, tt, maps, p, tm, pair, stream);
       if (rc < 0) rc = dispatch_f16_kq(a.fmt, tx, tw, tp, tt, maps, p, tm, pair, stream);

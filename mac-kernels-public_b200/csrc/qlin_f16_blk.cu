@@ -10,7 +10,7 @@ int dispatch_f16_blk(int fmt, const CUtensorMap& tx, const CUtensorMap& tw, cons
     case WF_Q4_1: return dispatch_tm<DecQ4_1>(tx, tw, tp, tt, maps, p, tm, pair, stream);
     case WF_Q5_0: return dispatch_tm<DecQ5Block<false>>(tx, tw, tp, tt, maps, p, tm, pair, stream);
     case WF_Q5_1: return dispatch_tm<DecQ5Block<true>>(tx, tw, tp, tt, maps, p, tm, pair, stream);
-    case WF_IQ4_XS: return dispatch_tm<DecIQ4_XS>(tx, tw, tp, tt, maps, p, tm, pair, stream);
+    case WF_IQ4_XS: return dispatch_tm<DecIQ4<true>>(tx, tw, tp, tt, maps, p, tm, pair, stream);
     default: return -1;
   }
 }

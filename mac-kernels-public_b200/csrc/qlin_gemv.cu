@@ -209,8 +209,8 @@ int run_gemv(const F16GemmArgs& a, cudaStream_t stream) {
   switch (a.fmt) {
     case WF_INT8: return launch_gemv<DecInt8, true>(p, stream);
     case WF_Q8_0: return launch_gemv<DecQ8_0, false>(p, stream);
-    case WF_Q4_0: return launch_gemv<DecQ4Block<false>, false>(p, stream);
-    case WF_IQ4_NL: return launch_gemv<DecQ4Block<true>, false>(p, stream);
+    case WF_Q4_0: return launch_gemv<DecQ4_0, false>(p, stream);
+    case WF_IQ4_NL: return launch_gemv<DecIQ4<false>, false>(p, stream);
     case WF_Q4_K: return launch_gemv<DecQ4_K, false>(p, stream);
     case WF_Q6_K: return launch_gemv<DecQ6_K, false>(p, stream);
     case WF_Q4_1: return launch_gemv<DecQ4_1, false>(p, stream);
@@ -219,7 +219,7 @@ int run_gemv(const F16GemmArgs& a, cudaStream_t stream) {
     case WF_Q2_K: return launch_gemv<DecQ23_K<false>, false>(p, stream);
     case WF_Q3_K: return launch_gemv<DecQ23_K<true>, false>(p, stream);
     case WF_Q5_K: return launch_gemv<DecQ5_K, false>(p, stream);
-    case WF_IQ4_XS: return launch_gemv<DecIQ4_XS, false>(p, stream);
+    case WF_IQ4_XS: return launch_gemv<DecIQ4<true>, false>(p, stream);
     default: return -1;
   }
 }
