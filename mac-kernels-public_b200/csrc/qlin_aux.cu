@@ -873,7 +873,13 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
 }
 
 // Rotated values of group g for this lane: z[a][nb][c] = row (lane/4 + 8*(c>>1)),
-// column 16a + 8nb + 2*(lane%4) + (c&1) of the group, already normalized by 1/sqrt(G).
+// column 16a + 8nb + 2*(lane%4) + (c&1) of the group, not yet normalized: the caller multiplies by
+// prologue_norm<A>() = 1/sqrt(G), folded into its power-of-two scale.
+template <int A>
+__device__ __forceinline__ constexpr float prologue_norm() {
+  return A == 2 ? 0.17677669529663687f : A == 4 ? 0.125f : 0.08838834764831845f;
+}
+
 template <int A, int KIND, bool BF16>
 __device__ __forceinline__ void rotate_group(const uint8_t* tile, int pitch, int g, int lane,
                                              const uint32_t (&hb)[2][2], float (&z)[A][2][4]) {
@@ -888,7 +894,6 @@ __device__ __forceinline__ void rotate_group(const uint8_t* tile, int pitch, int
     mma_16816<BF16>(z[a][0], fr, hb[0][0], hb[0][1]);
     mma_16816<BF16>(z[a][1], fr, hb[1][0], hb[1][1]);
   }
-  constexpr float kNorm = A == 2 ? 0.17677669529663687f : A == 4 ? 0.125f : 0.08838834764831845f;
 #pragma unroll
   for (int nb = 0; nb < 2; ++nb) {
 #pragma unroll
@@ -912,29 +917,65 @@ __device__ __forceinline__ void rotate_group(const uint8_t* tile, int pitch, int
 #pragma unroll
         for (int k = 0; k < 4; ++k) z[k][nb][c] = y[k];
       }
-#pragma unroll
-      for (int a = 0; a < A; ++a) z[a][nb][c] = __fmul_rn(z[a][nb][c], kNorm);
     }
   }
 }
 
+// Exponent e with |v| * 2^-e in [2^14, 2^15) for the largest |v| = amax (0 for zero / non-finite).
+__device__ __forceinline__ int pow2_exponent(float amax) {
+  int f = 0;
+  if (amax > 0.f && amax <= 3.402823466e38f) {
+    int ex;
+    frexpf(amax, &ex);
+    f = ex - 15;
+  }
+  return f;
+}
+
+// Group exponent records of the single-pass prologue: a group of zeros and a group holding a
+// non-finite value are marked (their values were scaled by 2^0).
+constexpr int kGroupZero = -(1 << 20), kGroupNonFinite = 1 << 20;
+__device__ __forceinline__ int group_exponent_code(float amax, int f) {
+  return amax == 0.f ? kGroupZero : !(amax <= 3.402823466e38f) ? kGroupNonFinite : f;
+}
+
+// One pass over the tile: each warp rotates its groups once, scales each (row, group) by its own
+// power of two (the group's maximum into [2^14, 2^15)), rounds to fp16 in place and records the
+// exponent.  The row exponent is the largest of its groups' (the exponent of the row maximum);
+// the store loop multiplies each group by 2^(group - row) on the way out, exact in fp16 except for
+// results below the fp16 normal range (|v| < 2^-14 against a row maximum of at least 2^14).  The
+// tile arrives in rounds of 8 groups (one per warp) so the first rotations overlap later loads.
 template <int A, int KIND, bool BF16>
 __global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restrict__ x, long long ldx, int M, int K,
                                                            __half* __restrict__ out, long long ldo,
                                                            int32_t* __restrict__ row_exp) {
   extern __shared__ __align__(16) uint8_t psm[];
   const int pitch = K * 2 + 16;
+  const int groups = K / (16 * A);
   uint8_t* tile = psm;
-  unsigned* rmax = reinterpret_cast<unsigned*>(psm + 16 * pitch);
+  int* gexp = reinterpret_cast<int*>(psm + 16 * pitch);  // [16 rows][groups]
+  int* rexp = gexp + 16 * groups;                          // [16 rows]
   const int row0 = blockIdx.x * 16;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid < 16) rmax[tid] = 0u;
-  const int cpr = K / 8;  // 16-byte chunks per row
-  for (int i = tid; i < 16 * cpr; i += 256) {
-    const int r = i / cpr, c = i - r * cpr;
-    uint8_t* dst = tile + r * pitch + c * 16;
-    if (row0 + r < M) cp_async16(dst, reinterpret_cast<const uint8_t*>(x) + ((long long)(row0 + r) * ldx + c * 8) * 2);
-    else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  constexpr int kGroupCols = 16 * A;
+  const int rounds = (groups + 7) / 8;
+  // Loads, one commit group per round of 8 groups.  (row, chunk) advance without divisions.
+  for (int j = 0; j < rounds; ++j) {
+    const int c0 = j * kGroupCols, c1 = min(groups, j * 8 + 8) * kGroupCols / 8;  // 16-byte chunks
+    const int cpr = c1 - c0;
+    const int dr = 256 / cpr, dc = 256 - dr * cpr;
+    int r = tid / cpr, c = tid - r * cpr;
+    for (; r < 16; r += dr, c += dc) {
+      if (c >= cpr) {
+        c -= cpr;
+        if (++r >= 16) break;
+      }
+      uint8_t* dst = tile + r * pitch + (c0 + c) * 16;
+      if (row0 + r < M)
+        cp_async16(dst, reinterpret_cast<const uint8_t*>(x) + ((long long)(row0 + r) * ldx + (c0 + c) * 8) * 2);
+      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
   // B fragments of H16 (symmetric): n-block nb, k rows 2(lane%4)+{0,1} and +8, column lane/4.
   uint32_t hb[2][2];
@@ -944,65 +985,104 @@ __global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restric
     hb[nb][0] = pack_pm1<BF16>(hadamard16_entry<KIND>(k0, n), hadamard16_entry<KIND>(k0 + 1, n));
     hb[nb][1] = pack_pm1<BF16>(hadamard16_entry<KIND>(k0 + 8, n), hadamard16_entry<KIND>(k0 + 9, n));
   }
-  cp_async_wait_all();
-  __syncthreads();
-  const int groups = K / (16 * A);
-  // pass 1: row maxima
-  float m_lo = 0.f, m_hi = 0.f;
-  for (int g = warp; g < groups; g += 8) {
-    float z[A][2][4];
-    rotate_group<A, KIND, BF16>(tile, pitch, g, lane, hb, z);
+  constexpr float kNorm = prologue_norm<A>();
+  for (int j = 0; j < rounds; ++j) {
+    const int pending = rounds - 1 - j;  // commit groups still allowed in flight
+    if (pending >= 2) asm volatile("cp.async.wait_group 2;" ::: "memory");
+    else if (pending == 1) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const int g = j * 8 + warp;
+    if (g < groups) {
+      float z[A][2][4];
+      rotate_group<A, KIND, BF16>(tile, pitch, g, lane, hb, z);
+      float m_lo = 0.f, m_hi = 0.f;
 #pragma unroll
-    for (int a = 0; a < A; ++a)
+      for (int a = 0; a < A; ++a)
 #pragma unroll
-      for (int nb = 0; nb < 2; ++nb) {
-        m_lo = fmaxf(m_lo, fmaxf(fabsf(z[a][nb][0]), fabsf(z[a][nb][1])));
-        m_hi = fmaxf(m_hi, fmaxf(fabsf(z[a][nb][2]), fabsf(z[a][nb][3])));
+        for (int nb = 0; nb < 2; ++nb) {
+          m_lo = fmaxf(m_lo, fmaxf(fabsf(z[a][nb][0]), fabsf(z[a][nb][1])));
+          m_hi = fmaxf(m_hi, fmaxf(fabsf(z[a][nb][2]), fabsf(z[a][nb][3])));
+        }
+#pragma unroll
+      for (int o = 1; o <= 2; o <<= 1) {
+        m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, o));
+        m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, o));
       }
-  }
+      // max |z * kNorm| = RN(max|z| * kNorm): rounding is monotonic
+      const float a_lo = __fmul_rn(m_lo, kNorm), a_hi = __fmul_rn(m_hi, kNorm);
+      const int f_lo = pow2_exponent(a_lo), f_hi = pow2_exponent(a_hi);
+      if ((lane & 3) == 0) {
+        gexp[(lane >> 2) * groups + g] = group_exponent_code(a_lo, f_lo);
+        gexp[((lane >> 2) + 8) * groups + g] = group_exponent_code(a_hi, f_hi);
+      }
+      // z * (kNorm * 2^-f) = RN(z * kNorm) * 2^-f while the scale is a normal fp32 number; rows
+      // of extreme exponents take the two-step form (a warp-uniform branch around whole loops)
+      const bool fast = __all_sync(0xffffffffu, f_lo >= -100 && f_lo <= 100 && f_hi >= -100 && f_hi <= 100);
+      if (fast) {
+        const float s_lo = exp2i(-f_lo) * kNorm, s_hi = exp2i(-f_hi) * kNorm;
 #pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, o));
-    m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, o));
-  }
-  if ((lane & 3) == 0) {
-    atomicMax(&rmax[lane >> 2], __float_as_uint(m_lo));
-    atomicMax(&rmax[(lane >> 2) + 8], __float_as_uint(m_hi));
-  }
-  __syncthreads();
-  auto row_f = [&](int r) {
-    const float amax = __uint_as_float(rmax[r]);
-    int f = 0;
-    if (amax > 0.f && amax <= 3.402823466e38f) {
-      int ex;
-      frexpf(amax, &ex);
-      f = ex - 15;
+        for (int a = 0; a < A; ++a)
+#pragma unroll
+          for (int nb = 0; nb < 2; ++nb) {
+            const int col = g * kGroupCols + 16 * a + 8 * nb + 2 * (lane & 3);
+            *reinterpret_cast<uint32_t*>(tile + (lane >> 2) * pitch + col * 2) =
+                pack_f16x2(__fmul_rn(z[a][nb][0], s_lo), __fmul_rn(z[a][nb][1], s_lo));
+            *reinterpret_cast<uint32_t*>(tile + ((lane >> 2) + 8) * pitch + col * 2) =
+                pack_f16x2(__fmul_rn(z[a][nb][2], s_hi), __fmul_rn(z[a][nb][3], s_hi));
+          }
+      } else {
+#pragma unroll
+        for (int a = 0; a < A; ++a)
+#pragma unroll
+          for (int nb = 0; nb < 2; ++nb) {
+            const int col = g * kGroupCols + 16 * a + 8 * nb + 2 * (lane & 3);
+            *reinterpret_cast<uint32_t*>(tile + (lane >> 2) * pitch + col * 2) =
+                pack_f16x2(scale_pow2(__fmul_rn(z[a][nb][0], kNorm), f_lo), scale_pow2(__fmul_rn(z[a][nb][1], kNorm), f_lo));
+            *reinterpret_cast<uint32_t*>(tile + ((lane >> 2) + 8) * pitch + col * 2) =
+                pack_f16x2(scale_pow2(__fmul_rn(z[a][nb][2], kNorm), f_hi), scale_pow2(__fmul_rn(z[a][nb][3], kNorm), f_hi));
+          }
+      }
     }
-    return f;
-  };
-  const int f_lo = row_f(lane >> 2), f_hi = row_f((lane >> 2) + 8);
-  // pass 2: rotate again, scale, round to fp16 in place (each warp overwrites only its groups)
-  for (int g = warp; g < groups; g += 8) {
-    float z[A][2][4];
-    rotate_group<A, KIND, BF16>(tile, pitch, g, lane, hb, z);
-#pragma unroll
-    for (int a = 0; a < A; ++a)
-#pragma unroll
-      for (int nb = 0; nb < 2; ++nb) {
-        const int col = g * 16 * A + 16 * a + 8 * nb + 2 * (lane & 3);
-        *reinterpret_cast<uint32_t*>(tile + (lane >> 2) * pitch + col * 2) =
-            pack_f16x2(scale_pow2(z[a][nb][0], f_lo), scale_pow2(z[a][nb][1], f_lo));
-        *reinterpret_cast<uint32_t*>(tile + ((lane >> 2) + 8) * pitch + col * 2) =
-            pack_f16x2(scale_pow2(z[a][nb][2], f_hi), scale_pow2(z[a][nb][3], f_hi));
-      }
   }
   __syncthreads();
-  if (tid < 16 && row0 + tid < M) row_exp[row0 + tid] = row_f(tid);
-  for (int i = tid; i < 16 * cpr; i += 256) {
-    const int r = i / cpr, c = i - r * cpr;
-    if (row0 + r < M)
-      *reinterpret_cast<uint4*>(out + (long long)(row0 + r) * ldo + c * 8) =
-          *reinterpret_cast<const uint4*>(tile + r * pitch + c * 16);
+  if (tid < 16) {
+    // the exponent of the row maximum: the largest over nonzero groups; 0 for a zero row or a row
+    // with a non-finite value (as the exponent of the row maximum itself)
+    int f = kGroupZero;
+    for (int g = 0; g < groups; ++g) f = max(f, gexp[tid * groups + g]);
+    if (f == kGroupZero || f == kGroupNonFinite) f = 0;
+    rexp[tid] = f;
+    if (row0 + tid < M) row_exp[row0 + tid] = f;
+  }
+  __syncthreads();
+  const int cpr = K / 8;
+  const int dr = 256 / cpr, dc = 256 - dr * cpr;
+  int r = tid / cpr, c = tid - r * cpr;
+  for (; r < 16; r += dr, c += dc) {
+    if (c >= cpr) {
+      c -= cpr;
+      if (++r >= 16) break;
+    }
+    if (row0 + r >= M) break;
+    uint4 v = *reinterpret_cast<const uint4*>(tile + r * pitch + c * 16);
+    const int code = gexp[r * groups + (c * 8) / kGroupCols];
+    const int d = (code == kGroupZero ? rexp[r] : code == kGroupNonFinite ? 0 : code) - rexp[r];
+    if (d != 0) {
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+      if (d >= -14 && d < 0) {
+        const __half2 sc = __half2half2(__ushort_as_half((unsigned short)((d + 15) << 10)));  // 2^d
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = hmul2_u32(w[e], sc);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+          w[e] = pack_f16x2(scale_pow2(f2.x, -d), scale_pow2(f2.y, -d));
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(out + (long long)(row0 + r) * ldo + c * 8) = v;
   }
 }
 
@@ -1014,7 +1094,7 @@ static bool launch_prologue_mma(const void* x, int x_dtype, long long ldx, int M
   if ((x_dtype != 1 && x_dtype != 2) || K != Kp || K % group != 0 || K % 8 != 0 || ldx % 8 != 0 ||
       (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
     return false;
-  const size_t smem = 16 * ((size_t)K * 2 + 16) + 64;
+  const size_t smem = 16 * ((size_t)K * 2 + 16) + 4 * (16 * (size_t)(K / group) + 16);
   if (smem > 200 * 1024) return false;
   const bool bf = x_dtype == 2;
   const dim3 grid((M + 15) / 16);

@@ -205,6 +205,38 @@ def test_prologue_rotation_matches_oracle(qlin):
 
 
 @pytest.mark.parametrize("x_dtype", [torch.float16, torch.bfloat16])
+def test_prologue_rows_with_zero_tiny_and_mixed_scale_groups(qlin, x_dtype):
+    """Rows whose rotation groups differ wildly in scale: zero groups, all-tiny rows, one group
+    2^27 below the row maximum, an all-zero row.  The row exponent is that of the row maximum and
+    every group keeps fp16 precision relative to its own magnitude."""
+    m, k, group = 20, 1024, 128
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(m, k, generator=g)
+    x[1, :256] = 0
+    x[1] *= 1e-4
+    x[2, :128] *= 1e3
+    x[2, 640:768] *= 1e-5
+    x[3] = 0
+    x[4, 128:] = 0
+    x = x.to(x_dtype)
+    xr, f = qlin.prologue_f16(x.cuda(), group)
+    xr = xr[:, :k].float().cpu().numpy().astype(np.float64)
+    f = f.cpu().numpy().astype(np.int64)
+    ref = O.rotate_rows(x.float().numpy(), group)
+    got = xr * np.ldexp(1.0, f)[:, None]
+    for r in range(m):
+        amax = np.abs(ref[r]).max()
+        if amax == 0:
+            assert f[r] == 0 and np.all(xr[r] == 0)
+            continue
+        assert 2 ** 14 <= np.abs(xr[r]).max() <= 2 ** 15, r  # the row maximum sets the exponent
+        for c in range(0, k, group):  # each group against its own scale
+            gmax = np.abs(ref[r, c:c + group]).max()
+            if gmax > 0:
+                assert np.abs(got[r, c:c + group] - ref[r, c:c + group]).max() <= 2e-3 * gmax, (r, c)
+
+
+@pytest.mark.parametrize("x_dtype", [torch.float16, torch.bfloat16])
 def test_quantize_rows_int8_bit_exact(qlin, x_dtype):
     m, k = 64, 1536
     g = torch.Generator().manual_seed(12)

@@ -69,3 +69,39 @@ def test_asymmetric_correction_declines(qlin):
     with pytest.raises(NotImplementedError):
         qlin.w4a8_int8_linear(torch.randn(4, 1024, device="cuda", dtype=torch.float16), q, s_rel, s_ch, cb,
                               torch.zeros(96, device="cuda"))
+
+
+def _random_kitchen(n, k, bits, seed, codebook):
+    """Seeded packed codes at checkpoint widths: uniform codes, finite positive e4m3 s_rel
+    (bytes 0x20..0x5F: 2^-4 .. 15), fp32 s_channel, and a sorted 16-level codebook for 4 bits."""
+    rng = np.random.default_rng(seed)
+    lo = 1 if bits == 6 else 0
+    codes = rng.integers(lo, 1 << bits, size=(n, k))
+    q = O.pack_codes_kitchen(codes, bits)
+    s_rel = rng.integers(0x20, 0x60, size=(n, k // 16)).astype(np.uint8)
+    s_ch = (np.abs(rng.standard_normal(n)) * 1e-3 + 1e-4).astype(np.float32)
+    cb = np.sort(rng.uniform(-8, 8, 16)).astype(np.float32) if codebook else None
+    return q, s_rel, s_ch, cb
+
+
+@pytest.mark.parametrize("bits,codebook", [(4, True), (4, False), (6, False)])
+@pytest.mark.parametrize("n,k", [(12288, 3072), (3072, 12288)])
+def test_grid_and_linear_at_checkpoint_widths(qlin, bits, codebook, n, k):
+    """Qwen-Image / Wan MLP widths: the int8 grid is bit-identical with the oracle's restatement of
+    the reference port's decode over the whole tensor, and the linear (H4-256 rotation) meets the
+    fp64 tolerance."""
+    q, s_rel, s_ch, cb = _random_kitchen(n, k, bits, seed=n + k + bits, codebook=codebook)
+    from qlin._w4a8 import kitchen_grid
+    cb_t = None if cb is None else torch.from_numpy(cb).cuda()
+    grid = kitchen_grid(torch.from_numpy(q).cuda(), torch.from_numpy(s_rel).view(torch.float8_e4m3fn).cuda(), cb_t, 16)
+    want = O.kitchen_int8_grid(q, s_rel, k, bits, 16, cb)
+    assert np.array_equal(grid.cpu().numpy(), want)
+    m = 96
+    g = torch.Generator().manual_seed(k)
+    x = torch.randn(m, k, generator=g).to(torch.float16)
+    w = O.dequantize_kitchen_w4a8(q, s_rel, s_ch, k, bits, 16, cb, 256)
+    ref = O.linear_f64(x.float().numpy(), w)
+    y = qlin.w4a8_int8_linear(x.cuda(), torch.from_numpy(q).cuda(),
+                              torch.from_numpy(s_rel).view(torch.float8_e4m3fn).cuda(),
+                              torch.from_numpy(s_ch).cuda(), cb_t, None, None, 16, 256)
+    assert O.max_abs_rel(y.float().cpu().numpy(), ref) <= 2e-3
