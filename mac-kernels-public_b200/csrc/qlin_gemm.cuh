@@ -212,16 +212,13 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         const int ks = tile_ks(t);
         const int s0 = ks * p.stages_per_split;
         const int s1 = min(p.num_k_stages, s0 + p.stages_per_split);
-        for (int kst = s0; kst < s1; ++kst, ++it) {
+        // weight stages, then (fused LoRA) the low-rank stages in a loop of their own, so the
+        // weight-stage loop is the same code with or without LoRA support
+        const int s_main = min(s1, p.main_k_stages);
+        for (int kst = s0; kst < s_main; ++kst, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
-          if (kst >= p.main_k_stages) {  // LoRA stage: the low-rank activation only
-            mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes);
-            tma_load_2d(sx + s * Cfg::kXStageBytes, &tmap_t, &full[s], (kst - p.main_k_stages) * 64,
-                        mt * TM + (int)rank * Cfg::kXRows);
-            continue;
-          }
           mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes + Dec::kStageBytes);
           {
             const int k0 = kst * 64;
@@ -235,6 +232,14 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             const uint8_t* src = p.w_stages + ((size_t)nt * p.main_k_stages + kst) * Dec::kStageBytes;
             bulk_load(sw + s * kWStage, src, Dec::kStageBytes, &full[s]);
           }
+        }
+        for (int kst = max(s0, p.main_k_stages); kst < s1 && ok; ++kst, ++it) {  // LoRA: T' only
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes);
+          tma_load_2d(sx + s * Cfg::kXStageBytes, &tmap_t, &full[s], (kst - p.main_k_stages) * 64,
+                      mt * TM + (int)rank * Cfg::kXRows);
         }
       }
       if (!ok) {
@@ -263,19 +268,35 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         if (!mbar_wait(&acc_empty[b], aph ^ 1, abort_flag, p.status, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * Cfg::kAccCols;
-        for (int kst = s0; kst < s1; ++kst, ++it) {
+        const int s_main = min(s1, p.main_k_stages);
+        for (int kst = s0; kst < s_main; ++kst, ++it) {
           const int s = it % STAGES;
           const int as = it % Cfg::kASlots;
           if (!mbar_wait(&a_full[as], (it / Cfg::kASlots) & 1, abort_flag, p.status, 3)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_tmem = tmem_base + Cfg::kACol0 + as * 32;
           const uint64_t b_desc = smem_desc_sw128(smem_u32(sx + s * Cfg::kXStageBytes));
-          const uint32_t idesc = kst < p.main_k_stages ? idesc_main : idesc_lora;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t acc = (kst > s0 || kk > 0) ? 1u : 0u;
-            if constexpr (PAIR) mma_f16_ts_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, acc);
-            else mma_f16_ts(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, acc);
+            if constexpr (PAIR) mma_f16_ts_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc_main, acc);
+            else mma_f16_ts(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc_main, acc);
+          }
+          commit_all(&empty[s]);
+          commit_all(&a_empty[as]);
+        }
+        for (int kst = max(s0, p.main_k_stages); kst < s1 && ok; ++kst, ++it) {  // LoRA: bf16 operands
+          const int s = it % STAGES;
+          const int as = it % Cfg::kASlots;
+          if (!mbar_wait(&a_full[as], (it / Cfg::kASlots) & 1, abort_flag, p.status, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_tmem = tmem_base + Cfg::kACol0 + as * 32;
+          const uint64_t b_desc = smem_desc_sw128(smem_u32(sx + s * Cfg::kXStageBytes));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t acc = (kst > s0 || kk > 0) ? 1u : 0u;
+            if constexpr (PAIR) mma_f16_ts_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc_lora, acc);
+            else mma_f16_ts(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc_lora, acc);
           }
           commit_all(&empty[s]);
           commit_all(&a_empty[as]);
@@ -306,23 +327,36 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       const int n = nt * 128 + r;
       float rscale = 1.f;
       if (p.w_row_exp != nullptr && p.col_scale_kind == CS_EXP2) rscale = exp2i(-p.w_row_exp[min(n, p.N - 1)]);
-      for (int kst = s0; kst < s1; ++kst, ++it) {
+      const int s_main = min(s1, p.main_k_stages);
+      for (int kst = s0; kst < s_main; ++kst, ++it) {
         if ((int)(it % Cfg::kDecGroups) != group) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag, p.status, 4)) { ok = false; break; }
         uint32_t a[32];
-        if (kst < p.main_k_stages) {
-          Dec::decode(sw + s * kWStage, r, rscale, a);
-        } else {  // LoRA stage: 64 bf16 values of this row of U', as stored
-          const uint4* u = reinterpret_cast<const uint4*>(p.lora_u + (size_t)n * p.lora_k + (kst - p.main_k_stages) * 64);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint4 v = __ldg(u + j);
-            a[4 * j] = v.x; a[4 * j + 1] = v.y; a[4 * j + 2] = v.z; a[4 * j + 3] = v.w;
-          }
-        }
+        Dec::decode(sw + s * kWStage, r, rscale, a);
         // the slot's previous weights have been consumed by their MMAs
+        const int as = it % Cfg::kASlots;
+        if (!mbar_wait(&a_empty[as], ((it / Cfg::kASlots) & 1) ^ 1, abort_flag, p.status, 8)) { ok = false; break; }
+        tc_fence_after();
+        tmem_st32(tmem_base + ((uint32_t)(quarter * 32) << 16) + Cfg::kACol0 + as * 32, a);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) arrive_leader(&a_full[as]);
+      }
+      for (int kst = max(s0, p.main_k_stages); kst < s1 && ok; ++kst, ++it) {
+        if ((int)(it % Cfg::kDecGroups) != group) continue;
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag, p.status, 4)) { ok = false; break; }
+        uint32_t a[32];  // LoRA stage: 64 bf16 values of this row of U', as stored
+        const uint4* u = reinterpret_cast<const uint4*>(p.lora_u + (size_t)n * p.lora_k + (kst - p.main_k_stages) * 64);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 v = __ldg(u + j);
+          a[4 * j] = v.x; a[4 * j + 1] = v.y; a[4 * j + 2] = v.z; a[4 * j + 3] = v.w;
+        }
         const int as = it % Cfg::kASlots;
         if (!mbar_wait(&a_empty[as], ((it / Cfg::kASlots) & 1) ^ 1, abort_flag, p.status, 8)) { ok = false; break; }
         tc_fence_after();
