@@ -740,10 +740,7 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
             const int hi = (b[128 + 32 * h + (rr % 32)] >> (2 * (rr / 32))) & 0x3;
             v[i] = (uint8_t)(lo | (hi << 4));
           }
-          for (int i = 0; i < 32; ++i) payload[i] = (uint8_t)((v[i] & 0xF) | ((v[i + 32] & 0xF) << 4));
-          for (int i = 0; i < 16; ++i)
-            payload[32 + i] =
-                (uint8_t)((v[i] >> 4) | ((v[i + 16] >> 4) << 2) | ((v[i + 32] >> 4) << 4) | ((v[i + 48] >> 4) << 6));
+          for (int i = 0; i < 64; ++i) payload[i] = v[i];  // one byte per code
           for (int t = 0; t < 4; ++t) side[t] = b[192 + base / 16 + t];
           side[4] = b[208];
           side[5] = b[209];

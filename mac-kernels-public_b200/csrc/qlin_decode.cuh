@@ -14,8 +14,7 @@
 //            4t..4t+3 in bits 0-15 and 16+4t..16+4t+3 in bits 16-31, value 4t+k in nibble k)
 //                                                       S=4 (d0, d1 fp16)
 //     Q4_K   P=2 (the 32-byte qs chunk of sub-blocks 2c, 2c+1)  S=8 (d, dmin fp16, sc0, sc1, m0, m1 u8)
-//     Q6_K   P=3 (32 B low nibbles: v[i] | v[i+32]<<4; 16 B high pairs: v[i], v[i+16], v[i+32],
-//            v[i+48] at bits 0,2,4,6)                  S=8 (sc0..sc3 int8, d fp16, pad)
+//     Q6_K   P=4 (one byte per value: the unsigned 6-bit code)  S=8 (sc0..sc3 int8, d fp16, pad)
 //     Q4_1   P=2 (qs of two blocks)                     S=8 (d0, m0, d1, m1 fp16)
 //     Q5_0   P=2 (qs of two blocks)                     S=12 (d0, d1 fp16, H0, H1)
 //     Q5_1   P=2 (qs of two blocks)                     S=16 (d0, m0, d1, m1 fp16, H0, H1)
@@ -279,37 +278,27 @@ struct DecQ4_K : PlaneStage<2, 8> {
   }
 };
 
-// Q6_K: w = (d*sc)*(q-32) per 16 values (gguf/quants.py:554-572), in packed fp16.  The 6-bit code
-// is assembled under the 0x64 magic byte (low nibble from the 32-byte plane, high two bits from
-// the 16-byte plane) and (1024 + q) - 1056 = q - 32 is exact; d*sc*2^-e is formed in fp32 and
-// rounded once to fp16, then one fp16 multiply per value.
-struct DecQ6_K : PlaneStage<3, 8> {
+// Q6_K: w = (d*sc)*(q-32) per 16 values (gguf/quants.py:552-574).  The repack stores each 6-bit
+// code in a byte (1.125 bytes per value with the scales, +37% over the raw blocks, for the decode
+// cost of Q8_0): the code goes under the 0x64 magic byte, (1024 + q) - 1056 = q - 32 is exact, and
+// one fp16 multiply by d*sc*2^-e (formed in fp32, rounded once to fp16).
+struct DecQ6_K : PlaneStage<4, 8> {
   static constexpr bool kTma = false;
   __device__ __forceinline__ static void decode(const uint8_t* st, int r, float rscale, uint32_t (&out)[32]) {
     const uint2 sd = *reinterpret_cast<const uint2*>(side(st, r));
     const float d = __fmul_rn(half_bits_to_float(sd.y), rscale);
-    __half2 ds[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) ds[t] = __float2half2_rn(__fmul_rn(d, (float)(int8_t)((sd.x >> (8 * t)) & 0xFF)));
-    const uint4 l0 = chunk(st, 0, r), l1 = chunk(st, 1, r), hv = chunk(st, 2, r);
-    const uint32_t lo[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-    const uint32_t hi[4] = {hv.x, hv.y, hv.z, hv.w};
     constexpr uint32_t kBias = 0x64206420u;  // fp16 (1056, 1056) = 1024 + 32
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      // l bytes 4k..4k+3: low nibbles are values 4k.., high nibbles values 32+4k..; their high
-      // bits sit in h bytes (4k..4k+3) mod 16 at bit 0 (values < 16), 2 (< 32), 4 (< 48), 6.
-      const uint32_t hw = hi[k & 3];
+    for (int j = 0; j < 4; ++j) {  // chunk j = the 16-value group j
+      const __half2 ds = __float2half2_rn(__fmul_rn(d, (float)(int8_t)((sd.x >> (8 * j)) & 0xFF)));
+      const uint4 v = chunk(st, j, r);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t a = prmt(lo[k], 0x64646464u, h ? 0x7362u : 0x5140u);  // [l, 0x64, l', 0x64]
-        const uint32_t hb = prmt(hw, 0u, h ? 0x4342u : 0x4140u);             // [h, 0, h', 0]
-        const uint32_t hl = (k < 4 ? (hb << 4) : (hb << 2)) & 0x00300030u;
-        const uint32_t hh = ((k < 4 ? hb : (hb >> 2)) & 0x00300030u) | 0x64006400u;
-        const uint32_t ql = (a & 0xFF0FFF0Fu) | hl;            // 1024 + v[4k+2h], v[4k+2h+1]
-        const uint32_t qh = ((a >> 4) & 0x000F000Fu) | hh;     // 1024 + v[32+4k+2h], ...
-        out[2 * k + h] = hmul2_u32(hsub2_u32(ql, kBias), ds[k >> 2]);
-        out[16 + 2 * k + h] = hmul2_u32(hsub2_u32(qh, kBias), ds[2 + (k >> 2)]);
+      for (int t = 0; t < 4; ++t) {
+        uint32_t lo, hi;
+        u8x4_to_f16x4(w[t], kBias, lo, hi);
+        out[8 * j + 2 * t + 0] = hmul2_u32(lo, ds);
+        out[8 * j + 2 * t + 1] = hmul2_u32(hi, ds);
       }
     }
   }

@@ -156,7 +156,7 @@ uint32_t gguf_stage_bytes(int qtype, int* P, int* S) {
     case WF_Q5_K: p = 2; s = 16; break;
     case WF_Q2_K: p = 1; s = 8; break;
     case WF_Q3_K: p = 1; s = 16; break;
-    case WF_Q6_K: p = 3; s = 8; break;
+    case WF_Q6_K: p = 4; s = 8; break;
     default: return 0;
   }
   if (P) *P = p;
@@ -199,22 +199,22 @@ static bool use_pair(int tm, int n_tiles) {
   return enabled && tm >= 128 && n_tiles % 2 == 0;
 }
 
-// Relative decode cost of a 64-deep stage per format (the 4-bit formats are the unit; Q6_K was
-// measured ~12% slower, the formats that insert a fifth / third bit or scale 16-value groups are
-// between the two).
+// Relative decode cost of a 64-deep stage per format (the 4-bit formats are the unit; measured at
+// configuration-2 shape: the formats that insert a fifth / third bit are ~4% slower, the IQ4
+// codebook lookups ~25%).
 static double fmt_stage_cost(int fmt) {
   switch (fmt) {
-    case WF_Q6_K: return 1.12;
-    case WF_Q5_0: case WF_Q5_1: case WF_Q5_K: case WF_Q3_K: return 1.06;
-    case WF_Q2_K: return 1.03;
+    case WF_IQ4_NL: case WF_IQ4_XS: return 1.25;
+    case WF_Q5_0: case WF_Q5_1: case WF_Q5_K: case WF_Q3_K: return 1.04;
+    case WF_Q2_K: case WF_Q8_0: case WF_Q6_K: return 1.02;
     default: return 1.0;
   }
 }
 
 // Modelled time of one plan (microseconds at the boost clock), from measured per-stage costs of
 // the persistent kernel on B200: a 64-deep K stage of one tile costs c(TM), the 256-token tile
-// (single-buffered accumulator) adds an exposed epilogue per tile, Q6_K decodes ~12% slower, and
-// a K split adds the finalize pass over the fp32 partials.
+// (single-buffered accumulator) adds an exposed epilogue per tile, the format scales the stage cost
+// (fmt_stage_cost), and a K split adds the finalize pass over the fp32 partials.
 static double plan_cost(int M, int N, int kst, int fmt, int tm, int splits, int sms) {
   const int n_tiles = (N + 127) / 128;
   const bool pair = use_pair(tm, n_tiles);

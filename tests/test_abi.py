@@ -37,7 +37,7 @@ def test_version_and_host_side_declines_without_gpu():
     assert lib.qlin_gguf_repacked_bytes(12, 130, 512, ctypes.byref(size), ctypes.byref(npad)) == 0
     assert npad.value == 256 and size.value == 2 * 8 * 128 * 40
     # every supported type: bytes per 64-value stage of a 128-row tile (16 B planes + side record)
-    stage = {2: 36, 3: 40, 6: 44, 7: 48, 8: 68, 10: 24, 11: 32, 12: 40, 13: 48, 14: 56, 20: 36, 23: 36}
+    stage = {2: 36, 3: 40, 6: 44, 7: 48, 8: 68, 10: 24, 11: 32, 12: 40, 13: 48, 14: 72, 20: 36, 23: 36}
     for qtype, per_row in stage.items():
         qk = 256 if qtype in (10, 11, 12, 13, 14, 23) else 32
         assert lib.qlin_gguf_repacked_bytes(qtype, 10, 4 * qk, ctypes.byref(size), ctypes.byref(npad)) == 0
