@@ -5,10 +5,17 @@
 //
 // xq are the per-token INT8 activations (prologue), wq' = D * wq the decoded weights scaled by
 // an exact power of two D (16 for 4-bit, 4 for 6-bit) so the decode needs no shuffles, and
-// inv = 1/D.  Every K-group accumulates into its own int32 TMEM buffer (double-buffered); eight
+// inv = 1/D.  Every K-group accumulates into its own int32 TMEM buffer (double-buffered); the
 // rescale warps fold s[n, g] * P_g into fp32 registers while the tensor cores run the next
 // group.  With one group spanning all of K (per-channel scales) this is a plain int8 GEMM with
 // the scale in the epilogue.
+//
+// The rescale is the per-group serial step (its cost grows with every value of every group), so
+// it is kept to one packed-fp32 pair of instructions per two values: each accumulator buffer is
+// pre-biased in TMEM with the bit pattern of 1.5*2^23 (0x4B400000) before its group's first MMA,
+// so the int32 result read back IS the float 1.5*2^23 + P (exact while |P| < 2^22: groups of
+// <= 128 values of 8-bit x 8-bit products), and s*P = s*(f - 1.5*2^23) needs no integer add.
+// The rescale warps re-write the bias right after reading a buffer (one tcgen05.st per 32 values).
 //
 // Warp roles (448 threads, one CTA per SM, persistent):
 //   warp 0        TMA producer            warp 1   TMEM alloc + MMA issuer
@@ -69,12 +76,14 @@ template <int TM, int STAGES>
 struct I8Cfg {
   static constexpr int kDecGroups = 1;
   static constexpr int kEpiWarps = 8;
+  static constexpr int kEpiParts = kEpiWarps / 4;  // rescale warps per TMEM lane quarter
   static constexpr int kThreads = 32 * (2 + 4 * kDecGroups + kEpiWarps);
   static constexpr int kXStageBytes = TM * 128;  // TM rows x 128 int8
   static constexpr int kACol0 = 2 * TM;
   static constexpr uint32_t kTmemCols = 512;
   static_assert(2 * TM + STAGES * 32 <= 512, "TMEM budget");
-  static_assert(TM >= 32, "the rescale warps split TM into two halves of >= 16 columns");
+  static_assert(TM / kEpiParts >= 8 && (TM / kEpiParts <= 32 || TM / kEpiParts % 32 == 0),
+                "each rescale warp reads its columns in chunks of 8, 16 or 32");
 };
 
 template <class Dec, int TM, int STAGES>
@@ -128,6 +137,22 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (warp >= 2 + 4 * Cfg::kDecGroups) {
+    // the rescale warps pre-bias both accumulator buffers before the first MMA
+    constexpr int kCols = TM / Cfg::kEpiParts;
+    constexpr int kChunk = kCols < 32 ? kCols : 32;
+    const int part = (warp - (2 + 4 * Cfg::kDecGroups)) >> 2;
+    const uint32_t bias_bits = p.group <= 128 ? 0x4B400000u : 0u;
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int c0 = 0; c0 < kCols; c0 += kChunk)
+        tmem_fill_cols<kChunk>(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + b * TM + part * kCols + c0, bias_bits);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   if (warp == 0) {
     if (elect_one()) {
       uint32_t it = 0;
@@ -165,7 +190,6 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         uint32_t b = 0;
-        uint32_t accumulate = 0;
         int gk = 0;  // K position inside the current group (no divisions on this thread's path)
         for (int kst = 0; kst < p.num_k_stages && ok; ++kst, ++it) {
           const int s = it % STAGES;
@@ -176,14 +200,12 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           const uint64_t b_desc = smem_desc_sw128(smem_u32(sx + s * Cfg::kXStageBytes));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            if (gk == 0) {  // first MMA of a group: wait for its accumulator buffer
+            if (gk == 0) {  // first MMA of a group: wait for its (re-biased) accumulator buffer
               b = g_all & 1;
               if (!mbar_wait(&acc_empty[b], ((g_all >> 1) & 1) ^ 1, abort_flag, p.status, 13)) { ok = false; break; }
               tc_fence_after();
-              accumulate = 0;
             }
-            mma_i8_ts(tmem_base + b * TM, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, accumulate);
-            accumulate = 1;
+            mma_i8_ts(tmem_base + b * TM, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, 1u);
             gk += 32;
             if (gk == p.group) {
               tc_commit(&acc_full[b]);
@@ -211,12 +233,12 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       for (int kst = 0; kst < p.num_k_stages; kst += 2) {
         const bool two = kst + 1 < p.num_k_stages;
         const int s0 = it % STAGES, s1 = (it + 1) % STAGES;
-        if (!mbar_wait(&full[s0], (it / STAGES) & 1, abort_flag, p.status, 14)) { ok = false; break; }
+        if (!mbar_wait_sleep(&full[s0], (it / STAGES) & 1, abort_flag, p.status, 14)) { ok = false; break; }
         uint32_t a[32];
         Dec::decode(sw + s0 * kWStage, r, a);
         tmem_st32(tmem_base + lanes + Cfg::kACol0 + s0 * 32, a);
         if (two) {
-          if (!mbar_wait(&full[s1], ((it + 1) / STAGES) & 1, abort_flag, p.status, 14)) { ok = false; break; }
+          if (!mbar_wait_sleep(&full[s1], ((it + 1) / STAGES) & 1, abort_flag, p.status, 14)) { ok = false; break; }
           uint32_t a1[32];
           Dec::decode(sw + s1 * kWStage, r, a1);
           tmem_st32(tmem_base + lanes + Cfg::kACol0 + s1 * 32, a1);
@@ -233,11 +255,17 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     }
   } else {
     // ----------------------------------------------------------------- rescale + epilogue
-    constexpr int kHalf = TM / 2;
-    const int ew = warp - (2 + 4 * Cfg::kDecGroups);  // 0..7
+    constexpr int kCols = TM / Cfg::kEpiParts;  // tokens per rescale warp
+    constexpr int kChunk = kCols < 16 ? kCols : 16;  // columns per TMEM load (register budget)
+    const int ew = warp - (2 + 4 * Cfg::kDecGroups);
     const int quarter = warp & 3;
-    const int half = ew >> 2;
+    const int part = ew >> 2;
     const int r = quarter * 32 + lane;
+    // Pre-bias (groups of <= 128 values, exact magic-number conversion) or zero (larger groups,
+    // converted with cvt) for the int32 accumulators; both buffers were filled before the roles
+    // started.
+    const bool magic = p.group <= 128;
+    const uint32_t bias_bits = magic ? 0x4B400000u : 0u;
     uint32_t g_all = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -245,46 +273,38 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       const int nt = t / p.m_tiles;
       const int n = nt * 128 + r;
       const bool n_ok = n < p.N;
-      float accf[kHalf];
+      float accf[kCols];
 #pragma unroll
-      for (int j = 0; j < kHalf; ++j) accf[j] = 0.f;
+      for (int j = 0; j < kCols; ++j) accf[j] = 0.f;
       const __half* gscale = reinterpret_cast<const __half*>(p.scales) + (size_t)min(n, p.N - 1) * p.groups_per_row;
       float s_next = 0.f;
       if (n_ok) s_next = (p.scale_kind == I8S_GROUP_F16) ? __half2float(gscale[0]) : reinterpret_cast<const float*>(p.scales)[n];
-      // Exact int32 -> fp32 without the conversion unit while |P| < 2^22 (groups of <= 128 values of
-      // 8-bit x 8-bit products): the int32 bits plus the bit pattern of 1.5*2^23, read as a float,
-      // are 1.5*2^23 + P exactly; larger groups use the conversion instruction.
-      const bool magic = p.group <= 128;
       for (int g = 0; g < groups_per_tile; ++g, ++g_all) {
         const float sg = s_next;
         if (n_ok && p.scale_kind == I8S_GROUP_F16 && g + 1 < groups_per_tile) s_next = __half2float(gscale[g + 1]);
         const uint32_t b = g_all & 1;
-        if (!mbar_wait(&acc_full[b], (g_all >> 1) & 1, abort_flag, p.status, 15)) { ok = false; break; }
+        if (!mbar_wait_sleep(&acc_full[b], (g_all >> 1) & 1, abort_flag, p.status, 15)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + b * TM + half * kHalf;
-        if (magic) {
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + b * TM + part * kCols;
 #pragma unroll
-          for (int c0 = 0; c0 < kHalf; c0 += 32) {
-            constexpr int W = kHalf < 32 ? kHalf : 32;
-            uint32_t v[32];
-            if constexpr (W == 32) tmem_ld32(taddr + c0, v);
-            else tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
-            tmem_wait_ld();
+        for (int c0 = 0; c0 < kCols; c0 += kChunk) {
+          uint32_t v[kChunk];
+          tmem_ld_cols<kChunk>(taddr + c0, v);
+          tmem_wait_ld();
+          if (magic) {
 #pragma unroll
-            for (int j = 0; j < W; j += 2)
-              ffma2_sub_magic(sg, __uint_as_float(v[j] + 0x4B400000u), __uint_as_float(v[j + 1] + 0x4B400000u),
-                              accf[c0 + j], accf[c0 + j + 1]);
+            for (int j = 0; j < kChunk; j += 2)
+              ffma2_sub_magic(sg, __uint_as_float(v[j]), __uint_as_float(v[j + 1]), accf[c0 + j], accf[c0 + j + 1]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) accf[c0 + j] = fmaf(sg, (float)(int32_t)v[j], accf[c0 + j]);
           }
-        } else {
+          // re-bias the columns for the buffer's next group, 8 at a time (an x32 store would need
+          // 32 consecutive registers holding the same value)
 #pragma unroll
-          for (int c0 = 0; c0 < kHalf; c0 += 16) {
-            uint32_t v[16];
-            tmem_ld16(taddr + c0, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) accf[c0 + j] = fmaf(sg, (float)(int32_t)v[j], accf[c0 + j]);
-          }
+          for (int j = 0; j < kChunk; j += 8) tmem_fill_cols<8>(taddr + c0 + j, bias_bits);
         }
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -292,13 +312,13 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       if (!ok) break;
       const float bias = n_ok ? load_bias_i8(p.bias, p.bias_kind, n) : 0.f;
 #pragma unroll
-      for (int c0 = 0; c0 < kHalf; c0 += 32) {
-        const int mj = mt * TM + half * kHalf + c0 + lane;
-        const float sx_lane = (mj < p.M) ? __ldg(&p.x_scale[mj]) * p.inv_scale : 0.f;
+      for (int c0 = 0; c0 < kCols; c0 += kChunk) {
+        const int m0 = mt * TM + part * kCols + c0;
+        const float sx_lane = (lane < kChunk && m0 + lane < p.M) ? __ldg(&p.x_scale[m0 + lane]) * p.inv_scale : 0.f;
 #pragma unroll
-        for (int j = 0; j < 32 && c0 + j < kHalf; ++j) {
+        for (int j = 0; j < kChunk; ++j) {
           const float sxm = __shfl_sync(0xffffffffu, sx_lane, j);
-          const int m = mt * TM + half * kHalf + c0 + j;
+          const int m = m0 + j;
           if (n_ok && m < p.M) {
             const float o = __fadd_rn(__fmul_rn(accf[c0 + j], sxm), bias);
             const long long idx = (long long)m * p.ldy + n;

@@ -96,6 +96,40 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or about
+// `hint_ns` nanoseconds pass, instead of spinning on issue slots that other warps need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for the many-warp roles (sleeping waiters), bounded the same way.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                DeviceStatus* status, uint32_t site, uint32_t hint_ns = 2000) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_sleep(a, parity, hint_ns)) return true;
+    if ((i & 7) == 0) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > QLIN_WAIT_TIMEOUT_NS) {
+        *abort = 1;
+        if (status != nullptr && atomicExch(&status->timed_out, 1u) == 0u)
+          status->where = (blockIdx.x << 8) | (site & 0xff);
+        return false;
+      }
+    }
+  }
+}
+
 // Waits for the phase with the given parity to complete.  Returns false (and raises *abort)
 // when the wait exceeds the timeout or another warp of the CTA already aborted.
 template <bool kCluster = false>
@@ -308,6 +342,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+// N (8, 16 or 32) consecutive columns of the warp's lane quarter.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 8 || N == 16 || N == 32, "tcgen05.ld widths used here");
+  if constexpr (N == 32) tmem_ld32(taddr, r);
+  else if constexpr (N == 16) tmem_ld16(taddr, r);
+  else tmem_ld8(taddr, r);
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -327,6 +382,30 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
+}
+
+// N (8, 16 or 32) consecutive columns of the warp's lane quarter all set to one value.
+template <int N>
+__device__ __forceinline__ void tmem_fill_cols(uint32_t taddr, uint32_t v) {
+  static_assert(N == 8 || N == 16 || N == 32, "tcgen05.st widths used here");
+  if constexpr (N == 32) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+                 "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v) : "memory");
+  } else if constexpr (N == 16) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};"
+                 ::"r"(taddr), "r"(v) : "memory");
+  } else {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
+                 : "memory");
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[N]) {
+  static_assert(N == 8 || N == 16 || N == 32, "tcgen05.st widths used here");
+  if constexpr (N == 32) tmem_st32(taddr, r);
+  else if constexpr (N == 16) tmem_st16(taddr, r);
+  else tmem_st8(taddr, r);
 }
 
 // ---------------------------------------------------------------------------------------------
