@@ -82,8 +82,7 @@ struct F16Cfg {
   static constexpr int kASlotsMax = (512 - kAccBufs * TM) / 32;
   static constexpr int kASlots = STAGES < kASlotsMax ? STAGES : (kASlotsMax < 8 ? kASlotsMax : 8);
   static constexpr uint32_t kTmemCols = 512;
-  static_assert(kASlots >= 2 && kASlots % 2 == 0, "decoded-weight slots are released in pairs");
-  static_assert(STAGES >= 2 && STAGES % 2 == 0, "shared-memory stages are released in pairs");
+  static_assert(kASlots >= 2, "at least two decoded-weight slots");
 };
 
 __device__ __forceinline__ float load_bias(const void* bias, int kind, int n) {
@@ -121,13 +120,9 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
   uint8_t* sw = sx + STAGES * Cfg::kXStageBytes;      // STAGES x kWStage
   uint64_t* bars = reinterpret_cast<uint64_t*>(sw + STAGES * kWStage);
   uint64_t* full = bars;                    // [STAGES] X + W landed
-  // Stages and TMEM slots are released in pairs (ring iterations 2j, 2j+1): every commit that
-  // another role waits on costs the tensor pipe a round trip, so the MMA issuer commits one
-  // release per two stages, on the barrier of the pair's even member (the odd members' barriers
-  // are unused); the producer and the decoders wait on that barrier for both stages.
-  uint64_t* empty = full + STAGES;          // [STAGES] (even entries) MMAs that read the stage pair completed
+  uint64_t* empty = full + STAGES;          // [STAGES] MMAs that read the stage completed
   uint64_t* a_full = empty + STAGES;        // [kASlots] decoded weights written to TMEM
-  uint64_t* a_empty = a_full + Cfg::kASlots;  // [kASlots] (even entries) MMAs that read the slot pair completed
+  uint64_t* a_empty = a_full + Cfg::kASlots;  // [kASlots] MMAs that read the slot completed
   uint64_t* acc_full = a_empty + Cfg::kASlots;  // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint64_t* drain = acc_empty + 2;          // [1]
@@ -223,7 +218,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         for (int kst = s0; kst < s_main; ++kst, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if ((it & 1) == 0 && !mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes + Dec::kStageBytes);
           {
             const int k0 = kst * 64;
@@ -241,7 +236,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         for (int kst = max(s0, p.main_k_stages); kst < s1 && ok; ++kst, ++it) {  // LoRA: T' only
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if ((it & 1) == 0 && !mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes);
           tma_load_2d(sx + s * Cfg::kXStageBytes, &tmap_t, &full[s], (kst - p.main_k_stages) * 64,
                       mt * TM + (int)rank * Cfg::kXRows);
@@ -273,14 +268,6 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         if (!mbar_wait(&acc_empty[b], aph ^ 1, abort_flag, p.status, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * Cfg::kAccCols;
-        // Release after the odd member of each pair (pairs may straddle tiles: nothing waits on a
-        // pair before both of its stages were issued, since both rings are at least two deep).
-        auto release = [&](int s, int as) {
-          if (it & 1) {
-            commit_all(&empty[s - 1]);
-            commit_all(&a_empty[as - 1]);
-          }
-        };
         const int s_main = min(s1, p.main_k_stages);
         for (int kst = s0; kst < s_main; ++kst, ++it) {
           const int s = it % STAGES;
@@ -295,7 +282,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             if constexpr (PAIR) mma_f16_ts_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc_main, acc);
             else mma_f16_ts(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc_main, acc);
           }
-          release(s, as);
+          commit_all(&empty[s]);
+          commit_all(&a_empty[as]);
         }
         for (int kst = max(s0, p.main_k_stages); kst < s1 && ok; ++kst, ++it) {  // LoRA: bf16 operands
           const int s = it % STAGES;
@@ -310,7 +298,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             if constexpr (PAIR) mma_f16_ts_pair(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc_lora, acc);
             else mma_f16_ts(d_tmem, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc_lora, acc);
           }
-          release(s, as);
+          commit_all(&empty[s]);
+          commit_all(&a_empty[as]);
         }
         if (!ok) break;
         commit_all(&acc_full[b]);
@@ -348,7 +337,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         Dec::decode(sw + s * kWStage, r, rscale, a);
         // the slot's previous weights have been consumed by their MMAs
         const int as = it % Cfg::kASlots;
-        if (!mbar_wait(&a_empty[as & ~1], ((it / Cfg::kASlots) & 1) ^ 1, abort_flag, p.status, 8)) { ok = false; break; }
+        if (!mbar_wait(&a_empty[as], ((it / Cfg::kASlots) & 1) ^ 1, abort_flag, p.status, 8)) { ok = false; break; }
         tc_fence_after();
         tmem_st32(tmem_base + ((uint32_t)(quarter * 32) << 16) + Cfg::kACol0 + as * 32, a);
         tmem_wait_st();
@@ -369,7 +358,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           a[4 * j] = v.x; a[4 * j + 1] = v.y; a[4 * j + 2] = v.z; a[4 * j + 3] = v.w;
         }
         const int as = it % Cfg::kASlots;
-        if (!mbar_wait(&a_empty[as & ~1], ((it / Cfg::kASlots) & 1) ^ 1, abort_flag, p.status, 8)) { ok = false; break; }
+        if (!mbar_wait(&a_empty[as], ((it / Cfg::kASlots) & 1) ^ 1, abort_flag, p.status, 8)) { ok = false; break; }
         tc_fence_after();
         tmem_st32(tmem_base + ((uint32_t)(quarter * 32) << 16) + Cfg::kACol0 + as * 32, a);
         tmem_wait_st();
@@ -551,7 +540,7 @@ template <class Dec, int TM, bool PAIR>
 constexpr int qgemm_f16_stages() {
   constexpr int kWStage = (Dec::kStageBytes + 1023) / 1024 * 1024;
   constexpr int fit = (232448 - 1024 - 1024 - 2 * 16384) / ((PAIR ? TM / 2 : TM) * 128 + kWStage);
-  return (fit < 8 ? fit : 8) & ~1;  // even: stages are released in pairs
+  return fit < 8 ? fit : 8;
 }
 
 }  // namespace qlin
