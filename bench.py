@@ -35,6 +35,7 @@ import torch  # noqa: E402
 
 M, K, N = 4096, 3072, 12288
 GROUP = 128
+REF_BUDGET_S = 150.0  # reference arm: bound on the host-side run (warm-up + timed steps), seconds
 FLOPS = 2.0 * M * K * N
 METRIC = "quantized-linear TFLOP/s and % roofline at M=4096,K=3072,N=12288 per format"
 
@@ -158,6 +159,10 @@ def cpu_baseline(steps=2, rows=M):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the CPU path timed on the host cores for exactly `--steps` steps after
+    `--warmup` untimed ones.  A step covers all M token rows unless that would make the run longer
+    than REF_BUDGET_S; then every step (warm-up and timed alike) covers the same smaller row sample,
+    a multiple of 256 rows, sized from the first full-size step's time."""
     if rank != 0:
         return
     steps, warm = max(1, args.steps), max(0, args.warmup)
@@ -165,23 +170,32 @@ def run_reference(args, rank, world):
     from oracle import qlin_oracle as O
     x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=0)
     rows = M
-    for _ in range(min(warm, 1)):
+    done_warm = 0
+    if warm > 0:
+        t0 = time.perf_counter()
+        cpu_reference_step(x, q, s, b, rows)
+        t_full = time.perf_counter() - t0
+        done_warm = 1
+        left = warm - 1 + steps
+        if left * t_full > REF_BUDGET_S:
+            rows = max(256, min(M, int(M * REF_BUDGET_S / (left * t_full)) // 256 * 256))
+    for _ in range(warm - done_warm):
         cpu_reference_step(x, q, s, b, rows)
     times = []
-    for _ in range(min(steps, 3)):
+    for _ in range(steps):
         t0 = time.perf_counter()
         cpu_reference_step(x, q, s, b, rows)
         times.append(time.perf_counter() - t0)
     dt = statistics.mean(times)
     value = 2.0 * rows * K * N / dt / 1e12
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
-            "steps": len(times), "warmup": min(warm, 1), "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "int8_convrot_linear M=4096 K=3072 N=12288 group=128 fp16 out",
                        "format": "int8_convrot", "sample_rows": rows, "l2": "n/a (host)"},
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"{len(times)} full steps ({rows} of {M} token rows); weight dequantized per step; "
-                                       f"fp32 torch"},
+                             "sample": f"{steps} timed steps of {rows} of {M} token rows; weight dequantized "
+                                       f"(q*s, rotate) per step; fp32 torch"},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
