@@ -622,12 +622,15 @@ __device__ __forceinline__ void put_u32(uint8_t* p, uint32_t v) {
 
 // A run of 32 IQ4 codes (ggml order: byte i holds value i in its low nibble, value i+16 in its
 // high nibble) -> 4 words in selector order: word t = codes of values 4t..4t+3 in bits 0-15 and
-// 16+4t..16+4t+3 in bits 16-31, value 4t+k in nibble k.
+// 16+4t..16+4t+3 in bits 16-31, value 4t+k in nibble k, each code with its bits 2 and 3 swapped
+// (the two-permute level lookup of the decoder relies on it).
+__device__ __forceinline__ uint32_t iq4_swap23(uint32_t c) { return (c & 3u) | ((c & 4u) << 1) | ((c & 8u) >> 1); }
+
 __device__ __forceinline__ void iq4_selector_order(const uint8_t* qs, uint8_t* out) {
   for (int t = 0; t < 4; ++t) {
     uint32_t w = 0;
     for (int k = 0; k < 4; ++k)
-      w |= ((uint32_t)(qs[4 * t + k] & 0xF) << (4 * k)) | ((uint32_t)(qs[4 * t + k] >> 4) << (16 + 4 * k));
+      w |= (iq4_swap23(qs[4 * t + k] & 0xFu) << (4 * k)) | (iq4_swap23((uint32_t)qs[4 * t + k] >> 4) << (16 + 4 * k));
     put_u32(out + 4 * t, w);
   }
 }

@@ -11,7 +11,8 @@
 //     Q8_0   P=4 (qs of two blocks)                     S=4 (d0, d1 fp16)
 //     Q4_0   P=2 (qs of two blocks, ggml nibble order)   S=4 (d0, d1 fp16)
 //     IQ4_NL P=2 (two runs of 32 in "selector order": word t of a run holds the nibbles of values
-//            4t..4t+3 in bits 0-15 and 16+4t..16+4t+3 in bits 16-31, value 4t+k in nibble k)
+//            4t..4t+3 in bits 0-15 and 16+4t..16+4t+3 in bits 16-31, value 4t+k in nibble k;
+//            each code with its bits 2 and 3 swapped)
 //                                                       S=4 (d0, d1 fp16)
 //     Q4_K   P=2 (the 32-byte qs chunk of sub-blocks 2c, 2c+1)  S=8 (d, dmin fp16, sc0, sc1, m0, m1 u8)
 //     Q6_K   P=4 (one byte per value: the unsigned 6-bit code)  S=8 (sc0..sc3 int8, d fp16, pad)
@@ -198,15 +199,18 @@ struct DecQ4_0 : PlaneStage<2, 4> {
 };
 
 // The IQ4 non-linear levels (gguf/quants.py:1331) of four 4-bit codes -> two exact fp16 pairs.
-// f holds the codes of four consecutive values in its nibbles 0-3 ("selector order", written by
-// the repack).  Two prmt lookups over the levels + 128 as bytes (codes 0-7, 8-15), a third picks
-// per byte by bit 3 of the code, and the bytes go under the 0x64 magic byte: (1024 + L + 128) -
-// 1152 = L exactly.
-__device__ __forceinline__ void iq4_levels_f16(uint32_t f, uint32_t& lo, uint32_t& hi) {
-  const uint32_t sel = f & 0x7777u;
-  const uint32_t l = prmt(0x3F2D1801u, 0x766A5D4Fu, sel);  // -127 -104 -83 -65 -49 -35 -22 -10, + 128
-  const uint32_t h = prmt(0xA6998D81u, 0xF1D9C5B5u, sel);  // 1 13 25 38 53 69 89 113, + 128
-  const uint32_t v = prmt(l, h, ((f >> 1) & 0x4444u) | 0x3210u);
+// f holds four codes in its nibbles 0-3 ("selector order", written by the repack), each with its
+// bits 2 and 3 swapped: stored code s stands for level L(swap(s)).  The levels + 128 as bytes
+// (B = L + 128, 1..241) are looked up with two byte permutes:
+//   lookup A (selectors s): s < 8 picks A[s] = B(swap(s)); s >= 8 replicates the sign bit of
+//     A[s & 7], which is 0 for s = 8..11 and 1 for s = 12..15 (A[0..3] < 128 <= A[4..7]);
+//   lookup H (selectors s ^ 8): s >= 8 picks H[s & 7] = B(swap(s)) ^ (that replicated byte);
+//     s < 8 replicates the sign bit of H[s], and every H entry is below 128, so 0.
+// A ^ H is B(swap(s)) for every s: the swap pairs codes j and j + 8 whose levels have the same
+// sign, which is what keeps all of H below 128.  The bytes then go under the 0x64 magic byte:
+// (1024 + L + 128) - 1152 = L exactly.
+__device__ __forceinline__ void iq4_levels_f16(uint32_t f, uint32_t fx, uint32_t& lo, uint32_t& hi) {
+  const uint32_t v = prmt(0x3F2D1801u, 0xA6998D81u, f) ^ prmt(0x766A5D4Fu, 0x0E263A4Au, fx);  // fx = f ^ 0x8888
   const uint32_t bias = 0x64806480u;  // fp16 (1152, 1152)
   lo = hsub2_u32(prmt(v, 0x64646464u, 0x5140u), bias);
   hi = hsub2_u32(prmt(v, 0x64646464u, 0x7362u), bias);
@@ -234,8 +238,9 @@ struct DecIQ4 : PlaneStage<2, 4> {
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         uint32_t a0, a1, b0, b1;
-        iq4_levels_f16(w[t], a0, a1);        // values 4t .. 4t+3
-        iq4_levels_f16(w[t] >> 16, b0, b1);  // values 16+4t .. 16+4t+3
+        const uint32_t wx = w[t] ^ 0x88888888u;
+        iq4_levels_f16(w[t], wx, a0, a1);              // values 4t .. 4t+3
+        iq4_levels_f16(w[t] >> 16, wx >> 16, b0, b1);  // values 16+4t .. 16+4t+3
         out[16 * blk + 2 * t + 0] = hmul2_u32(a0, d);
         out[16 * blk + 2 * t + 1] = hmul2_u32(a1, d);
         out[16 * blk + 8 + 2 * t + 0] = hmul2_u32(b0, d);

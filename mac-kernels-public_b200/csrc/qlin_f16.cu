@@ -204,7 +204,7 @@ static bool use_pair(int tm, int n_tiles) {
 // codebook lookups ~25%).
 static double fmt_stage_cost(int fmt) {
   switch (fmt) {
-    case WF_IQ4_NL: case WF_IQ4_XS: return 1.25;
+    case WF_IQ4_NL: case WF_IQ4_XS: return 1.12;
     case WF_Q5_0: case WF_Q5_1: case WF_Q5_K: case WF_Q3_K: return 1.04;
     case WF_Q2_K: case WF_Q8_0: case WF_Q6_K: return 1.02;
     default: return 1.0;

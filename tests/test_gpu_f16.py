@@ -68,6 +68,32 @@ def test_gguf_repack_row_exponents(qlin, qtype):
     assert np.all(got[n:] == 0)
 
 
+EXACT_DECODE = (2, 6, 8, 20)  # Q4_0, Q5_0, Q8_0, IQ4_NL: RN16(w * 2^-e), one rounding
+
+
+@pytest.mark.parametrize("qtype", ALL_TYPES)
+def test_gguf_decoded_weights_through_the_linear(qlin, qtype):
+    """One-hot activation rows pull single decoded weights through the linear (fp32 output, no
+    bias; adding zeros is exact): the identity over all K columns runs the tensor-core GEMM, two
+    rows run the small-M kernel.  Types decoded with one rounding must give RN16(w * 2^-e) * 2^e
+    bit for bit; the others stay within two fp16 rounding steps at the row's largest weight."""
+    n, k = 256, 512
+    raw = O.random_gguf_blocks(qtype, n, k, seed=70 + qtype)
+    wn, e = O.gguf_normalized_fp16(raw, qtype, n, k)
+    exact = np.ldexp(wn.astype(np.float32), e.reshape(-1, 1)).T  # [k, n]
+    w = O.gguf_dequantize(raw, qtype, n, k).T
+    raw_d = torch.from_numpy(raw).cuda()
+    eye = torch.eye(k, dtype=torch.float16)
+    for rows in (slice(0, k), slice(37, 39)):
+        y = qlin.gguf_linear(eye[rows].cuda(), raw_d, qtype, (n, k), out_dtype=torch.float32).cpu().numpy()
+        if qtype in EXACT_DECODE:
+            assert np.array_equal(y, exact[rows]), qtype  # equal values (+0 and -0 alike)
+        else:
+            tol = np.abs(w).max(axis=0) * 2.0 ** -9
+            assert np.all(np.abs(y - w[rows]) <= tol), (qtype, np.abs(y - w[rows]).max())
+    _check_status(qlin)
+
+
 def _gguf_case(qtype, m, n, k, seed, x_dtype=torch.float16, bias=True, scale=None):
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(m, k, generator=g).to(x_dtype)
