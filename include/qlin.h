@@ -80,6 +80,30 @@ int qlin_int8_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int6
                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Input gradient of the INT8 ConvRot linear for a frozen weight: dx = dy . W, where
+ * W = (q * scale) un-rotated per block (W = W_rot . H; H symmetric, the forward's rotation).
+ * Replaces comfy-kitchen's MPS `int8_linear_grad_input(dy, q, s, convrot, convrot_groupsize,
+ * out_dtype)` (call sites bench/bench_int8_backward.py:52, bench/probe_packed_backward_real_k.py:151
+ * in the reference; its W4A8 twin `w4a8_linear_grad_input` runs on the kitchen layout's int8 grid).
+ *
+ * qlin_int8_grad_weight writes, once per weight, the transposed copy the gradient GEMM reads:
+ * qt int8 [k, roundup(n, 64)] (zeros past column n), qlin_int8_grad_weight_bytes(n, k) bytes,
+ * 16-byte aligned.  qlin_int8_linear_grad_input then runs dy * scale (per column) normalized to
+ * fp16 per row, the tensor-core GEMM over n, and, when rotate_group != 0, the block Hadamard of
+ * every row of dx (computed in fp32, rounded once to dx's dtype).
+ *   dy  [m, n] with row pitch lddy (f16 / bf16 / f32); scale [n] (f16 / f32)
+ *   dx  [m, k] with row pitch lddx (f16 / bf16 / f32); k % 16 == 0 (and % rotate_group)
+ * n == 0 writes zeros.  The workspace holds the fp16 operand, split-K partials and, with a
+ * rotation, the fp32 dx before it.
+ * ------------------------------------------------------------------------------------------ */
+size_t qlin_int8_grad_weight_bytes(int64_t n, int64_t k);
+int qlin_int8_grad_weight(const int8_t* q, int64_t n, int64_t k, int8_t* qt, size_t qt_bytes, void* stream);
+size_t qlin_int8_linear_grad_input_workspace(int64_t m, int64_t n, int64_t k, int rotate_group);
+int qlin_int8_linear_grad_input(const void* dy, int dy_dtype, int64_t m, int64_t n, int64_t lddy, const int8_t* qt,
+                                int64_t k, const void* scale, int scale_dtype, int rotate_group, void* dx,
+                                int dx_dtype, int64_t lddx, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * GGUF block-format linear: the twelve types of the reference's kernel, Q4_0, Q4_1, Q5_0, Q5_1,
  * Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_NL, IQ4_XS (docs/research/2026-10-03-gguf-on-metal.md:59).
  * Replaces comfy-kitchen `gguf_linear(x, weight, qtype, shape, bias, out_dtype)` and its decode

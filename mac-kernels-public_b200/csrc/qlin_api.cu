@@ -336,6 +336,106 @@ int qlin_int8_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int6
                           ldy, workspace, workspace_bytes, stream, &l);
 }
 
+// ------------------------------------------------------------------------ INT8 input gradient
+size_t qlin_int8_grad_weight_bytes(int64_t n, int64_t k) {
+  return n <= 0 || k <= 0 ? 0 : (size_t)k * (size_t)round_up(n, 64);
+}
+
+int qlin_int8_grad_weight(const int8_t* q, int64_t n, int64_t k, int8_t* qt, size_t qt_bytes, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (n <= 0 || k <= 0 || n > 0x7fffffff || k > 0x7fffffff) {
+    set_error("bad sizes n=%lld k=%lld", (long long)n, (long long)k);
+    return QLIN_EINVAL;
+  }
+  if (q == nullptr || qt == nullptr || (reinterpret_cast<uintptr_t>(qt) & 15) || qt_bytes < qlin_int8_grad_weight_bytes(n, k)) {
+    set_error("null or misaligned pointer, or qt smaller than qlin_int8_grad_weight_bytes");
+    return QLIN_EINVAL;
+  }
+  launch_int8_transpose(q, (int)n, (int)k, qt, (int)round_up(n, 64), stream);
+  return check_cuda("int8 transpose launch");
+}
+
+size_t qlin_int8_linear_grad_input_workspace(int64_t m, int64_t n, int64_t k, int rotate_group) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  const int64_t np = round_up(n, 64);
+  size_t b = f16_operand_bytes(m, np) + align256(f16_gemm_partial_bytes((int)m, (int)k, (int)np, WF_INT8, 0, 0));
+  if (rotate_group) b += align256((size_t)m * k * 4);
+  return b;
+}
+
+int qlin_int8_linear_grad_input(const void* dy, int dy_dtype, int64_t m, int64_t n, int64_t lddy, const int8_t* qt,
+                                int64_t k, const void* scale, int scale_dtype, int rotate_group, void* dx,
+                                int dx_dtype, int64_t lddx, void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (m < 0 || n < 0 || k < 0 || lddy < n || lddx < k || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) {
+    set_error("bad sizes m=%lld n=%lld k=%lld lddy=%lld lddx=%lld", (long long)m, (long long)n, (long long)k,
+              (long long)lddy, (long long)lddx);
+    return QLIN_EINVAL;
+  }
+  if (!is_float_dtype(dy_dtype) || out_kind_of(dx_dtype) < 0 || (scale_dtype != QLIN_F16 && scale_dtype != QLIN_F32)) {
+    set_error("unsupported dtype combination");
+    return QLIN_EDECLINE;
+  }
+  if (k % 16 != 0 || !valid_group(rotate_group) || (rotate_group && k % rotate_group)) {
+    set_error("unsupported shape: k=%lld group=%d (k must be a multiple of 16 and of the group)", (long long)k,
+              rotate_group);
+    return QLIN_EDECLINE;
+  }
+  if (m == 0 || k == 0) return QLIN_OK;
+  if (dx == nullptr) {
+    set_error("null dx");
+    return QLIN_EINVAL;
+  }
+  const int esz = dx_dtype == QLIN_F32 ? 4 : 2;
+  if (n == 0) {  // empty contraction: dX = 0
+    if (cudaMemset2DAsync(dx, (size_t)lddx * esz, 0, (size_t)k * esz, (size_t)m, stream) != cudaSuccess)
+      return check_cuda("dx clear");
+    return QLIN_OK;
+  }
+  if (dy == nullptr || qt == nullptr || scale == nullptr || (reinterpret_cast<uintptr_t>(qt) & 15)) {
+    set_error("null or misaligned pointer (qt needs 16-byte alignment)");
+    return QLIN_EINVAL;
+  }
+  const int64_t np = round_up(n, 64);
+  Carver ws{reinterpret_cast<uint8_t*>(workspace), workspace_bytes};
+  void* xr = ws.take((size_t)m * np * 2);
+  int32_t* rexp = reinterpret_cast<int32_t*>(ws.take((size_t)m * 4));
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)k, (int)np, WF_INT8, 0, 0);
+  float* partial = reinterpret_cast<float*>(ws.take(pb));
+  float* unrot = rotate_group ? reinterpret_cast<float*>(ws.take((size_t)m * k * 4)) : nullptr;
+  if (ws.off > ws.cap) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  launch_grad_prologue(dy, dy_dtype, lddy, (int)m, (int)n, (int)np, scale, scale_dtype == QLIN_F16 ? 1 : 0, xr, rexp,
+                       stream);
+  int rc = check_cuda("gradient prologue launch");
+  if (rc) return rc;
+  F16GemmArgs a{};
+  a.fmt = WF_INT8;
+  a.x = xr;
+  a.ldx = np;
+  a.M = (int)m;
+  a.N = (int)k;
+  a.K = (int)np;
+  a.w = qt;
+  a.w_row_exp = nullptr;
+  a.col_scale = nullptr;
+  a.col_scale_kind = CS_NONE;
+  a.x_row_exp = rexp;
+  a.bias = nullptr;
+  a.bias_kind = 0;
+  a.y = rotate_group ? static_cast<void*>(unrot) : dx;
+  a.y_dtype = rotate_group ? (int)OUT_F32 : out_kind_of(dx_dtype);
+  a.ldy = rotate_group ? k : lddx;
+  a.partial = partial;
+  a.partial_bytes = pb;
+  rc = run_f16_gemm(a, stream);
+  if (rc || !rotate_group) return rc;
+  launch_grad_rotate(unrot, (int)m, (int)k, rotate_group, dx, out_kind_of(dx_dtype), lddx, stream);
+  return check_cuda("gradient rotation launch");
+}
+
 // ------------------------------------------------------------------------------------------ GGUF
 int qlin_gguf_repacked_bytes(int qtype, int64_t n, int64_t k, size_t* bytes, int64_t* padded_n) {
   const uint32_t sb = gguf_stage_bytes(qtype, nullptr, nullptr);

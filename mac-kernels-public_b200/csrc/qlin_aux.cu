@@ -1331,4 +1331,129 @@ void launch_lora_operands(const void* t, int t_dtype, long long ldt, int M, cons
                                                                w_row_exp, reinterpret_cast<__nv_bfloat16*>(u_out));
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Input gradient of the weight-only INT8 linear for a frozen weight (comfy-kitchen's
+// int8_linear_grad_input): dX = dY . W with W = (q * s) un-rotated per block, W = W_rot . H (H the
+// symmetric block Hadamard of the forward).  The contraction runs along N, so the GEMM reads a
+// transposed copy of q made once; the per-channel scale s moves onto dY's columns.
+// ---------------------------------------------------------------------------------------------
+
+// q int8 [N, K] -> qt int8 [K, ldt] (ldt a multiple of 64 >= N, zeros in columns N .. ldt-1).
+// grid = (ceil(K / 64), ldt / 64), block = 256: a 64 x 64 byte tile through shared memory.
+__global__ void __launch_bounds__(256) int8_transpose_kernel(const int8_t* __restrict__ q, int N, int K,
+                                                             int8_t* __restrict__ qt, int ldt) {
+  __shared__ uint8_t tile[64][65];  // [n][k]
+  const int k0 = blockIdx.x * 64, n0 = blockIdx.y * 64;
+  const int t = threadIdx.x;
+  {
+    const int r = t >> 2, c = (t & 3) * 16;
+    const int n = n0 + r;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int k = k0 + c + i;
+      tile[r][c + i] = (n < N && k < K) ? (uint8_t)q[(size_t)n * K + k] : 0;
+    }
+  }
+  __syncthreads();
+  const int r = t >> 2, c = (t & 3) * 16;  // output row k0 + r, columns n0 + c .. + 15
+  const int k = k0 + r;
+  if (k >= K) return;
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    w[j] = (uint32_t)tile[c + 4 * j][r] | ((uint32_t)tile[c + 4 * j + 1][r] << 8) |
+           ((uint32_t)tile[c + 4 * j + 2][r] << 16) | ((uint32_t)tile[c + 4 * j + 3][r] << 24);
+  *reinterpret_cast<uint4*>(qt + (size_t)k * ldt + n0 + c) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// dY' = dY * s per column, normalized per row like the forward's activation operand: a power of
+// two 2^f from the row's largest |dY * s| (f = exponent - 15), one rounding to fp16, zeros in
+// columns N .. Np-1.  One CTA per row; the second pass rereads the row (mostly from L2).
+__global__ void __launch_bounds__(256) grad_prologue_kernel(const void* __restrict__ dy, int dy_dtype, long long lddy,
+                                                            int N, int Np, const void* __restrict__ s, int s_f16,
+                                                            __half* __restrict__ out, int32_t* __restrict__ row_exp) {
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  auto value = [&](int c) {
+    const float sc = s_f16 ? __half2float(reinterpret_cast<const __half*>(s)[c]) : reinterpret_cast<const float*>(s)[c];
+    return __fmul_rn(load_x(dy, dy_dtype, (long long)row * lddy + c), sc);
+  };
+  float amax = 0.f;
+  for (int c = threadIdx.x; c < N; c += blockDim.x) amax = fmaxf(amax, fabsf(value(c)));
+  amax = block_max(amax, red);
+  int f = 0;
+  if (amax > 0.f && amax <= 3.402823466e38f) {
+    int ex;
+    frexpf(amax, &ex);
+    f = ex - 15;
+  }
+  if (threadIdx.x == 0) row_exp[row] = f;
+  __half* o = out + (long long)row * Np;
+  for (int c = 2 * threadIdx.x; c < Np; c += 2 * blockDim.x) {
+    const float v0 = c < N ? scale_pow2(value(c), f) : 0.f;
+    const float v1 = c + 1 < N ? scale_pow2(value(c + 1), f) : 0.f;
+    *reinterpret_cast<__half2*>(o + c) = __floats2half2_rn(v0, v1);
+  }
+}
+
+// Rows of dX (fp32 [M, K]) times the block Hadamard, one warp per block of G = 32 * E values,
+// written in the output dtype.
+template <int E>
+__global__ void __launch_bounds__(256) grad_rotate_kernel(const float* __restrict__ in, int M, int K, int kind,
+                                                          void* __restrict__ out, int out_dtype, long long ldo) {
+  constexpr int G = 32 * E;
+  const int nblk = K / G;
+  const long long wg = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wg >= (long long)M * nblk) return;  // uniform per warp
+  const int row = (int)(wg / nblk), b = (int)(wg % nblk);
+  const float* src = in + (size_t)row * K + b * G + lane * E;
+  float v[E];
+  if constexpr (E >= 4) {
+#pragma unroll
+    for (int e = 0; e < E; e += 4) {
+      const float4 t = *reinterpret_cast<const float4*>(src + e);
+      v[e] = t.x; v[e + 1] = t.y; v[e + 2] = t.z; v[e + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = src[e];
+  }
+  block_hadamard<E>(v, kind, lane);
+  const long long o = (long long)row * ldo + b * G + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    if (out_dtype == OUT_F16) reinterpret_cast<__half*>(out)[o + e] = __float2half_rn(v[e]);
+    else if (out_dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(out)[o + e] = __float2bfloat16_rn(v[e]);
+    else reinterpret_cast<float*>(out)[o + e] = v[e];
+  }
+}
+
+void launch_int8_transpose(const int8_t* q, int N, int K, int8_t* qt, int ldt, cudaStream_t s) {
+  if (N == 0 || K == 0) return;
+  int8_transpose_kernel<<<dim3((K + 63) / 64, ldt / 64), 256, 0, s>>>(q, N, K, qt, ldt);
+}
+
+void launch_grad_prologue(const void* dy, int dy_dtype, long long lddy, int M, int N, int Np, const void* scale,
+                          int scale_f16, void* out, int32_t* row_exp, cudaStream_t s) {
+  if (M == 0) return;
+  grad_prologue_kernel<<<M, 256, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, reinterpret_cast<__half*>(out),
+                                         row_exp);
+}
+
+int launch_grad_rotate(const float* in, int M, int K, int group, void* out, int out_dtype, long long ldo,
+                       cudaStream_t s) {
+  if (M == 0 || K == 0) return 0;
+  const long long warps = (long long)M * (K / group);
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  switch (group) {  // the forward prologue's rotation for each group size
+    case 32: grad_rotate_kernel<1><<<blocks, 256, 0, s>>>(in, M, K, 0, out, out_dtype, ldo); return 0;
+    case 64: grad_rotate_kernel<2><<<blocks, 256, 0, s>>>(in, M, K, 1, out, out_dtype, ldo); return 0;
+    case 128: grad_rotate_kernel<4><<<blocks, 256, 0, s>>>(in, M, K, 0, out, out_dtype, ldo); return 0;
+    case 256: grad_rotate_kernel<8><<<blocks, 256, 0, s>>>(in, M, K, 1, out, out_dtype, ldo); return 0;
+    default: return -1;
+  }
+}
+
 }  // namespace qlin

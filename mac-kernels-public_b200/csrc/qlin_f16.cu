@@ -298,6 +298,7 @@ void plan_f16(int M, int N, int K, int fmt, int* tm_out, int* splits_out) {
 }
 
 size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;  // nothing to plan (the callers return before any launch)
   plan_f16(M, N, K, fmt, &tm, &k_splits);
   const size_t mp = (size_t)(M + tm - 1) / tm * tm;
   return k_splits > 1 ? (size_t)k_splits * N * mp * sizeof(float) : 0;

@@ -28,6 +28,13 @@ void launch_lora_operands(const void* t, int t_dtype, long long ldt, int M, cons
                           long long ldu, int N, int n_pad, int R, int rk, float scale, const void* cs, int cs_kind,
                           const int32_t* w_row_exp, const int32_t* x_row_exp, void* t_out, void* u_out,
                           cudaStream_t s);
+// INT8 input gradient (dX = dY . W): the transposed weight copy, dY * s normalized to fp16, and the
+// block Hadamard of dX's rows (group 32, 64, 128 or 256; returns -1 for other groups).
+void launch_int8_transpose(const int8_t* q, int N, int K, int8_t* qt, int ldt, cudaStream_t s);
+void launch_grad_prologue(const void* dy, int dy_dtype, long long lddy, int M, int N, int Np, const void* scale,
+                          int scale_f16, void* out, int32_t* row_exp, cudaStream_t s);
+int launch_grad_rotate(const float* in, int M, int K, int group, void* out, int out_dtype, long long ldo,
+                       cudaStream_t s);
 void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* codebook, int bits, int group, int N,
                          int K, int8_t* out, cudaStream_t s);
 

@@ -6,6 +6,8 @@ Python signatures follow the reference's callers (roblennon/mac-kernels-public):
   dequantize_gguf      docs/upstream/comfy-kitchen-mps-followups.md:43
   w4a8_int8_linear     bench/bench_lora_fused_rank.py:42-44, bench/bench_lora_sidepath_kernel.py:78
   quantize_int8_rowwise  modal/weight_error_app.py:109-115 (activation quantizer of the A8 formats)
+  int8_linear_grad_input, w4a8_linear_grad_input, int8_linear_trainable, w4a8_linear_trainable
+                       bench/bench_int8_backward.py:52,70, bench/probe_packed_backward_real_k.py:151-158
 
 Every op runs the CUDA library (libqlin.so, sm_100a) on the tensors' device and the current
 stream.  There is no CPU or eager fallback: unsupported inputs raise `QlinDecline`
@@ -23,7 +25,8 @@ from ._lib import QlinDecline, QlinError, check, lib
 
 __all__ = ["int8_linear", "int8_linear_streamed", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear", "dequantize_w4a8_int8_weight",
            "quantize_int8_rowwise", "prologue_f16", "repack_gguf", "GGUF_TYPES", "QlinDecline", "QlinError",
-           "device_status"]
+           "device_status", "int8_linear_grad_input", "w4a8_linear_grad_input", "int8_linear_trainable",
+           "w4a8_linear_trainable"]
 
 # ggml type id -> (name, values per block, bytes per block)
 GGUF_TYPES = {2: ("Q4_0", 32, 18), 3: ("Q4_1", 32, 20), 6: ("Q5_0", 32, 22), 7: ("Q5_1", 32, 24),
@@ -369,3 +372,8 @@ def dequantize_w4a8_int8_weight(*args, **kwargs):
     """Kitchen W4A8 / W6A8 decode-only entry point; see _w4a8."""
     from ._w4a8 import dequantize_w4a8_int8_weight as impl
     return impl(*args, **kwargs)
+
+
+# ---------------------------------------------------------------------------------------------- gradients
+from ._grad import (int8_linear_grad_input, int8_linear_trainable, w4a8_linear_grad_input,  # noqa: E402
+                    w4a8_linear_trainable)

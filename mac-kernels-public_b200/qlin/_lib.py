@@ -30,6 +30,10 @@ SIGNATURES = {
     "qlin_int8_linear_lora_workspace": (_sz, [_i64, _i64, _i64, _i64]),
     "qlin_int8_linear_lora": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i, _p, _i, _i, _p, _i, _i64, _p, _i, _i64,
                                    _i64, ctypes.c_float, _p, _i, _i64, _p, _sz, _p]),
+    "qlin_int8_grad_weight_bytes": (_sz, [_i64, _i64]),
+    "qlin_int8_grad_weight": (_i, [_p, _i64, _i64, _p, _sz, _p]),
+    "qlin_int8_linear_grad_input_workspace": (_sz, [_i64, _i64, _i64, _i]),
+    "qlin_int8_linear_grad_input": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i, _i, _p, _i, _i64, _p, _sz, _p]),
     "qlin_gguf_repacked_bytes": (_i, [_i, _i64, _i64, ctypes.POINTER(_sz), ctypes.POINTER(_i64)]),
     "qlin_gguf_repack": (_i, [_p, _i, _i64, _i64, _p, _sz, _p, _i64, _p]),
     "qlin_gguf_linear_workspace": (_sz, [_i64, _i64, _i64, _i, _i64]),

@@ -94,6 +94,16 @@ def rotate_rows(x, group: int, kind: str = "auto"):
 # INT8 row-wise quantizer (weights, and the per-token activation quantizer of the A8 formats)
 # ----------------------------------------------------------------------------------------------
 
+
+def int8_grad_input(dy, q, s, group: int = 0) -> np.ndarray:
+    """dx = dy . W (float64) for the frozen INT8 ConvRot weight: W = (q * s) un-rotated per block,
+    W = W_rot . H, the weight in the original basis as the reference's backward bench builds its
+    exact answer (`bench/bench_int8_backward.py:36-39,53`: `dequant`, then `dy @ W`)."""
+    w = np.asarray(q, dtype=np.float64) * np.asarray(s, dtype=np.float64).reshape(-1, 1)
+    if group:
+        w = rotate_rows(w, group)
+    return np.asarray(dy, dtype=np.float64) @ w
+
 def quantize_int8_rowwise(x: torch.Tensor):
     """Per-row absmax/127 INT8 quantization in x's dtype.
 

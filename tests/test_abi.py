@@ -47,6 +47,12 @@ def test_version_and_host_side_declines_without_gpu():
     assert b"block" in lib.qlin_last_error() or lib.qlin_last_error() == b""
     # workspace queries are pure host arithmetic
     assert lib.qlin_int8_linear_workspace(4096, 12288, 3072) >= 4096 * 3072 * 2
+    # input gradient: transposed weight [k, roundup(n, 64)]; empty problems need no workspace
+    assert lib.qlin_int8_grad_weight_bytes(130, 256) == 256 * 192
+    assert lib.qlin_int8_grad_weight_bytes(0, 256) == 0
+    assert lib.qlin_int8_linear_grad_input_workspace(5, 0, 256, 128) == 0
+    assert lib.qlin_int8_linear_grad_input_workspace(0, 64, 256, 0) == 0
+    assert lib.qlin_int8_linear_grad_input_workspace(64, 100, 256, 128) >= 64 * 128 * 2 + 64 * 256 * 4
 
 
 def test_kitchen_signatures_match_reference_surface():
