@@ -1397,36 +1397,148 @@ __global__ void __launch_bounds__(256) grad_prologue_kernel(const void* __restri
   }
 }
 
-// Rows of dX (fp32 [M, K]) times the block Hadamard, one warp per block of G = 32 * E values,
-// written in the output dtype.
-template <int E>
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // a -> low half
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 8 consecutive values of a 16-byte aligned row (f16 / bf16 / f32) as floats.
+__device__ __forceinline__ void load8(const void* base, int dtype, long long idx, float (&v)[8]) {
+  if (dtype == 0) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    return;
+  }
+  const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + idx);
+  const uint32_t p[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const unsigned short lo = (unsigned short)(p[e] & 0xFFFF), hi = (unsigned short)(p[e] >> 16);
+    v[2 * e] = dtype == 1 ? __half2float(__ushort_as_half(lo)) : __bfloat162float(__ushort_as_bfloat16(lo));
+    v[2 * e + 1] = dtype == 1 ? __half2float(__ushort_as_half(hi)) : __bfloat162float(__ushort_as_bfloat16(hi));
+  }
+}
+
+// The same operand with 16-byte loads and stores: each thread keeps CH chunks of 8 columns in
+// registers between the max pass and the write pass, so dY is read once.  Needs N % 8 == 0,
+// 16-byte aligned rows of dy and s, and CH * blockDim.x * 8 >= Np.
+template <int CH>
+__global__ void __launch_bounds__(512) grad_prologue_vec_kernel(const void* __restrict__ dy, int dy_dtype,
+                                                                long long lddy, int N, int Np,
+                                                                const void* __restrict__ s, int s_f16,
+                                                                __half* __restrict__ out, int32_t* __restrict__ row_exp) {
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  float v[CH][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const int c = (j * (int)blockDim.x + (int)threadIdx.x) * 8;
+    if (c < N) {
+      float sc[8];
+      load8(dy, dy_dtype, (long long)row * lddy + c, v[j]);
+      load8(s, s_f16 ? 1 : 0, c, sc);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[j][e] = __fmul_rn(v[j][e], sc[e]);
+        amax = fmaxf(amax, fabsf(v[j][e]));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+    }
+  }
+  amax = block_max(amax, red);
+  int f = 0;
+  if (amax > 0.f && amax <= 3.402823466e38f) {
+    int ex;
+    frexpf(amax, &ex);
+    f = ex - 15;
+  }
+  if (threadIdx.x == 0) row_exp[row] = f;
+#pragma unroll
+  for (int j = 0; j < CH; ++j) {
+    const int c = (j * (int)blockDim.x + (int)threadIdx.x) * 8;
+    if (c < Np) {
+      uint4 pk;
+      uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pw[e] = pack_f16x2(scale_pow2(v[j][2 * e], f), scale_pow2(v[j][2 * e + 1], f));
+      *reinterpret_cast<uint4*>(out + (long long)row * Np + c) = pk;
+    }
+  }
+}
+
+// Rows of dX (fp32 [M, K]) times the block Hadamard, written in the output dtype: each warp
+// rotates R blocks of G = 32 * E values (all loads issued before the butterflies), lane l holding
+// values l*E .. l*E+E-1 of a block.  `vec`: 16-byte aligned output rows, stored as whole vectors.
+template <int E, int R>
 __global__ void __launch_bounds__(256) grad_rotate_kernel(const float* __restrict__ in, int M, int K, int kind,
-                                                          void* __restrict__ out, int out_dtype, long long ldo) {
+                                                          void* __restrict__ out, int out_dtype, long long ldo,
+                                                          int vec) {
   constexpr int G = 32 * E;
   const int nblk = K / G;
-  const long long wg = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const long long total = (long long)M * nblk;
+  const long long w0 = ((long long)blockIdx.x * 8 + (threadIdx.x >> 5)) * R;
   const int lane = threadIdx.x & 31;
-  if (wg >= (long long)M * nblk) return;  // uniform per warp
-  const int row = (int)(wg / nblk), b = (int)(wg % nblk);
-  const float* src = in + (size_t)row * K + b * G + lane * E;
-  float v[E];
-  if constexpr (E >= 4) {
+  if (w0 >= total) return;  // uniform per warp
+  float v[R][E];
 #pragma unroll
-    for (int e = 0; e < E; e += 4) {
-      const float4 t = *reinterpret_cast<const float4*>(src + e);
-      v[e] = t.x; v[e + 1] = t.y; v[e + 2] = t.z; v[e + 3] = t.w;
+  for (int r = 0; r < R; ++r) {
+    const long long wg = w0 + r;
+    if (wg < total) {
+      const float* src = in + (size_t)(wg / nblk) * K + (int)(wg % nblk) * G + lane * E;
+      if constexpr (E >= 4) {
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+          const float4 t = *reinterpret_cast<const float4*>(src + e);
+          v[r][e] = t.x; v[r][e + 1] = t.y; v[r][e + 2] = t.z; v[r][e + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[r][e] = src[e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[r][e] = 0.f;
     }
-  } else {
-#pragma unroll
-    for (int e = 0; e < E; ++e) v[e] = src[e];
   }
-  block_hadamard<E>(v, kind, lane);
-  const long long o = (long long)row * ldo + b * G + lane * E;
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    if (out_dtype == OUT_F16) reinterpret_cast<__half*>(out)[o + e] = __float2half_rn(v[e]);
-    else if (out_dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(out)[o + e] = __float2bfloat16_rn(v[e]);
-    else reinterpret_cast<float*>(out)[o + e] = v[e];
+  for (int r = 0; r < R; ++r) block_hadamard<E>(v[r], kind, lane);  // every lane joins the shuffles
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const long long wg = w0 + r;
+    if (wg >= total) break;
+    const long long o = (long long)(wg / nblk) * ldo + (int)(wg % nblk) * G + lane * E;
+    bool done = false;
+    if constexpr (E >= 4) {
+      if (vec && out_dtype != OUT_F32) {
+        uint32_t pw[E / 2];
+#pragma unroll
+        for (int e = 0; e < E / 2; ++e)
+          pw[e] = out_dtype == OUT_F16 ? pack_f16x2(v[r][2 * e], v[r][2 * e + 1])
+                                       : pack_bf16x2(v[r][2 * e], v[r][2 * e + 1]);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(out) + o;
+#pragma unroll
+        for (int e = 0; e < E / 2; e += 2) *reinterpret_cast<uint2*>(dst + 2 * e) = make_uint2(pw[e], pw[e + 1]);
+        done = true;
+      } else if (vec) {
+        float* dst = reinterpret_cast<float*>(out) + o;
+#pragma unroll
+        for (int e = 0; e < E; e += 4)
+          *reinterpret_cast<float4*>(dst + e) = make_float4(v[r][e], v[r][e + 1], v[r][e + 2], v[r][e + 3]);
+        done = true;
+      }
+    }
+    if (!done) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if (out_dtype == OUT_F16) reinterpret_cast<__half*>(out)[o + e] = __float2half_rn(v[r][e]);
+        else if (out_dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(out)[o + e] = __float2bfloat16_rn(v[r][e]);
+        else reinterpret_cast<float*>(out)[o + e] = v[r][e];
+      }
+    }
   }
 }
 
@@ -1438,20 +1550,33 @@ void launch_int8_transpose(const int8_t* q, int N, int K, int8_t* qt, int ldt, c
 void launch_grad_prologue(const void* dy, int dy_dtype, long long lddy, int M, int N, int Np, const void* scale,
                           int scale_f16, void* out, int32_t* row_exp, cudaStream_t s) {
   if (M == 0) return;
-  grad_prologue_kernel<<<M, 256, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, reinterpret_cast<__half*>(out),
-                                         row_exp);
+  const int esz = dy_dtype == 0 ? 4 : 2;
+  const bool vec = N % 8 == 0 && ((reinterpret_cast<uintptr_t>(dy) | (uintptr_t)(lddy * esz)) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(scale) & 15) == 0;
+  __half* o = reinterpret_cast<__half*>(out);
+  if (vec) {
+    const int chunks = (Np + 512 * 8 - 1) / (512 * 8);
+    if (chunks <= 1) return (void)grad_prologue_vec_kernel<1><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
+    if (chunks <= 2) return (void)grad_prologue_vec_kernel<2><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
+    if (chunks <= 4) return (void)grad_prologue_vec_kernel<4><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
+    if (chunks <= 8) return (void)grad_prologue_vec_kernel<8><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
+  }
+  grad_prologue_kernel<<<M, 256, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
 }
 
 int launch_grad_rotate(const float* in, int M, int K, int group, void* out, int out_dtype, long long ldo,
                        cudaStream_t s) {
   if (M == 0 || K == 0) return 0;
-  const long long warps = (long long)M * (K / group);
+  constexpr int R = 4;  // blocks per warp
+  const long long warps = ((long long)M * (K / group) + R - 1) / R;
   const unsigned blocks = (unsigned)((warps + 7) / 8);
+  const int esz = out_dtype == OUT_F32 ? 4 : 2;
+  const int vec = ((reinterpret_cast<uintptr_t>(out) | (uintptr_t)(ldo * esz)) & 15) == 0 ? 1 : 0;
   switch (group) {  // the forward prologue's rotation for each group size
-    case 32: grad_rotate_kernel<1><<<blocks, 256, 0, s>>>(in, M, K, 0, out, out_dtype, ldo); return 0;
-    case 64: grad_rotate_kernel<2><<<blocks, 256, 0, s>>>(in, M, K, 1, out, out_dtype, ldo); return 0;
-    case 128: grad_rotate_kernel<4><<<blocks, 256, 0, s>>>(in, M, K, 0, out, out_dtype, ldo); return 0;
-    case 256: grad_rotate_kernel<8><<<blocks, 256, 0, s>>>(in, M, K, 1, out, out_dtype, ldo); return 0;
+    case 32: grad_rotate_kernel<1, R><<<blocks, 256, 0, s>>>(in, M, K, 0, out, out_dtype, ldo, vec); return 0;
+    case 64: grad_rotate_kernel<2, R><<<blocks, 256, 0, s>>>(in, M, K, 1, out, out_dtype, ldo, vec); return 0;
+    case 128: grad_rotate_kernel<4, R><<<blocks, 256, 0, s>>>(in, M, K, 0, out, out_dtype, ldo, vec); return 0;
+    case 256: grad_rotate_kernel<8, R><<<blocks, 256, 0, s>>>(in, M, K, 1, out, out_dtype, ldo, vec); return 0;
     default: return -1;
   }
 }
