@@ -448,6 +448,15 @@ def run_ours(args, rank, world):
         t = statistics.mean(timed_steps(fn, max(3, args.steps // 2), args.warmup, flush, stream))
         formats["int8_convrot_g128_lora_r128_fused"] = {"tflops": FLOPS / (t * 1e-3) / 1e12, "ms": t,
                                                          "overhead_vs_no_lora": t / ms - 1.0}
+        # input gradient of the same frozen weight: dy [M, N] fp16 -> dx [M, K] (the transposed
+        # weight copy is made once, before timing, as a training loop would)
+        dy = torch.randn(M, N, generator=gl).half().to(dev)
+        qlin.int8_linear_grad_input(dy, qd, sd, True, GROUP)
+        fn = lambda: qlin.int8_linear_grad_input(dy, qd, sd, True, GROUP)  # noqa: E731
+        t = statistics.mean(timed_steps(fn, max(3, args.steps // 2), args.warmup, flush, stream))
+        formats["int8_convrot_g128_grad_input"] = {"tflops": FLOPS / (t * 1e-3) / 1e12, "ms": t,
+                                                    "vs_forward_time": t / ms,
+                                                    "note": "dx = dy . W, dy fp16 [4096, 12288] -> dx fp16 [4096, 3072]"}
 
     mmdit = None
     if not args.no_mmdit:

@@ -5,6 +5,7 @@
 Synthetic seeded inputs with the configurations' shapes and value distributions:
   cfg1_q8_0 / cfg1_q4_0   GGUF Q8_0 / Q4_0 linear, X fp16 [256, 3072], W [3072, 3072]
   cfg2                    INT8 ConvRot weight-only linear, X [4096, 3072], W [12288, 3072], H-128
+  cfg2_grad               its input gradient: dY fp16 [4096, 12288] -> dX [4096, 3072], H-128
   cfg3                    W4A8, X [4096, 12288], W 4-bit [3072, 12288], group 128
   cfg4_fwd / cfg4_rev     W6A8, X [3240, 5120] / [3240, 13824], W 6-bit, group 64
   cfg5_q4k / cfg5_q6k     MMDiT-block GGUF linears, X [4608, 3072] / [4608, 12288]
@@ -48,6 +49,13 @@ def build(name, dev):
         s = (torch.randn(n, generator=gen).abs() * 0.02 / 127).to(torch.float16).to(dev)
         b = (torch.randn(n, generator=gen) * 0.01).to(torch.float16).to(dev)
         return (lambda: qlin.int8_linear(x, q, s, b, torch.float16, convrot=True, convrot_groupsize=128)), 2.0 * m * k * n
+    if name == "cfg2_grad":
+        m, k, n = 4096, 3072, 12288
+        q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int32).to(torch.int8).to(dev)
+        s = (torch.randn(n, generator=gen).abs() * 0.02 / 127).to(torch.float16).to(dev)
+        dy = torch.randn(m, n, generator=gen).to(torch.float16).to(dev)
+        qlin.int8_linear_grad_input(dy, q, s, True, 128)  # the one-time transposed weight copy
+        return (lambda: qlin.int8_linear_grad_input(dy, q, s, True, 128)), 2.0 * m * k * n
     m, k, n, bits, grp = {"cfg3": (4096, 12288, 3072, 4, 128), "cfg4_fwd": (3240, 5120, 13824, 6, 64),
                           "cfg4_rev": (3240, 13824, 5120, 6, 64)}[name]
     x = torch.randn(m, k, generator=gen).to(torch.float16).to(dev)
