@@ -1421,32 +1421,54 @@ __device__ __forceinline__ void load8(const void* base, int dtype, long long idx
 }
 
 // The same operand with 16-byte loads and stores: each thread keeps CH chunks of 8 columns in
-// registers between the max pass and the write pass, so dY is read once.  Needs N % 8 == 0,
-// 16-byte aligned rows of dy and s, and CH * blockDim.x * 8 >= Np.
-template <int CH>
+// registers between the max pass and the write pass, so dY is read once; 16-bit inputs are kept
+// as loaded (4 registers a chunk) and the products dY * s recomputed in the write pass, the same
+// fp32 products as in the max pass.  Needs N % 8 == 0, 16-byte aligned rows of dy and s, and
+// CH * blockDim.x * 8 >= Np.
+template <int CH, bool F32>
 __global__ void __launch_bounds__(512) grad_prologue_vec_kernel(const void* __restrict__ dy, int dy_dtype,
                                                                 long long lddy, int N, int Np,
                                                                 const void* __restrict__ s, int s_f16,
                                                                 __half* __restrict__ out, int32_t* __restrict__ row_exp) {
   __shared__ float red[33];
   const int row = blockIdx.x;
-  float v[CH][8];
+  constexpr int W = F32 ? 8 : 4;  // registers a chunk
+  uint32_t raw[CH][W];
+  auto products = [&](int j, int c, float (&v)[8]) {
+    if constexpr (F32) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(raw[j][e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const unsigned short lo = (unsigned short)(raw[j][e] & 0xFFFF), hi = (unsigned short)(raw[j][e] >> 16);
+        v[2 * e] = dy_dtype == 1 ? __half2float(__ushort_as_half(lo)) : __bfloat162float(__ushort_as_bfloat16(lo));
+        v[2 * e + 1] = dy_dtype == 1 ? __half2float(__ushort_as_half(hi)) : __bfloat162float(__ushort_as_bfloat16(hi));
+      }
+    }
+    float sc[8];
+    load8(s, s_f16 ? 1 : 0, c, sc);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], sc[e]);
+  };
   float amax = 0.f;
 #pragma unroll
   for (int j = 0; j < CH; ++j) {
     const int c = (j * (int)blockDim.x + (int)threadIdx.x) * 8;
     if (c < N) {
-      float sc[8];
-      load8(dy, dy_dtype, (long long)row * lddy + c, v[j]);
-      load8(s, s_f16 ? 1 : 0, c, sc);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        v[j][e] = __fmul_rn(v[j][e], sc[e]);
-        amax = fmaxf(amax, fabsf(v[j][e]));
+      if constexpr (F32) {
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(dy) + (long long)row * lddy + c);
+        const uint4 a = src[0], b = src[1];
+        raw[j][0] = a.x; raw[j][1] = a.y; raw[j][2] = a.z; raw[j][3] = a.w;
+        raw[j][4] = b.x; raw[j][5] = b.y; raw[j][6] = b.z; raw[j][7] = b.w;
+      } else {
+        const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(dy) + (long long)row * lddy + c);
+        raw[j][0] = a.x; raw[j][1] = a.y; raw[j][2] = a.z; raw[j][3] = a.w;
       }
-    } else {
+      float v[8];
+      products(j, c, v);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
     }
   }
   amax = block_max(amax, red);
@@ -1461,10 +1483,12 @@ __global__ void __launch_bounds__(512) grad_prologue_vec_kernel(const void* __re
   for (int j = 0; j < CH; ++j) {
     const int c = (j * (int)blockDim.x + (int)threadIdx.x) * 8;
     if (c < Np) {
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (c < N) products(j, c, v);
       uint4 pk;
       uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) pw[e] = pack_f16x2(scale_pow2(v[j][2 * e], f), scale_pow2(v[j][2 * e + 1], f));
+      for (int e = 0; e < 4; ++e) pw[e] = pack_f16x2(scale_pow2(v[2 * e], f), scale_pow2(v[2 * e + 1], f));
       *reinterpret_cast<uint4*>(out + (long long)row * Np + c) = pk;
     }
   }
@@ -1556,10 +1580,17 @@ void launch_grad_prologue(const void* dy, int dy_dtype, long long lddy, int M, i
   __half* o = reinterpret_cast<__half*>(out);
   if (vec) {
     const int chunks = (Np + 512 * 8 - 1) / (512 * 8);
-    if (chunks <= 1) return (void)grad_prologue_vec_kernel<1><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
-    if (chunks <= 2) return (void)grad_prologue_vec_kernel<2><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
-    if (chunks <= 4) return (void)grad_prologue_vec_kernel<4><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
-    if (chunks <= 8) return (void)grad_prologue_vec_kernel<8><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
+#define QLIN_GRAD_PRO(CH)                                                                                          \
+    if (chunks <= CH) {                                                                                            \
+      if (dy_dtype == 0) grad_prologue_vec_kernel<CH, true><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp); \
+      else grad_prologue_vec_kernel<CH, false><<<M, 512, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp); \
+      return;                                                                                                      \
+    }
+    QLIN_GRAD_PRO(1)
+    QLIN_GRAD_PRO(2)
+    QLIN_GRAD_PRO(4)
+    QLIN_GRAD_PRO(8)
+#undef QLIN_GRAD_PRO
   }
   grad_prologue_kernel<<<M, 256, 0, s>>>(dy, dy_dtype, lddy, N, Np, scale, scale_f16, o, row_exp);
 }
