@@ -35,7 +35,7 @@ def _check_status(qlin):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 200, 256), (2, 64, 512), (37, 300, 512), (300, 1000, 768), (700, 520, 1024)])
-@pytest.mark.parametrize("group", [0, 128, 256])
+@pytest.mark.parametrize("group", [0, 32, 64, 128, 256])
 def test_int8_grad_input_matches_fp64(qlin, m, n, k, group):
     q, s, g = _weights(n, k, seed=m + n + group)
     dy = torch.randn(m, n, generator=g).to(torch.float16)
