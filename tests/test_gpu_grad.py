@@ -122,3 +122,33 @@ def test_w4a8_grad_input_matches_fp64(qlin, fmt, bits):
     assert torch.equal(x.grad, dx)
     with pytest.raises(NotImplementedError):
         qlin.w4a8_linear_grad_input(dy.cuda(), q, s_rel, s_ch, cb, torch.zeros(k // 16, n, device="cuda"), 16, 256)
+
+
+@pytest.mark.parametrize("pad", [0, 4, 8])
+def test_int8_grad_input_abi_row_pitch(qlin, pad):
+    """dx written with a row pitch of k + pad through the C ABI (pad 4: rows not 16-byte aligned,
+    so the rotation stores element by element; pad 8: aligned rows, vector stores); the padding
+    columns stay untouched."""
+    from qlin import _lib
+    m, n, k = 33, 200, 256
+    q, s, g = _weights(n, k, seed=11)
+    dy = torch.randn(m, n, generator=g).to(torch.float16)
+    qd, sd, dyd = q.cuda(), s.cuda(), dy.cuda()
+    qt = qlin._grad.grad_weight(qd)
+    ld = k + pad
+    dx = torch.full((m, ld), 7.0, dtype=torch.float16, device="cuda")
+    nws = _lib.lib.qlin_int8_linear_grad_input_workspace(m, n, k, 128)
+    ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
+    rc = _lib.lib.qlin_int8_linear_grad_input(dyd.data_ptr(), 1, m, n, n, qt.data_ptr(), k, sd.data_ptr(), 1, 128,
+                                              dx.data_ptr(), 1, ld, ws.data_ptr(), nws,
+                                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, _lib.lib.qlin_last_error()
+    ref = O.int8_grad_input(dy.double().numpy(), q.numpy(), s.float().numpy(), 128)
+    assert O.max_abs_rel(dx[:, :k].float().cpu().numpy(), ref) <= 2e-3
+    if pad:
+        assert bool((dx[:, k:] == 7.0).all())
+    # a workspace one byte short is refused before any launch
+    rc = _lib.lib.qlin_int8_linear_grad_input(dyd.data_ptr(), 1, m, n, n, qt.data_ptr(), k, sd.data_ptr(), 1, 128,
+                                              dx.data_ptr(), 1, ld, ws.data_ptr(), nws - 1,
+                                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 2
