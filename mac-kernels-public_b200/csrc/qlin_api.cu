@@ -425,13 +425,22 @@ int qlin_int8_linear_grad_input(const void* dy, int dy_dtype, int64_t m, int64_t
   a.x_row_exp = rexp;
   a.bias = nullptr;
   a.bias_kind = 0;
-  a.y = rotate_group ? static_cast<void*>(unrot) : dx;
-  a.y_dtype = rotate_group ? (int)OUT_F32 : out_kind_of(dx_dtype);
-  a.ldy = rotate_group ? k : lddx;
   a.partial = partial;
   a.partial_bytes = pb;
+  // The rotation runs in the GEMM's epilogue where that is faster (groups of 32 / 64, 2-byte dx,
+  // no K split); otherwise the GEMM writes fp32 dx and a separate pass rotates it.  Both apply
+  // the same butterflies to the same fp32 values.
+  a.y = dx;
+  a.y_dtype = out_kind_of(dx_dtype);
+  a.ldy = lddx;
+  a.rot_group = rotate_group;
+  if (rotate_group == 0 || f16_gemm_can_rotate(a)) return run_f16_gemm(a, stream);
+  a.rot_group = 0;
+  a.y = unrot;
+  a.y_dtype = OUT_F32;
+  a.ldy = k;
   rc = run_f16_gemm(a, stream);
-  if (rc || !rotate_group) return rc;
+  if (rc) return rc;
   launch_grad_rotate(unrot, (int)m, (int)k, rotate_group, dx, out_kind_of(dx_dtype), lddx, stream);
   return check_cuda("gradient rotation launch");
 }

@@ -12,65 +12,11 @@
 #include <cstdint>
 
 #include "qlin_decode.cuh"
+#include "qlin_hadamard.cuh"
 #include "qlin_peer.cuh"
 #include "qlin_internal.h"
 
 namespace qlin {
-
-// ---------------------------------------------------------------------------------------------
-// Block-Hadamard rotation in a warp: a block of G = 32*E values, lane l holding elements
-// l*E .. l*E+E-1.  y[p] = sum_i H[p][i] x[i] / sqrt(G) with
-//   kind 0: Sylvester H2 (x) ... (x) H2 (H2 = [[1,1],[1,-1]]), any power of two;
-//   kind 1: H4 (x) ... (x) H4 with the regular H4 = J - 2*antidiag (the reference's
-//           build_hadamard, modal/weight_error_app.py:90-98), powers of four.
-// ---------------------------------------------------------------------------------------------
-template <int E>
-__device__ __forceinline__ float partner(const float (&x)[E], int e, int mask) {
-  constexpr int LE = (E == 1) ? 0 : (E == 2) ? 1 : (E == 4) ? 2 : 3;
-  const int rm = mask & (E - 1);
-  const int lm = mask >> LE;
-  float v = x[e ^ rm];
-  if (lm) v = __shfl_xor_sync(0xffffffffu, v, lm);
-  return v;
-}
-
-template <int E>
-__device__ __forceinline__ void block_hadamard(float (&x)[E], int kind, int lane) {
-  constexpr int LE = (E == 1) ? 0 : (E == 2) ? 1 : (E == 4) ? 2 : 3;
-  constexpr int LG = LE + 5;
-  if (kind == 0) {
-#pragma unroll
-    for (int t = 0; t < LG; ++t) {
-      float y[E];
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const int i = lane * E + e;
-        const float p = partner<E>(x, e, 1 << t);
-        y[e] = (i >> t) & 1 ? __fsub_rn(p, x[e]) : __fadd_rn(x[e], p);
-      }
-#pragma unroll
-      for (int e = 0; e < E; ++e) x[e] = y[e];
-    }
-  } else {
-#pragma unroll
-    for (int t = 0; t < LG / 2; ++t) {
-      float y[E];
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const float p1 = partner<E>(x, e, 1 << (2 * t));
-        const float p2 = partner<E>(x, e, 2 << (2 * t));
-        const float p3 = partner<E>(x, e, 3 << (2 * t));
-        const float s = __fadd_rn(__fadd_rn(x[e], p1), __fadd_rn(p2, p3));
-        y[e] = __fsub_rn(s, __fmul_rn(2.f, p3));
-      }
-#pragma unroll
-      for (int e = 0; e < E; ++e) x[e] = y[e];
-    }
-  }
-  const float norm = (E == 1) ? 0.17677669529663687f : (E == 2) ? 0.125f : (E == 4) ? 0.08838834764831845f : 0.0625f;
-#pragma unroll
-  for (int e = 0; e < E; ++e) x[e] = __fmul_rn(x[e], norm);
-}
 
 __device__ __forceinline__ float load_x(const void* x, int dtype, long long idx) {
   if (dtype == 1) return __half2float(reinterpret_cast<const __half*>(x)[idx]);
@@ -1395,11 +1341,6 @@ __global__ void __launch_bounds__(256) grad_prologue_kernel(const void* __restri
     const float v1 = c + 1 < N ? scale_pow2(value(c + 1), f) : 0.f;
     *reinterpret_cast<__half2*>(o + c) = __floats2half2_rn(v0, v1);
   }
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // a -> low half
-  return *reinterpret_cast<uint32_t*>(&h);
 }
 
 // 8 consecutive values of a 16-byte aligned row (f16 / bf16 / f32) as floats.

@@ -68,6 +68,11 @@ __device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // a -> low half
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 __device__ __forceinline__ float exp2i(int e) {  // 2^e for -126 <= e <= 127
   return __int_as_float((e + 127) << 23);
 }

@@ -317,9 +317,22 @@ static bool staged_output_ok(const F16GemmArgs& a) {
          (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
 }
 
+bool f16_gemm_can_rotate(const F16GemmArgs& a) {
+  static const bool disabled = [] {
+    const char* e = getenv("QLIN_NO_ROT_EPILOGUE");  // tuning knob: rotate in a separate pass
+    return e && atoi(e) != 0;
+  }();
+  if (disabled || a.fmt != WF_INT8 || a.out != nullptr || a.lora_k != 0 || a.M <= 2 || a.N == 0 ||
+      (a.rot_group != 32 && a.rot_group != 64) || !staged_output_ok(a))
+    return false;
+  int tm = a.tm, splits = a.k_splits;
+  plan_f16(a.M, a.N, a.K, a.fmt, &tm, &splits);
+  return splits == 1;
+}
+
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return 0;
-  if (a.M <= 2 && a.lora_k == 0) {
+  if (a.M <= 2 && a.lora_k == 0 && a.rot_group == 0) {
     const int rc = run_gemv(a, stream);
     if (rc >= 0) return rc;
   }
@@ -347,6 +360,7 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   p.y = a.y;
   p.y_dtype = a.y_dtype;
   p.ldy = a.ldy;
+  p.rot_group = a.rot_group;
   p.partial = nullptr;
   p.status = reinterpret_cast<DeviceStatus*>(device_status_ptr());
   p.Mp = p.m_tiles * tm;
@@ -409,7 +423,17 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
     if (rc) return rc;
   }
   switch (a.fmt) {
-    case WF_INT8: rc = dispatch_tm<DecInt8>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
+    case WF_INT8:
+      if (a.rot_group != 0) {
+        if (!f16_gemm_can_rotate(a)) {
+          set_error("output rotation needs the staged single-pass epilogue");
+          return 2;
+        }
+        rc = dispatch_tm<DecInt8, true>(tx, tw, tp, tt, maps, p, tm, pair, stream);
+      } else {
+        rc = dispatch_tm<DecInt8>(tx, tw, tp, tt, maps, p, tm, pair, stream);
+      }
+      break;
     case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     case WF_Q4_0: rc = dispatch_tm<DecQ4_0>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     case WF_IQ4_NL: rc = dispatch_tm<DecIQ4<false>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;

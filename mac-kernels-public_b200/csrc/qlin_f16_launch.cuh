@@ -12,13 +12,13 @@
 
 namespace qlin {
 
-template <class Dec, int TM, int STAGES, bool PAIR>
+template <class Dec, int TM, int STAGES, bool PAIR, bool ROT = false>
 static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
                       const PeerMaps& maps,
                       const GemmParams& p, cudaStream_t stream) {
   constexpr int smem = qgemm_f16_smem_bytes<Dec, TM, STAGES, PAIR>();
   static_assert(smem <= 232448, "shared memory per CTA");
-  auto kern = qgemm_f16_kernel<Dec, TM, STAGES, PAIR>;
+  auto kern = qgemm_f16_kernel<Dec, TM, STAGES, PAIR, ROT>;
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -58,27 +58,27 @@ static int launch_one(const CUtensorMap& tx, const CUtensorMap& tw, const CUtens
   return 0;
 }
 
-template <class Dec, int TM>
+template <class Dec, int TM, bool ROT = false>
 static int launch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
                       const PeerMaps& maps,
                      const GemmParams& p, bool pair, cudaStream_t stream) {
   if constexpr (TM >= 128) {
-    if (pair) return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, true>(), true>(tx, tw, tp, tt, maps, p, stream);
+    if (pair) return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, true>(), true, ROT>(tx, tw, tp, tt, maps, p, stream);
   }
-  return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, false>(), false>(tx, tw, tp, tt, maps, p, stream);
+  return launch_one<Dec, TM, qgemm_f16_stages<Dec, TM, false>(), false, ROT>(tx, tw, tp, tt, maps, p, stream);
 }
 
-template <class Dec>
+template <class Dec, bool ROT = false>
 static int dispatch_tm(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tp, const CUtensorMap& tt,
                       const PeerMaps& maps,
                        const GemmParams& p, int tm, bool pair, cudaStream_t stream) {
   switch (tm) {
-    case 16: return launch_tm<Dec, 16>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 32: return launch_tm<Dec, 32>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 64: return launch_tm<Dec, 64>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 128: return launch_tm<Dec, 128>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 192: return launch_tm<Dec, 192>(tx, tw, tp, tt, maps, p, pair, stream);
-    case 256: return launch_tm<Dec, 256>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 16: return launch_tm<Dec, 16, ROT>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 32: return launch_tm<Dec, 32, ROT>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 64: return launch_tm<Dec, 64, ROT>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 128: return launch_tm<Dec, 128, ROT>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 192: return launch_tm<Dec, 192, ROT>(tx, tw, tp, tt, maps, p, pair, stream);
+    case 256: return launch_tm<Dec, 256, ROT>(tx, tw, tp, tt, maps, p, pair, stream);
     default: set_error("unsupported token tile %d", tm); return 2;
   }
 }

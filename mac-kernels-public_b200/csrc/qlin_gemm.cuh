@@ -22,6 +22,7 @@
 #include <cuda.h>
 
 #include "qlin_decode.cuh"
+#include "qlin_hadamard.cuh"
 #include "qlin_peer.cuh"
 
 namespace qlin {
@@ -54,6 +55,9 @@ struct GemmParams {
   int main_k_stages;
   const __nv_bfloat16* lora_u;
   int lora_k;
+  // ROT kernels only: each output row is multiplied by the block Hadamard of rot_group (32 or 64)
+  // channels, in fp32, before its one rounding (the staged 2-byte output path, no K split).
+  int rot_group;
   DeviceStatus* status;
   // Staged 2-byte output: out.ndst > 0 writes each finished 32-token chunk through shared memory
   // with 16-byte stores to every destination (this rank's slab in each rank's gathered buffer);
@@ -107,7 +111,7 @@ __device__ __forceinline__ void store_out(void* y, int dtype, long long idx, flo
   else reinterpret_cast<float*>(y)[idx] = v;
 }
 
-template <class Dec, int TM, int STAGES, bool PAIR>
+template <class Dec, int TM, int STAGES, bool PAIR, bool ROT = false>
 __global__ void __launch_bounds__(448, 1)
 qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                  const __grid_constant__ CUtensorMap tmap_p, const __grid_constant__ CUtensorMap tmap_t,
@@ -455,13 +459,34 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             if (issuer) bulk_wait_read<1>();  // the stores that last read this buffer are done with it
             if (!(epi_ok = epi_sync())) break;
           }
+          if constexpr (ROT) {
+            // fp32 chunk [kCh tokens][128 channels] in the upper half of the staging area (free on
+            // this path), then each warp rotates whole token rows: lane l holds channels
+            // 4l .. 4l+3, i.e. two 64-blocks or four 32-blocks of the row.
+            float* frot = reinterpret_cast<float*>(sepi + 16384);
 #pragma unroll
-          for (int j = 0; j < kCh; ++j) {
-            const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
-            float o = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs);
-            o = __fadd_rn(o, bias);
-            buf[j * 128 + r] = p.y_dtype == OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o))
-                                                     : __half_as_ushort(__float2half_rn(o));
+            for (int j = 0; j < kCh; ++j) {
+              const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
+              frot[j * 128 + r] = __fadd_rn(__fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs), bias);
+            }
+            if (!(epi_ok = epi_sync())) break;
+            for (int j = quarter; j < kCh; j += 4) {
+              const float4 t4 = *reinterpret_cast<const float4*>(frot + j * 128 + 4 * lane);
+              float o4[4] = {t4.x, t4.y, t4.z, t4.w};
+              row_hadamard4(o4, p.rot_group, lane);
+              const uint32_t w0 = p.y_dtype == OUT_BF16 ? pack_bf16x2(o4[0], o4[1]) : pack_f16x2(o4[0], o4[1]);
+              const uint32_t w1 = p.y_dtype == OUT_BF16 ? pack_bf16x2(o4[2], o4[3]) : pack_f16x2(o4[2], o4[3]);
+              *reinterpret_cast<uint2*>(buf + j * 128 + 4 * lane) = make_uint2(w0, w1);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < kCh; ++j) {
+              const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
+              float o = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs);
+              o = __fadd_rn(o, bias);
+              buf[j * 128 + r] = p.y_dtype == OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o))
+                                                       : __half_as_ushort(__float2half_rn(o));
+            }
           }
           if (use_tma) {
             fence_proxy_async_smem();

@@ -152,3 +152,38 @@ def test_int8_grad_input_abi_row_pitch(qlin, pad):
                                               dx.data_ptr(), 1, ld, ws.data_ptr(), nws - 1,
                                               torch.cuda.current_stream().cuda_stream)
     assert rc == 2
+
+
+@pytest.mark.parametrize("group", [32, 64])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+def test_fused_rotation_equals_separate_pass(qlin, group, out_dtype):
+    """With a 2-byte dx, no K split and groups of 32 / 64 the GEMM epilogue rotates dx's rows
+    itself; a row pitch that is not a multiple of 8 elements takes the fp32 output + separate
+    rotation pass instead.  Both apply the same butterflies to the same fp32 values, so they agree
+    bit for bit."""
+    from qlin import _lib
+    m, n, k = 2048, 1024, 3072  # 11 x 12 tile pairs: no K split
+    q, s, g = _weights(n, k, seed=group)
+    dy = torch.randn(m, n, generator=g).to(torch.float16).cuda()
+    qd, sd = q.cuda(), s.cuda()
+    qt = qlin._grad.grad_weight(qd)
+    nws = _lib.lib.qlin_int8_linear_grad_input_workspace(m, n, k, group)
+    ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
+    code = 1 if out_dtype == torch.float16 else 2
+    outs, rotate_launches = [], []
+    for ld in (k, k + 4):
+        dx = torch.zeros(m, ld, dtype=out_dtype, device="cuda")
+        torch.cuda.synchronize()
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            rc = _lib.lib.qlin_int8_linear_grad_input(dy.data_ptr(), 1, m, n, n, qt.data_ptr(), k, sd.data_ptr(), 1,
+                                                      group, dx.data_ptr(), code, ld, ws.data_ptr(), nws,
+                                                      torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+        assert rc == 0, _lib.lib.qlin_last_error()
+        rotate_launches.append(sum(1 for e in prof.events() if "grad_rotate_kernel" in e.name))
+        outs.append(dx[:, :k].clone())
+    assert rotate_launches == [0, 1]  # fused in the epilogue, then the separate pass
+    assert torch.equal(outs[0], outs[1])
+    ref = O.int8_grad_input(dy.double().cpu().numpy(), q.numpy(), s.float().numpy(), group)
+    assert O.max_abs_rel(outs[0].float().cpu().numpy(), ref) <= TOL[out_dtype]
+    _check_status(qlin)
