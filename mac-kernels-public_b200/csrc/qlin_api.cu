@@ -427,9 +427,9 @@ int qlin_int8_linear_grad_input(const void* dy, int dy_dtype, int64_t m, int64_t
   a.bias_kind = 0;
   a.partial = partial;
   a.partial_bytes = pb;
-  // The rotation runs in the GEMM's epilogue where that is faster (groups of 32 / 64, 2-byte dx,
-  // no K split); otherwise the GEMM writes fp32 dx and a separate pass rotates it.  Both apply
-  // the same butterflies to the same fp32 values.
+  // The rotation runs in the GEMM's epilogue where it can (groups up to 128, 2-byte dx, no K
+  // split); otherwise the GEMM writes fp32 dx and a separate pass rotates it.  Both apply the
+  // same butterflies to the same fp32 values.
   a.y = dx;
   a.y_dtype = out_kind_of(dx_dtype);
   a.ldy = lddx;

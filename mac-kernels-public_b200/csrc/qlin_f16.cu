@@ -323,7 +323,7 @@ bool f16_gemm_can_rotate(const F16GemmArgs& a) {
     return e && atoi(e) != 0;
   }();
   if (disabled || a.fmt != WF_INT8 || a.out != nullptr || a.lora_k != 0 || a.M <= 2 || a.N == 0 ||
-      (a.rot_group != 32 && a.rot_group != 64) || !staged_output_ok(a))
+      (a.rot_group != 32 && a.rot_group != 64 && a.rot_group != 128) || !staged_output_ok(a))
     return false;
   int tm = a.tm, splits = a.k_splits;
   plan_f16(a.M, a.N, a.K, a.fmt, &tm, &splits);

@@ -55,8 +55,8 @@ struct GemmParams {
   int main_k_stages;
   const __nv_bfloat16* lora_u;
   int lora_k;
-  // ROT kernels only: each output row is multiplied by the block Hadamard of rot_group (32 or 64)
-  // channels, in fp32, before its one rounding (the staged 2-byte output path, no K split).
+  // ROT kernels only: each output row is multiplied by the block Hadamard of rot_group (32, 64 or
+  // 128) channels, in fp32, before its one rounding (the staged 2-byte output path, no K split).
   int rot_group;
   DeviceStatus* status;
   // Staged 2-byte output: out.ndst > 0 writes each finished 32-token chunk through shared memory
@@ -462,7 +462,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           if constexpr (ROT) {
             // fp32 chunk [kCh tokens][128 channels] in the upper half of the staging area (free on
             // this path), then each warp rotates whole token rows: lane l holds channels
-            // 4l .. 4l+3, i.e. two 64-blocks or four 32-blocks of the row.
+            // 4l .. 4l+3, i.e. one 128-block, two 64-blocks or four 32-blocks of the row.
             float* frot = reinterpret_cast<float*>(sepi + 16384);
 #pragma unroll
             for (int j = 0; j < kCh; ++j) {
@@ -470,13 +470,24 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
               frot[j * 128 + r] = __fadd_rn(__fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs), bias);
             }
             if (!(epi_ok = epi_sync())) break;
-            for (int j = quarter; j < kCh; j += 4) {
-              const float4 t4 = *reinterpret_cast<const float4*>(frot + j * 128 + 4 * lane);
-              float o4[4] = {t4.x, t4.y, t4.z, t4.w};
-              row_hadamard4(o4, p.rot_group, lane);
-              const uint32_t w0 = p.y_dtype == OUT_BF16 ? pack_bf16x2(o4[0], o4[1]) : pack_f16x2(o4[0], o4[1]);
-              const uint32_t w1 = p.y_dtype == OUT_BF16 ? pack_bf16x2(o4[2], o4[3]) : pack_f16x2(o4[2], o4[3]);
-              *reinterpret_cast<uint2*>(buf + j * 128 + 4 * lane) = make_uint2(w0, w1);
+            constexpr int kRows = (kCh + 3) / 4;  // token rows of this warp: quarter, quarter + 4, ...
+            float o4[kRows][4];
+#pragma unroll
+            for (int jj = 0; jj < kRows; ++jj) {
+              const int j = jj * 4 + quarter;
+              float4 t4 = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (j < kCh) t4 = *reinterpret_cast<const float4*>(frot + j * 128 + 4 * lane);
+              o4[jj][0] = t4.x; o4[jj][1] = t4.y; o4[jj][2] = t4.z; o4[jj][3] = t4.w;
+            }
+            rows_hadamard4<kRows>(o4, p.rot_group, lane);  // the rows' butterfly chains overlap
+#pragma unroll
+            for (int jj = 0; jj < kRows; ++jj) {
+              const int j = jj * 4 + quarter;
+              if (j < kCh) {
+                const uint32_t w0 = p.y_dtype == OUT_BF16 ? pack_bf16x2(o4[jj][0], o4[jj][1]) : pack_f16x2(o4[jj][0], o4[jj][1]);
+                const uint32_t w1 = p.y_dtype == OUT_BF16 ? pack_bf16x2(o4[jj][2], o4[jj][3]) : pack_f16x2(o4[jj][2], o4[jj][3]);
+                *reinterpret_cast<uint2*>(buf + j * 128 + 4 * lane) = make_uint2(w0, w1);
+              }
             }
           } else {
 #pragma unroll

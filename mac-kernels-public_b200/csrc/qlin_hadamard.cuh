@@ -59,51 +59,69 @@ __device__ __forceinline__ void block_hadamard(float (&x)[E], int kind, int lane
   for (int e = 0; e < E; ++e) x[e] = __fmul_rn(x[e], norm);
 }
 
-// Sylvester butterflies over 2^LG values held four per lane (stages t = 0 .. LG-1); both the sum
-// and the difference are formed and one is selected by the element's bit t, so a lane-dependent
-// choice never becomes a divergent branch.
-template <int LG>
-__device__ __forceinline__ void sylvester_rows4(float (&x)[4], int lane) {
+// Sylvester butterflies over 2^LG values held four per lane, for R independent rows at once
+// (stage by stage, so the rows' shuffle chains overlap); both the sum and the difference are
+// formed and one is selected by the element's bit t, so a lane-dependent choice never becomes a
+// divergent branch.
+template <int R, int LG>
+__device__ __forceinline__ void sylvester_rows4(float (&x)[R][4], int lane) {
 #pragma unroll
   for (int t = 0; t < LG; ++t) {
-    float y[4];
+    float y[R][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float p = partner<4>(x, e, 1 << t);
-      const float a = __fadd_rn(x[e], p), b = __fsub_rn(p, x[e]);
-      y[e] = (((lane * 4 + e) >> t) & 1) ? b : a;
-    }
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) x[e] = y[e];
+      for (int e = 0; e < 4; ++e) {
+        const float p = partner<4>(x[r], e, 1 << t);
+        const float a = __fadd_rn(x[r][e], p), b = __fsub_rn(p, x[r][e]);
+        y[r][e] = (((lane * 4 + e) >> t) & 1) ? b : a;
+      }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[r][e] = y[r][e];
   }
 }
 
-// A 128-value row held four per lane (lane l: elements 4l .. 4l+3), rotated in blocks of G = 32
-// (Sylvester) or 64 (the H4 Kronecker power), the forward prologue's matrices for those sizes.
-// The butterfly stages run in the same order and with the same operations as block_hadamard's,
-// so each block's result is the same, value for value, as block_hadamard over that block.
-__device__ __forceinline__ void row_hadamard4(float (&x)[4], int G, int lane) {
-  if (G == 64) {
+// The H4 Kronecker power over blocks of 64 values held four per lane (base-4 digits 0, 1, 2),
+// R rows at once.
+template <int R>
+__device__ __forceinline__ void h4_rows4_64(float (&x)[R][4]) {
 #pragma unroll
-    for (int t = 0; t < 3; ++t) {
-      float y[4];
+  for (int t = 0; t < 3; ++t) {
+    float y[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float p1 = partner<4>(x, e, 1 << (2 * t));
-        const float p2 = partner<4>(x, e, 2 << (2 * t));
-        const float p3 = partner<4>(x, e, 3 << (2 * t));
-        const float s = __fadd_rn(__fadd_rn(x[e], p1), __fadd_rn(p2, p3));
-        y[e] = __fsub_rn(s, __fmul_rn(2.f, p3));
+        const float p1 = partner<4>(x[r], e, 1 << (2 * t));
+        const float p2 = partner<4>(x[r], e, 2 << (2 * t));
+        const float p3 = partner<4>(x[r], e, 3 << (2 * t));
+        const float s = __fadd_rn(__fadd_rn(x[r][e], p1), __fadd_rn(p2, p3));
+        y[r][e] = __fsub_rn(s, __fmul_rn(2.f, p3));
       }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) x[e] = y[e];
-    }
-  } else {
-    sylvester_rows4<5>(x, lane);
-  }
-  const float norm = G == 64 ? 0.125f : 0.17677669529663687f;
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-  for (int e = 0; e < 4; ++e) x[e] = __fmul_rn(x[e], norm);
+      for (int e = 0; e < 4; ++e) x[r][e] = y[r][e];
+  }
+}
+
+// R rows of 128 values, each held four per lane (lane l: elements 4l .. 4l+3), rotated in blocks
+// of G = 32 / 128 (Sylvester) or 64 (the H4 Kronecker power), the forward prologue's matrices for
+// those sizes.  The butterfly stages run in the same order and with the same operations as
+// block_hadamard's, so each block's result is the same, value for value, as block_hadamard over
+// that block.
+template <int R>
+__device__ __forceinline__ void rows_hadamard4(float (&x)[R][4], int G, int lane) {
+  if (G == 128) sylvester_rows4<R, 7>(x, lane);
+  else if (G == 64) h4_rows4_64<R>(x);
+  else sylvester_rows4<R, 5>(x, lane);
+  const float norm = G == 128 ? 0.08838834764831845f : G == 64 ? 0.125f : 0.17677669529663687f;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x[r][e] = __fmul_rn(x[r][e], norm);
 }
 
 }  // namespace qlin

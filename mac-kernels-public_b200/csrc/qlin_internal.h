@@ -72,16 +72,16 @@ struct F16GemmArgs {
   const void* lora_t = nullptr;
   const void* lora_u_ptr = nullptr;
   int lora_k = 0;
-  // > 0: every output row times the block Hadamard of rot_group channels (32 or 64) before its
-  // one rounding, in the GEMM epilogue; only where f16_gemm_can_rotate() says so.
+  // > 0: every output row times the block Hadamard of rot_group channels (32, 64 or 128) before
+  // its one rounding, in the GEMM epilogue; only where f16_gemm_can_rotate() says so.
   int rot_group = 0;
 };
 
 // Returns 0 on success, a positive QLIN_* code on failure (message via set_error).
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream);
-// Whether run_f16_gemm can apply a.rot_group in its epilogue: INT8 weights, groups of 32 or 64
-// (measured faster than the separate rotation pass; for 128 the separate pass is faster), no
-// small-M kernel, no K split, the staged 2-byte output path, a plain output.
+// Whether run_f16_gemm can apply a.rot_group in its epilogue: INT8 weights, groups of 32, 64 or
+// 128 (one 128-row weight tile), no small-M kernel, no K split, the staged 2-byte output path, a
+// plain output.
 bool f16_gemm_can_rotate(const F16GemmArgs& a);
 // Small-M (M <= 2) weight-streaming kernel; -1 when it does not apply.
 int run_gemv(const F16GemmArgs& a, cudaStream_t stream);

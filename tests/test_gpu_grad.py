@@ -154,10 +154,10 @@ def test_int8_grad_input_abi_row_pitch(qlin, pad):
     assert rc == 2
 
 
-@pytest.mark.parametrize("group", [32, 64])
+@pytest.mark.parametrize("group", [32, 64, 128])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
 def test_fused_rotation_equals_separate_pass(qlin, group, out_dtype):
-    """With a 2-byte dx, no K split and groups of 32 / 64 the GEMM epilogue rotates dx's rows
+    """With a 2-byte dx, no K split and groups up to 128 the GEMM epilogue rotates dx's rows
     itself; a row pitch that is not a multiple of 8 elements takes the fp32 output + separate
     rotation pass instead.  Both apply the same butterflies to the same fp32 values, so they agree
     bit for bit."""
