@@ -156,13 +156,13 @@ def test_int8_grad_input_abi_row_pitch(qlin, pad):
 
 @pytest.mark.parametrize("group", [32, 64, 128])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
-def test_fused_rotation_equals_separate_pass(qlin, group, out_dtype):
+@pytest.mark.parametrize("m,n,k", [(2048, 1024, 3072), (4096, 512, 1408)])  # CTA pairs; 11 tiles: single CTAs
+def test_fused_rotation_equals_separate_pass(qlin, group, out_dtype, m, n, k):
     """With a 2-byte dx, no K split and groups up to 128 the GEMM epilogue rotates dx's rows
     itself; a row pitch that is not a multiple of 8 elements takes the fp32 output + separate
     rotation pass instead.  Both apply the same butterflies to the same fp32 values, so they agree
     bit for bit."""
     from qlin import _lib
-    m, n, k = 2048, 1024, 3072  # 11 x 12 tile pairs: no K split
     q, s, g = _weights(n, k, seed=group)
     dy = torch.randn(m, n, generator=g).to(torch.float16).cuda()
     qd, sd = q.cuda(), s.cuda()
