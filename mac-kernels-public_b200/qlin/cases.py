@@ -6,6 +6,7 @@ Synthetic seeded inputs with the configurations' shapes and value distributions:
   cfg1_q8_0 / cfg1_q4_0   GGUF Q8_0 / Q4_0 linear, X fp16 [256, 3072], W [3072, 3072]
   cfg2                    INT8 ConvRot weight-only linear, X [4096, 3072], W [12288, 3072], H-128
   cfg2_grad               its input gradient: dY fp16 [4096, 12288] -> dX [4096, 3072], H-128
+  cfg2_q4_0 / cfg2_iq4nl  GGUF Q4_0 / IQ4_NL linear at the configuration-2 shape
   cfg3                    W4A8, X [4096, 12288], W 4-bit [3072, 12288], group 128
   cfg4_fwd / cfg4_rev     W6A8, X [3240, 5120] / [3240, 13824], W 6-bit, group 64
   cfg5_q4k / cfg5_q6k     MMDiT-block GGUF linears, X [4608, 3072] / [4608, 12288]
@@ -33,9 +34,11 @@ def _gguf_blocks(qtype, n, k, gen, dev):
 def build(name, dev):
     """Returns (callable running the op once, flops per call)."""
     gen = torch.Generator().manual_seed(0)
-    if name.startswith("cfg1") or name.startswith("cfg5"):
-        qtype, m, k, n = {"cfg1_q8_0": (8, 256, 3072, 3072), "cfg1_q4_0": (2, 256, 3072, 3072),
-                          "cfg5_q4k": (12, 4608, 3072, 9216), "cfg5_q6k": (14, 4608, 12288, 3072)}[name]
+    gguf_cases = {"cfg1_q8_0": (8, 256, 3072, 3072), "cfg1_q4_0": (2, 256, 3072, 3072),
+                  "cfg2_q4_0": (2, 4096, 3072, 12288), "cfg2_iq4nl": (20, 4096, 3072, 12288),
+                  "cfg5_q4k": (12, 4608, 3072, 9216), "cfg5_q6k": (14, 4608, 12288, 3072)}
+    if name in gguf_cases:
+        qtype, m, k, n = gguf_cases[name]
         x = torch.randn(m, k, generator=gen).to(torch.float16).to(dev)
         raw = _gguf_blocks(qtype, n, k, gen, dev)
         qlin.repack_gguf(raw, qtype, (n, k))
