@@ -459,6 +459,15 @@ def run_ours(args, rank, world):
         formats["int8_convrot_g128_grad_input"] = {"tflops": FLOPS / (t * 1e-3) / 1e12, "ms": t,
                                                     "vs_forward_time": t / ms,
                                                     "note": "dx = dy . W, dy fp16 [4096, 12288] -> dx fp16 [4096, 3072]"}
+        # the kitchen's default rotation (H4 Kronecker, 256): forward op and input gradient
+        fn = lambda: qlin.int8_linear(xd, qd, sd, bd, torch.float16, convrot=True, convrot_groupsize=256)  # noqa: E731
+        t256 = statistics.mean(timed_steps(fn, max(3, args.steps // 2), args.warmup, flush, stream))
+        formats["int8_convrot_g256"] = {"tflops": FLOPS / (t256 * 1e-3) / 1e12, "ms": t256}
+        fn = lambda: qlin.int8_linear_grad_input(dy, qd, sd, True, 256)  # noqa: E731
+        t = statistics.mean(timed_steps(fn, max(3, args.steps // 2), args.warmup, flush, stream))
+        formats["int8_convrot_g256_grad_input"] = {"tflops": FLOPS / (t * 1e-3) / 1e12, "ms": t,
+                                                    "vs_forward_time": t / t256,
+                                                    "note": "H4-256 rotates in a separate pass over fp32 dx"}
 
     mmdit = None
     if not args.no_mmdit:
