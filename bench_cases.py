@@ -1,6 +1,6 @@
 """Named benchmark configurations, runnable on their own (for profiling and reproduction):
 
-    python -m qlin.cases cfg1_q8_0 --iters 3
+    python bench_cases.py cfg1_q8_0 --iters 3
 
 Synthetic seeded inputs with the configurations' shapes and value distributions:
   cfg1_q8_0 / cfg1_q4_0   GGUF Q8_0 / Q4_0 linear, X fp16 [256, 3072], W [3072, 3072]
@@ -12,11 +12,18 @@ Synthetic seeded inputs with the configurations' shapes and value distributions:
   cfg5_q4k / cfg5_q6k     MMDiT-block GGUF linears, X [4608, 3072] / [4608, 12288]
 """
 import argparse
+import os
 import sys
 
-import torch
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mac-kernels-public_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
 
-import qlin
+import torch  # noqa: E402
+
+import qlin  # noqa: E402
 
 
 def _gguf_blocks(qtype, n, k, gen, dev):

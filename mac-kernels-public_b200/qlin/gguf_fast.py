@@ -10,10 +10,16 @@ It returns None (stock path) for: weights that are not GGML-quantized with a sup
 patches, any patch that is not a plain LoRA (DoRA, other adapters), and inputs that are not on a
 CUDA device.  Plain LoRAs stay unmerged: call-local fp32 factors are built from the patches on
 every call (`_lora_for_call`; nothing is cached, so factors follow patch changes and never outlive
-the call), whole-layer LoRAs are stacked along the rank and run inside the GEMM as extra K stages
-(up to rank 256; beside it otherwise), row-slice LoRAs are applied to their output slice beside a
-base output produced in fp32; either way the LoRA terms join the sum before the single rounding to
-the input dtype.
+the call).  Whole-layer LoRAs are stacked along the rank; for bf16 activations and a stacked rank of
+at most FUSED_MAX_RANK they run inside the GEMM as extra K stages (the fork's fused case), otherwise
+beside it in fp32.  Row-slice LoRAs are applied to their output slice beside a base output produced
+in fp32.  Either way the LoRA terms join the sum before the single rounding to the input dtype.
+
+`FUSED_MAX_RANK` and `_kernel()` are the module contract the fork's callers read: the ComfyUI glue
+classifies a call as fused when `rank > 0 and x.dtype == torch.bfloat16 and rank <= FUSED_MAX_RANK`
+(`bench/gguf_node.py:55-70`), and tests wrap `_kernel().gguf_linear` to count kernel calls
+(`tests/test_gguf_node.py:80-92`).  `linear` looks `gguf_linear` up on `_kernel()` at every call, so
+such a wrapper sees every call, with `lora_down` among the keyword arguments exactly when fused.
 """
 from __future__ import annotations
 
@@ -22,6 +28,15 @@ from dataclasses import dataclass, field
 import torch
 
 import qlin
+
+# Largest stacked LoRA rank that runs inside the GEMM (for bf16 activations), as in the fork.
+FUSED_MAX_RANK = 128
+
+
+def _kernel():
+    """The kernel module whose `gguf_linear` this hook calls (the fork's comfy_kitchen handle), or
+    None when no CUDA device is present."""
+    return qlin if torch.cuda.is_available() else None
 
 
 @dataclass
@@ -98,6 +113,9 @@ def linear(layer, x):
         return None
     if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16, torch.float32):
         return None
+    ck = _kernel()
+    if ck is None:
+        return None
     factors = _lora_for_call(w, x)
     if factors is None:
         return None
@@ -107,21 +125,22 @@ def linear(layer, x):
         bias = bias.as_subclass(torch.Tensor) if type(bias) is not torch.Tensor else bias
         bias = bias.to(x.device)
     shape = (int(w.tensor_shape[0]), int(w.tensor_shape[1]))
-    has_lora = factors.stacked is not None or factors.sliced
+    rank = 0 if factors.stacked is None else int(factors.stacked[0].shape[0])
+    fused = rank > 0 and x.dtype == torch.bfloat16 and rank <= FUSED_MAX_RANK
+    beside = (rank > 0 and not fused) or bool(factors.sliced)
+    kwargs = dict(bias=bias, out_dtype=torch.float32 if beside else x.dtype)
+    if fused:
+        # whole-layer LoRAs inside the GEMM (extra K stages), added before the output's rounding
+        down, up = factors.stacked
+        kwargs.update(lora_down=down, lora_up=up, lora_scale=1.0)
     try:
-        if factors.stacked is not None and not factors.sliced:
-            # whole-layer LoRAs run inside the GEMM (extra K stages), added before the one rounding
-            down, up = factors.stacked
-            return qlin.gguf_linear(x, raw, int(qtype), shape, bias=bias, out_dtype=x.dtype, lora_down=down,
-                                    lora_up=up, lora_scale=1.0)
-        y = qlin.gguf_linear(x, raw, int(qtype), shape, bias=bias,
-                             out_dtype=torch.float32 if has_lora else x.dtype)
+        y = ck.gguf_linear(x, raw, int(qtype), shape, **kwargs)
     except NotImplementedError:
         return None
-    if not has_lora:
+    if not beside:
         return y
     xf = x.float()
-    if factors.stacked is not None:
+    if rank > 0 and not fused:
         down, up = factors.stacked
         y += torch.nn.functional.linear(torch.nn.functional.linear(xf, down), up)
     for down, up, start in factors.sliced:

@@ -15,6 +15,25 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "slow: longer CPU test")
 
 
-def pytest_collection_modifyitems(config, items):
-    # Everything under -m gpu needs CUDA; fail loudly rather than skip when a GPU run has none.
-    pass
+@pytest.fixture(autouse=True)
+def _poison_uninitialized_memory(request):
+    """GPU tests run with every fresh torch allocation poisoned: floating-point tensors from
+    torch.empty are filled with NaN and integer tensors with their maximum value (PyTorch's
+    deterministic mode with fill_uninitialized_memory).  Outputs, workspaces and caches the
+    library is handed therefore never hold an earlier result, so a kernel that skips a store or
+    reads a workspace entry it never wrote shows up as a NaN or a wrong value instead of passing on
+    a recycled allocation.  warn_only keeps library ops without a deterministic variant usable."""
+    if request.node.get_closest_marker("gpu") is None:
+        yield
+        return
+    import torch
+    prev = torch.are_deterministic_algorithms_enabled()
+    prev_warn = torch.is_deterministic_algorithms_warn_only_enabled()
+    prev_fill = torch.utils.deterministic.fill_uninitialized_memory
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    torch.utils.deterministic.fill_uninitialized_memory = True
+    try:
+        yield
+    finally:
+        torch.utils.deterministic.fill_uninitialized_memory = prev_fill
+        torch.use_deterministic_algorithms(prev, warn_only=prev_warn)

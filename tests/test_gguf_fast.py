@@ -121,3 +121,110 @@ def test_declines_explicit_precision_settings_on_gpu():
     assert gguf_fast.linear(layer, x) is not None  # patch_dtype without patches: fast path
     layer.weight.patches = [([lora_patch(torch.zeros(192, 2), torch.zeros(2, 512))], "k")]
     assert gguf_fast.linear(layer, x) is None
+
+
+# ---------------------------------------------------------------------------------------------
+# The fork's module contract, exercised the way the reference's ComfyUI glue and node tests do:
+# a Spy wrapping `_kernel().gguf_linear` (tests/test_gguf_node.py:80-92) and the route audit that
+# classifies fused / beside LoRA calls with FUSED_MAX_RANK (bench/gguf_node.py:50-70).
+# ---------------------------------------------------------------------------------------------
+class Spy:
+    def __init__(self, fast, monkeypatch):
+        self.calls = []
+        ck = fast._kernel()
+        assert ck is not None, "a kernel module with gguf_linear on CUDA is required"
+        real = ck.gguf_linear
+
+        def spy(*a, **kw):
+            self.calls.append(kw)
+            return real(*a, **kw)
+
+        monkeypatch.setattr(ck, "gguf_linear", spy)
+
+
+def install_audit(fast, monkeypatch):
+    record = dict(kernel=False, kernel_fused=0, kernel_beside=0, kernel_slices=0)
+    real_prepare, real_linear = fast._lora_for_call, fast.linear
+
+    def prepare(weight, x):
+        factors = real_prepare(weight, x)
+        if factors is not None:
+            rank = 0 if factors.stacked is None else factors.stacked[0].shape[0]
+            fused = rank > 0 and x.dtype == torch.bfloat16 and rank <= fast.FUSED_MAX_RANK
+            record.update(kernel_fused=int(fused), kernel_beside=int(rank > 0 and not fused),
+                          kernel_slices=len(factors.sliced))
+        return factors
+
+    def linear(layer, x):
+        result = real_linear(layer, x)
+        record["kernel"] = result is not None
+        return result
+
+    monkeypatch.setattr(fast, "_lora_for_call", prepare)
+    monkeypatch.setattr(fast, "linear", linear)
+    return record
+
+
+def test_module_contract_names():
+    from qlin import gguf_fast
+    assert gguf_fast.FUSED_MAX_RANK == 128
+    assert callable(gguf_fast._kernel)
+    ck = gguf_fast._kernel()
+    assert ck is None or callable(ck.gguf_linear)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype", [12, 14, 8, 6, 11])
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 8e-3), (torch.float16, 3e-3)])
+def test_spy_sees_one_kernel_call_without_lora(qtype, dtype, tol, monkeypatch):
+    from qlin import gguf_fast
+    layer = make_layer(qtype, device="cuda")
+    x = torch.randn(2, 40, 512, device="cuda", dtype=dtype)
+    spy = Spy(gguf_fast, monkeypatch)
+    got = gguf_fast.linear(layer, x)
+    assert len(spy.calls) == 1 and "lora_down" not in spy.calls[0]
+    assert got.dtype == dtype and got.shape == (2, 40, 192)
+    ref = stock(layer, x)
+    assert ((got.float().cpu() - ref).norm() / ref.norm()).item() < tol
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,rank,fused", [(torch.bfloat16, 16, True), (torch.float16, 16, False),
+                                              (torch.bfloat16, 200, False)])
+@pytest.mark.parametrize("sliced", [False, True])
+def test_fused_classification_matches_the_kernel_call(dtype, rank, fused, sliced, monkeypatch):
+    from qlin import gguf_fast
+    layer = make_layer(12, device="cuda")
+    g = torch.Generator().manual_seed(1)
+    patches = [lora_patch(torch.randn(192, rank, generator=g) * 0.05, torch.randn(rank, 512, generator=g) * 0.05,
+                          alpha=rank / 2),
+               lora_patch(torch.randn(192, 4, generator=g) * 0.05, torch.randn(4, 512, generator=g) * 0.05, strength=0.5)]
+    if sliced:
+        patches.append(lora_patch(torch.randn(64, 4, generator=g) * 0.05, torch.randn(4, 512, generator=g) * 0.05,
+                                  offset=(0, 64, 64)))
+    layer.weight.patches = [(patches, "diffusion_model.x.weight")]
+    x = torch.randn(64, 512, device="cuda", dtype=dtype)
+    audit = install_audit(gguf_fast, monkeypatch)
+    spy = Spy(gguf_fast, monkeypatch)
+    got = gguf_fast.linear(layer, x)
+    assert audit["kernel"] and audit["kernel_slices"] == int(sliced)
+    assert audit["kernel_fused"] == int(fused) and audit["kernel_beside"] == int(not fused)
+    assert len(spy.calls) == 1 and ("lora_down" in spy.calls[0]) == fused
+    ref = stock(layer, x)
+    layer.weight.patches = []
+    base = stock(layer, x)
+    assert ((ref - base).norm() / base.norm()).item() > 0.05  # the LoRA is visible
+    tol = 8e-3 if dtype == torch.bfloat16 else 3e-3
+    assert got.dtype == dtype and ((got.float().cpu() - ref).norm() / ref.norm()).item() < tol
+
+
+@pytest.mark.gpu
+def test_dora_never_reaches_the_kernel(monkeypatch):
+    from qlin import gguf_fast
+    layer = make_layer(8, device="cuda")
+    g = torch.Generator().manual_seed(3)
+    layer.weight.patches = [([lora_patch(torch.randn(192, 8, generator=g) * 0.05, torch.randn(8, 512, generator=g) * 0.05,
+                                         dora=torch.ones(192, 1))], "k")]
+    spy = Spy(gguf_fast, monkeypatch)
+    assert gguf_fast.linear(layer, torch.randn(16, 512, device="cuda", dtype=torch.bfloat16)) is None
+    assert spy.calls == []
