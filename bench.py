@@ -10,9 +10,16 @@ linear of the benchmark configuration (X fp16 [4096, 3072] with 1% outlier chann
 `e2e` is the same op through the public API with the step's activations copied from pinned host
 memory and its output copied back inside the timed region.  Every timed step is preceded by an
 L2 flush (a 512 MB write) outside its CUDA-event window.  `formats` times every other weight
-format at the same shape.  With --gpus N each rank runs its own replica (weak scaling; the
-linear needs no collective).  --impl reference times the reference's CPU dequantize + matmul path
-(restated in oracle/) on the host cores instead.
+format at the same shape (one GPU).
+
+With --gpus N (N > 1, one process per GPU under torchrun) the line's `value` is configuration 5
+instead: the 60-block MMDiT linear stack with every weight sharded along N over the GPUs and the
+outputs all-gathered over NVLink (strong scaling, time = max over ranks); the replicated headline
+op moves to `replicated_cfg2`, and `mmdit_stack` carries the per-N breakdown (compute, exchange,
+overlap, the all-outputs-gathered variant, the M-split replica control).
+
+--impl reference times the reference's CPU dequantize + matmul path (restated in oracle/) on the
+host cores instead, on the same workload.
 """
 import argparse
 import json
@@ -47,6 +54,18 @@ def peaks():
         return {"hbm_gbs": p["hbm_gbs"], "tflops": p["bf16_tflops"], "tflops_sustained": p.get("bf16_tflops_sustained"),
                 "source": "measured"}
     return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def workload_config(world):
+    """The `config` of both arms' JSON lines (identical, so the two lines describe one workload)."""
+    if world == 1:
+        return {"workload": "int8_convrot_linear M=4096 K=3072 N=12288 group=128 fp16 out", "format": "int8_convrot",
+                "hadamard": "sylvester-128", "l2": "GPU arm: flushed before every step; host arm: n/a",
+                "parallelism": "1 GPU"}
+    return {"workload": "mmdit_stack: 60 blocks x (QKV 3072->9216, out 3072->3072, up 3072->12288 Q4_K; "
+                        "down 12288->3072 Q6_K), 4608 tokens",
+            "format": "gguf q4_k + q6_k", "l2": "GPU arm: flushed before every step; host arm: n/a",
+            "parallelism": f"N-sharded over {world} GPUs (weights split along N, outputs all-gathered over NVLink)"}
 
 
 def profile_traffic(name):
@@ -143,6 +162,10 @@ def cpu_reference_step(x_cpu, q_cpu, s_cpu, b_cpu, rows):
     return torch.nn.functional.linear(x_cpu[:rows].float(), w, b_cpu.float())
 
 
+KIND = "restatement"  # the reference's CPU path restated in oracle/qlin_oracle.py (the reference's own
+                     # port cannot build the Sylvester-128 rotation of the benchmark configuration)
+
+
 def cpu_baseline(steps=2, rows=M):
     from oracle import qlin_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
@@ -153,49 +176,92 @@ def cpu_baseline(steps=2, rows=M):
         cpu_reference_step(x, q, s, b, rows)
     dt = (time.perf_counter() - t0) / steps
     return {"value": 2.0 * rows * K * N / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-            "kind": "port",
+            "kind": KIND,
             "sample": f"{steps} full steps ({rows} of {M} token rows), weight dequantized (q*s, rotate) per step, "
                       f"fp32 torch on {torch.get_num_threads()} threads ({dt:.2f} s/step)"}
 
 
+class _StackReferenceStep:
+    """The reference's CPU path for one MMDiT block of configuration 5 (ComfyUI-GGUF's stock path:
+    every GGUF weight dequantized per call, then an fp32 linear), restated in oracle/: the four
+    linears QKV, out, up, down on all 4608 tokens, each over the first `frac` of its output
+    channels (the block's weights are drawn once)."""
+
+    def __init__(self, frac=1.0):
+        from oracle import qlin_oracle as O
+        self.O = O
+        hid, self.tokens = 3072, 4608
+        self.lin = [(12, 3 * hid, hid), (12, hid, hid), (12, 4 * hid, hid), (14, hid, 4 * hid)]
+        self.raw = [O.random_gguf_blocks(qt, n, k, seed=i) for i, (qt, n, k) in enumerate(self.lin)]
+        g = torch.Generator().manual_seed(7)
+        self.x = {k: torch.randn(self.tokens, k, generator=g) for k in (hid, 4 * hid)}
+        self.frac = frac
+
+    def flops(self):
+        return sum(2.0 * self.tokens * self.rows(n) * k for _, n, k in self.lin)
+
+    def rows(self, n):
+        return max(256, int(n * self.frac) // 256 * 256)
+
+    def __call__(self):
+        for (qt, n, k), raw in zip(self.lin, self.raw):
+            r = self.rows(n)
+            w = torch.from_numpy(self.O.gguf_dequantize(raw[:r], qt, r, k))
+            torch.nn.functional.linear(self.x[k], w)
+
+
 def run_reference(args, rank, world):
     """The reference arm: the CPU path timed on the host cores for exactly `--steps` steps after
-    `--warmup` untimed ones.  A step covers all M token rows unless that would make the run longer
-    than REF_BUDGET_S; then every step (warm-up and timed alike) covers the same smaller row sample,
-    a multiple of 256 rows, sized from the first full-size step's time."""
+    `--warmup` untimed ones, on the workload our arm's line reports (one GPU: the INT8 ConvRot
+    linear of configuration 2; several: one block of the configuration-5 stack).  A step covers the
+    whole workload unit (all M token rows; all of a block's output channels) unless that would make
+    the run longer than REF_BUDGET_S; then every step, warm-up and timed alike, covers the same
+    smaller sample (a multiple of 256 rows / channels), sized from the first full-size step's time.
+    Under torchrun only rank 0 runs it."""
     if rank != 0:
         return
     steps, warm = max(1, args.steps), max(0, args.warmup)
     torch.set_num_threads(os.cpu_count() or 1)
     from oracle import qlin_oracle as O
-    x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=0)
-    rows = M
+    if world == 1:
+        x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=0)
+        state = {"rows": M}
+        step = lambda: cpu_reference_step(x, q, s, b, state["rows"])  # noqa: E731
+        flops = lambda: 2.0 * state["rows"] * K * N  # noqa: E731
+        shrink = lambda f: state.update(rows=max(256, min(M, int(M * f) // 256 * 256)))  # noqa: E731
+        describe = lambda: (f"{state['rows']} of {M} token rows per step; weight dequantized (q*s, rotate) per "  # noqa: E731
+                            f"step; fp32 torch")
+    else:
+        step = _StackReferenceStep()
+        flops = step.flops
+        shrink = lambda f: setattr(step, "frac", min(1.0, f))  # noqa: E731
+        describe = lambda: (f"one MMDiT block per step (4 GGUF linears, 4608 tokens, {100 * step.frac:.0f}% of "  # noqa: E731
+                            f"each layer's output channels); weights dequantized per step (gguf-py restated); "
+                            f"fp32 torch")
     done_warm = 0
     if warm > 0:
         t0 = time.perf_counter()
-        cpu_reference_step(x, q, s, b, rows)
+        step()
         t_full = time.perf_counter() - t0
         done_warm = 1
         left = warm - 1 + steps
         if left * t_full > REF_BUDGET_S:
-            rows = max(256, min(M, int(M * REF_BUDGET_S / (left * t_full)) // 256 * 256))
+            shrink(REF_BUDGET_S / (left * t_full))
     for _ in range(warm - done_warm):
-        cpu_reference_step(x, q, s, b, rows)
+        step()
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
-        cpu_reference_step(x, q, s, b, rows)
+        step()
         times.append(time.perf_counter() - t0)
     dt = statistics.mean(times)
-    value = 2.0 * rows * K * N / dt / 1e12
+    value = flops() / dt / 1e12
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
             "steps": steps, "warmup": warm, "ms_per_step": dt * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "int8_convrot_linear M=4096 K=3072 N=12288 group=128 fp16 out",
-                       "format": "int8_convrot", "sample_rows": rows, "l2": "n/a (host)"},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"{steps} timed steps of {rows} of {M} token rows; weight dequantized "
-                                       f"(q*s, rotate) per step; fp32 torch"},
+            "scaling": "weak" if world == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(world),
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": KIND,
+                             "sample": f"{steps} timed steps; " + describe()},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -282,19 +348,22 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
         nbytes = raw.numel() + 256 * 3072 * 2 * 2
         cfgs[name] = {"tflops": fl / (t * 1e-3) / 1e12, "us": t * 1e3,
                       "roofline_frac": roofline_time_s(fl, nbytes, pk) / (t * 1e-3), "timing": "cuda graph replay"}
-    # Small M (text tokens, adapter side paths): HBM-bound weight streaming.
-    xs_all, raw_np = O.cfg_gguf(16, 3072, 3072, qtype=8, seed=0)
-    raw = torch.from_numpy(raw_np).to(dev)
-    for m in (1, 16):
-        xs = xs_all[:m].to(dev)
-        fn = lambda: qlin.gguf_linear(xs, raw, 8, (3072, 3072))  # noqa: E731
+    # Small M (text tokens, adapter side paths): HBM-bound weight streaming, one launch.
+    small = [(8, 3072, 3072, m, f"cfg1_small_gguf_q8_0_{m}x3072x3072") for m in (1, 16, 64)]
+    small += [(12, 3072, 12288, 1, "small_m_gguf_q4_k_1x3072x12288"), (2, 3072, 3072, 1, "small_m_gguf_q4_0_1x3072x3072")]
+    for qt, k, n, m, name in small:
+        xs, raw_np = O.cfg_gguf(m, k, n, qtype=qt, seed=0)
+        xs = xs.to(dev)
+        raw = torch.from_numpy(raw_np).to(dev)
+        fn = lambda: qlin.gguf_linear(xs, raw, qt, (n, k))  # noqa: E731
         t = statistics.mean(graph_steps(fn, steps, warmup, flush, stream))
-        fl = 2.0 * m * 3072 * 3072
-        nbytes = raw.numel() + m * 3072 * 2 * 2
-        cfgs[f"cfg1_small_gguf_q8_0_{m}x3072x3072"] = {
-            "us": t * 1e3, "weight_stream_gbs": raw.numel() / (t * 1e-3) / 1e9,
-            "roofline_frac": roofline_time_s(fl, nbytes, pk) / (t * 1e-3), "bound": "hbm",
-            "timing": "cuda graph replay, L2 flushed"}
+        fl = 2.0 * m * k * n
+        nbytes = raw.numel() + m * k * 2 + m * n * 2
+        cfgs[name] = {"us": t * 1e3, "weight_stream_gbs": raw.numel() / (t * 1e-3) / 1e9,
+                      "algorithmic_gbs": nbytes / (t * 1e-3) / 1e9,
+                      "roofline_frac": roofline_time_s(fl, nbytes, pk) / (t * 1e-3), "bound": "hbm",
+                      "timing": "cuda graph replay, L2 flushed"}
+        del raw
     for (m, k, n, bits, grp), name in (((4096, 12288, 3072, 4, 128), "cfg3_w4a8_4096x12288x3072"),
                                        ((3240, 5120, 13824, 6, 64), "cfg4_w6a8_fwd_3240x5120x13824"),
                                        ((3240, 13824, 5120, 6, 64), "cfg4_w6a8_rev_3240x13824x5120")):
@@ -314,41 +383,134 @@ def qlin_status():
     return qlin.device_status()
 
 
-def run_mmdit(args, world, dev, flush, stream):
-    """Configuration 5: the MMDiT block linear stack (60 blocks of QKV / out / MLP-up Q4_K and
-    MLP-down Q6_K GGUF linears, 4608 tokens, hidden 3072), weights sharded along N over the ranks,
-    outputs all-gathered into column slabs -- by the GEMM epilogues' stores into every rank's buffer
-    over NVLink ("peer", the default) or by NCCL all-gathers on a side stream ("nccl").  Returns
-    whole-job TFLOP/s (strong scaling: the total work is fixed) with the time taken as the max over
-    ranks."""
-    from qlin.sharded import ShardedStack
-    transport = args.mmdit_transport
-    # chunks only pay off when a separate gather overlaps the next chunk's GEMM
-    chunks = args.mmdit_chunks or (4 if world > 1 and transport == "nccl" else 1)
-    st = ShardedStack(blocks=args.mmdit_blocks, tokens=4608, hidden=3072, chunks=chunks, device=dev,
-                      transport=transport)
-    x = torch.randn(4608, 3072, generator=torch.Generator().manual_seed(7)).to(torch.float16).to(dev)
-    for _ in range(2):
-        st.forward(x)
+def _max_over_ranks(v, dev, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed_replays(fn, steps, warmup, flush, stream, dev, world):
+    """Mean device time (ms) of `steps` calls after `warmup`, bracketed by a barrier and a device
+    synchronize on both sides, max over ranks."""
+    if world > 1:
+        torch.distributed.barrier()
     torch.cuda.synchronize()
-    st.capture(x)  # one CUDA graph for the whole forward, NCCL gathers included
+    ms = statistics.mean(timed_steps(fn, steps, warmup, flush, stream))
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    times = timed_steps(st.replay, max(2, args.steps // 8), 1, flush, stream)
-    ms = statistics.mean(times)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    out = {"tflops": st.flops() / (ms * 1e-3) / 1e12, "ms_per_forward": ms, "blocks": args.mmdit_blocks,
-           "chunks": chunks, "n_gpus": world, "scaling": "strong", "timing": "cuda graph replay",
-           "transport": st.transport if world > 1 else "none",
-           "config": "4608 tokens, hidden 3072, QKV/out/up Q4_K + down Q6_K, N-sharded, all-gathered outputs"}
+    return _max_over_ranks(ms, dev, world)
+
+
+def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
+    """Configuration 5: the MMDiT block linear stack (60 blocks of QKV / out / MLP-up Q4_K and
+    MLP-down Q6_K GGUF linears, 4608 tokens, hidden 3072), weights sharded along N over the ranks
+    (strong scaling: the total work is fixed), outputs a later linear reads all-gathered into
+    column slabs by the GEMM epilogues' stores into every rank's buffer over NVLink ("peer", the
+    default) or by NCCL all-gathers on a side stream ("nccl").  Times are the max over ranks.
+
+    With several GPUs it also reports, per forward: the same stack over NCCL, its GEMMs alone
+    (exchange skipped) and its all-gathers alone (NCCL, back to back), the overlap those imply, the
+    variant that gathers every output (QKV's too), and the M-split replica control (every GPU holds
+    all weights and runs 4608 / N tokens, no exchange)."""
+    from qlin.sharded import ShardedStack
+    transport = args.mmdit_transport
+    tokens, hidden, blocks = 4608, 3072, args.mmdit_blocks
+    # chunks only pay off when a separate gather overlaps the next chunk's GEMM
+    chunks = args.mmdit_chunks or (4 if world > 1 and transport == "nccl" else 1)
+    x = torch.randn(tokens, hidden, generator=torch.Generator().manual_seed(7)).to(torch.float16).to(dev)
+
+    def graphed(st, **kw):
+        for _ in range(2):
+            st.forward(x, **kw)
+        torch.cuda.synchronize()
+        st.capture(x, **kw)  # one CUDA graph for the whole forward, NCCL gathers included
+        torch.cuda.synchronize()
+
+    st = ShardedStack(blocks=blocks, tokens=tokens, hidden=hidden, chunks=chunks, device=dev, transport=transport,
+                      gather=args.mmdit_gather)
+    graphed(st)
+    if clk is not None:
+        clk.__enter__()
+    ms = _timed_replays(st.replay, steps, warmup, flush, stream, dev, world)
+    if clk is not None:
+        clk.__exit__(None, None, None)
+    out = {"tflops": st.flops() / (ms * 1e-3) / 1e12, "ms_per_forward": ms, "blocks": blocks, "chunks": chunks,
+           "n_gpus": world, "scaling": "strong", "timing": "cuda graph replay, max over ranks",
+           "transport": st.transport if world > 1 else "none", "gather": args.mmdit_gather,
+           "launches_per_forward": st.launches_per_forward(),
+           "nvlink_bytes_in_per_rank_per_forward": st.gathered_bytes_per_forward(),
+           "config": f"{tokens} tokens, hidden {hidden}, QKV/out/up Q4_K + down Q6_K, N-sharded over {world} GPUs, "
+                     f"gathered outputs: {args.mmdit_gather}"}
+
+    # end to end: the block input copied from pinned host memory, the forward, the output back
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(len(st.graph_output), *st.graph_output[0].shape, dtype=torch.float16).pin_memory()
+
+    def e2e():
+        st.graph_input.copy_(xh, non_blocking=True)
+        st.replay()
+        for c, o in enumerate(st.graph_output):
+            yh[c].copy_(o, non_blocking=True)
+
+    e2e_ms = _timed_replays(e2e, max(3, steps // 2), 2, flush, stream, dev, world)
+    out["e2e"] = {"value": st.flops() / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": e2e_ms,
+                  "h2d_bytes_per_step": xh.numel() * 2, "d2h_bytes_per_step": yh.numel() * 2}
     code, where = qlin_status()
     if code:
         raise SystemExit(f"MMDiT stack: a kernel gave up a bounded wait (status {code}, where {where:#x})")
     st.close()  # graphs holding NCCL calls go before the process group does; peer buffers after a barrier
+
+    if world > 1 and not args.no_mmdit_breakdown:
+        shared = lambda b, name, base, qtype, n_loc, k, rows: st.blocks[b][name][3:5]  # noqa: E731
+        sub = max(3, steps // 2)
+        # the same stack over NCCL; its GEMMs alone; its all-gathers alone
+        nc = ShardedStack(blocks=blocks, tokens=tokens, hidden=hidden, chunks=chunks, device=dev, transport="nccl",
+                          gather=args.mmdit_gather, weights=shared)
+        graphed(nc)
+        t_nccl = _timed_replays(nc.replay, sub, 2, flush, stream, dev, world)
+        nc.release()
+        graphed(nc, exchange=False)
+        t_comp = _timed_replays(nc.replay, sub, 2, flush, stream, dev, world)
+        nc.release()
+        nc.comm_only()
+        torch.cuda.synchronize()
+        nc.capture_comm()
+        t_comm = _timed_replays(nc.replay_comm, sub, 2, flush, stream, dev, world)
+        nc.close()
+        del nc
+        gbytes = st.gathered_bytes_per_forward()
+        out["breakdown"] = {
+            "compute_ms": t_comp, "comm_ms_nccl_alone": t_comm, "total_ms": ms, "nccl_transport_ms": t_nccl,
+            "overlap_frac": max(0.0, (t_comp + t_comm - ms) / t_comm) if t_comm > 0 else None,
+            "nccl_allgather_gbs_per_rank_in": gbytes / (t_comm * 1e-3) / 1e9 if t_comm > 0 else None,
+            "nvlink_floor_ms": gbytes / 770e9 * 1e3,
+            "tensor_floor_ms": st.flops() / world / (peaks()["tflops"] * 1e12) * 1e3,
+            "limiter": "nvlink" if gbytes / 770e9 * 1e3 > t_comp else "compute",
+            "note": "compute = the NCCL-transport stack with its exchange skipped; comm = its all-gathers back to "
+                    "back; nvlink floor = bytes each rank receives / 770 GB/s (measured peer copy)"}
+        # every output gathered (QKV's too)
+        if args.mmdit_gather != "all":
+            al = ShardedStack(blocks=blocks, tokens=tokens, hidden=hidden, chunks=chunks, device=dev,
+                              transport=transport, gather="all")
+            graphed(al)
+            t_all = _timed_replays(al.replay, sub, 2, flush, stream, dev, world)
+            out["gather_all"] = {"tflops": al.flops() / (t_all * 1e-3) / 1e12, "ms_per_forward": t_all,
+                                 "nvlink_bytes_in_per_rank_per_forward": al.gathered_bytes_per_forward()}
+            al.close()
+            del al
+        # M-split replica control: all weights on every GPU, tokens / N each, no exchange
+        rp = ShardedStack(blocks=blocks, tokens=tokens // world, hidden=hidden, chunks=1, device=dev, replica=True,
+                          gather=args.mmdit_gather)
+        graphed(rp)
+        t_rep = _timed_replays(rp.replay, sub, 2, flush, stream, dev, world)
+        out["m_split_replicas"] = {"tflops": world * rp.flops() / (t_rep * 1e-3) / 1e12, "ms_per_forward": t_rep,
+                                   "tokens_per_gpu": tokens // world,
+                                   "weights_per_gpu_gb": sum(v[3].numel() for b in rp.blocks for v in b.values()) / 1e9}
+        rp.close()
+        del rp
     del st
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -472,10 +634,34 @@ def run_ours(args, rank, world):
         formats["int8_convrot_g256_grad_input"] = {"tflops": FLOPS / (t * 1e-3) / 1e12, "ms": t,
                                                     "vs_forward_time": t / t256,
                                                     "note": "H4-256 rotates in a separate pass over fp32 dx"}
+        # the kitchen's W4A8 / W6A8 layouts at the same shape: the packed codes decoded per call into a
+        # transient int8 grid, then the INT8 GEMM; against the GEMM on an already decoded grid
+        for bits, name in ((4, "kitchen_w4a8_cb_g16"), (6, "kitchen_w6a8_g16")):
+            codes = torch.randint(0, 1 << bits, (N, K), generator=gl, dtype=torch.int64)
+            qdata = torch.from_numpy(O.pack_codes_kitchen(codes.numpy(), bits).view(np.int8).copy()).to(dev)
+            s_rel = (torch.rand(N, K // 16, generator=gl) * 12 + 2).to(torch.float8_e4m3fn).to(dev)
+            s_ch = (torch.rand(N, generator=gl) * 1e-3 + 1e-4).to(dev)
+            cb = (torch.sort(torch.randn(16, generator=gl)).values * 3).to(dev) if bits == 4 else None
+            fn = lambda: qlin.w4a8_int8_linear(xd, qdata, s_rel, s_ch, cb, None, bd, 16, GROUP, torch.float16)  # noqa: E731
+            t_k = statistics.mean(timed_steps(fn, max(3, args.steps // 2), args.warmup, flush, stream))
+            from qlin._w4a8 import kitchen_grid
+            grid = kitchen_grid(qdata, s_rel, cb, 16)
+            fn = lambda: qlin.int8_linear(xd, grid, s_ch, bd, torch.float16, convrot=True, convrot_groupsize=GROUP)  # noqa: E731
+            t_g = statistics.mean(timed_steps(fn, max(3, args.steps // 2), args.warmup, flush, stream))
+            formats[name] = {"tflops": FLOPS / (t_k * 1e-3) / 1e12, "ms": t_k, "predecoded_grid_ms": t_g,
+                             "vs_predecoded_grid": t_k / t_g,
+                             "resident_bytes": qdata.numel() + s_rel.numel() + 4 * N + (64 if cb is not None else 0),
+                             "note": "codes decoded to a transient int8 grid every call (nothing cached)"}
+            del grid, qdata, s_rel
 
-    mmdit = None
-    if not args.no_mmdit:
-        mmdit = run_mmdit(args, world, dev, flush, stream)
+    mmdit, clk_stack = None, None
+    if world > 1:
+        # several GPUs: the headline is the N-sharded configuration-5 stack, timed for exactly the
+        # requested steps
+        clk_stack = ClockSampler(dev)
+        mmdit = run_mmdit(args, world, dev, flush, stream, args.steps, args.warmup, clk=clk_stack)
+    elif not args.no_mmdit:
+        mmdit = run_mmdit(args, world, dev, flush, stream, max(2, args.steps // 8), 1)
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -486,9 +672,7 @@ def run_ours(args, rank, world):
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f16 (int8 weights decoded exactly to fp16, fp32 accumulate)",
                 "data": "synthetic (seeded; configuration 2 shapes and distributions)",
-                "config": {"workload": "int8_convrot_linear M=4096 K=3072 N=12288 group=128 fp16 out",
-                           "format": "int8_convrot", "hadamard": "sylvester-128", "l2": "flushed before every step",
-                           "parallelism": f"replicas x{world}"},
+                "config": workload_config(world),
                 "roofline": roofline,
                 "roofline_op": {"bound": "tensor", "time_frac": roof_t / (ms * 1e-3),
                                 "note": "whole op (rotation prologue + GEMM) vs max(bytes/HBM, flops/peak)"},
@@ -497,6 +681,22 @@ def run_ours(args, rank, world):
                 "cpu_baseline": base, "formats": formats, "configs": configs, "mmdit_stack": mmdit,
                 "int8_peak_tops_measured": int8_peak, "gpu_launches": 2 * args.steps,
                 "parity_max_abs_rel": err, "clocks": clk.summary()}
+        if world > 1:
+            # the replicated configuration-2 op moves to its own key; the stack is the line
+            line["replicated_cfg2"] = {"tflops": value, "ms": ms, "e2e_tflops": line["e2e"]["value"],
+                                       "scaling": "weak", "note": "one independent replica of the headline op per GPU"}
+            line.update(value=mmdit["tflops"], ms_per_step=mmdit["ms_per_forward"], scaling="strong",
+                        dtype="f16 (GGUF Q4_K / Q6_K decoded to fp16, fp32 accumulate)",
+                        data="synthetic (seeded; configuration 5 shapes, random legal GGUF blocks)",
+                        e2e={k: mmdit["e2e"][k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")},
+                        gpu_launches=mmdit["launches_per_forward"] * args.steps, clocks=clk_stack.summary())
+            line["mmdit_stack"] = mmdit
+            line.pop("roofline_op")
+            line["roofline_stack"] = {k: mmdit.get("breakdown", {}).get(k) for k in
+                                      ("nvlink_floor_ms", "tensor_floor_ms", "limiter")}
+            if mmdit.get("breakdown"):
+                floor = max(mmdit["breakdown"]["nvlink_floor_ms"], mmdit["breakdown"]["tensor_floor_ms"])
+                line["roofline_stack"]["time_frac"] = floor / mmdit["ms_per_forward"]
         print(json.dumps(line), flush=True)
 
 
@@ -512,6 +712,8 @@ def main():
     ap.add_argument("--mmdit-blocks", type=int, default=60)
     ap.add_argument("--mmdit-chunks", type=int, default=0)
     ap.add_argument("--mmdit-transport", choices=("peer", "nccl"), default="peer")
+    ap.add_argument("--mmdit-gather", choices=("consumed", "all"), default="consumed")
+    ap.add_argument("--no-mmdit-breakdown", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -519,10 +721,12 @@ def main():
     if world > 1 and args.impl == "ours":
         import datetime
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-        # NCCL's own log lines (its version banner among them) go to a file: stdout carries only
-        # the JSON line of rank 0.
-        os.environ.setdefault("NCCL_DEBUG_FILE", f"/tmp/qlin_bench_nccl.{rank}.log")
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        # NCCL's own log lines (its version banner and communicator lines, when NCCL_DEBUG asks for
+        # them) go to stderr: stdout carries only the JSON line of rank 0.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
+        args.no_formats = True  # the format sweep is a 1-GPU measurement
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)

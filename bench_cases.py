@@ -10,6 +10,8 @@ Synthetic seeded inputs with the configurations' shapes and value distributions:
   cfg3                    W4A8, X [4096, 12288], W 4-bit [3072, 12288], group 128
   cfg4_fwd / cfg4_rev     W6A8, X [3240, 5120] / [3240, 13824], W 6-bit, group 64
   cfg5_q4k / cfg5_q6k     MMDiT-block GGUF linears, X [4608, 3072] / [4608, 12288]
+  small_q8_0_m1 / _m16 / _m64   the small-M path: Q8_0 [3072, 3072] with M = 1 / 16 / 64 tokens
+  small_q4k_m1            the small-M path: Q4_K [12288, 3072], M = 1
 """
 import argparse
 import os
@@ -43,7 +45,9 @@ def build(name, dev):
     gen = torch.Generator().manual_seed(0)
     gguf_cases = {"cfg1_q8_0": (8, 256, 3072, 3072), "cfg1_q4_0": (2, 256, 3072, 3072),
                   "cfg2_q4_0": (2, 4096, 3072, 12288), "cfg2_iq4nl": (20, 4096, 3072, 12288),
-                  "cfg5_q4k": (12, 4608, 3072, 9216), "cfg5_q6k": (14, 4608, 12288, 3072)}
+                  "cfg5_q4k": (12, 4608, 3072, 9216), "cfg5_q6k": (14, 4608, 12288, 3072),
+                  "small_q8_0_m1": (8, 1, 3072, 3072), "small_q8_0_m16": (8, 16, 3072, 3072),
+                  "small_q8_0_m64": (8, 64, 3072, 3072), "small_q4k_m1": (12, 1, 3072, 12288)}
     if name in gguf_cases:
         qtype, m, k, n = gguf_cases[name]
         x = torch.randn(m, k, generator=gen).to(torch.float16).to(dev)

@@ -178,6 +178,13 @@ int qlin_peer_free(void* ptr);
 int qlin_peer_export(const void* ptr, void* handle);
 int qlin_peer_import(const void* handle, void** ptr);
 int qlin_peer_close(void* ptr);
+/* Stream-ordered: waits (one-thread kernel, bounded by timeout_ms, 0: 10 s) until every rank has
+ * finished as many qlin_gguf_linear_allgather calls as this rank, i.e. until the other ranks'
+ * stores into this rank's gathered buffers from those calls are complete.  Call it before
+ * reading a gathered output that no later all-gather call waits for (the last one of a
+ * sequence).  On expiry qlin_device_status reports QLIN_ETIMEOUT.  No counterpart in the
+ * reference (which runs on one GPU). */
+int qlin_peer_wait(int world, int rank, void* const* sync_ranks, uint32_t timeout_ms, void* stream);
 
 /* The GGUF linear above with no workspace argument: the scratch (fp16 activation copy and split-K
  * partial sums) lives in a fixed 16 MiB array in device memory that the library reserves on every
@@ -185,9 +192,10 @@ int qlin_peer_close(void* ptr);
  * for callers that cannot allocate device memory at call time: hosts without a caching allocator
  * (cudaMalloc synchronizes the device and costs far more than the layer) and hosts with a fixed
  * memory budget or allocation-free steady state.  Calls whose scratch need exceeds 16 MiB are
- * rejected with QLIN_EINVAL and a message; nothing is allocated.  The first call on a device
- * looks up the scratch address (make that call before any stream capture).  Calls on one device
- * share the scratch, so calls that overlap on the GPU race: order them on one stream. */
+ * rejected with QLIN_EINVAL and a message; nothing is allocated.  The first call in a CUDA
+ * context (per device, and again after cudaDeviceReset or under another context the caller made
+ * current) looks up the scratch address (make that call before any stream capture).  Calls on one
+ * device share the scratch, so calls that overlap on the GPU race: order them on one stream. */
 int qlin_gguf_linear_noalloc(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
                              const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
                              int y_dtype, int64_t ldy, void* stream);

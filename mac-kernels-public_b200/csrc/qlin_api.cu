@@ -103,29 +103,70 @@ static bool valid_group(int g) { return g == 0 || g == 32 || g == 64 || g == 128
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch for the current device.  In host code the symbol is only
-// a host-side stand-in; the real address comes from cudaGetSymbolAddress, looked up once per
-// device with that device current.
+// Unique id of the calling thread's current CUDA context (cuCtxGetId: never reused within the
+// process, unlike a context handle or a device index), through the runtime's driver entry points;
+// 0 when no context is current yet.
+typedef CUresult (*PFN_ctxGetCurrent_t)(CUcontext*);
+typedef CUresult (*PFN_ctxGetId_t)(CUcontext, unsigned long long*);
+
+static unsigned long long current_context_id() {
+  static PFN_ctxGetCurrent_t get_current = nullptr;
+  static PFN_ctxGetId_t get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_ctxGetCurrent_t>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_ctxGetId_t>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of g_noalloc_scratch in the current context.  In host code the symbol is only a
+// host-side stand-in; the real address comes from cudaGetSymbolAddress, looked up once per CUDA
+// context (keyed by the context's unique id, so a context created after cudaDeviceReset, or a
+// non-primary context the caller made current, gets its own lookup) with that context current.
 static int noalloc_scratch(void** out) {
   static std::mutex mu;
-  static void* addr[64] = {nullptr};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    set_error("qlin_gguf_linear_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+  struct Entry {
+    unsigned long long ctx;
+    void* addr;
+  };
+  static Entry cache[64] = {};
+  static int next = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  unsigned long long id = current_context_id();
+  if (id != 0) {
+    for (const Entry& e : cache)
+      if (e.ctx == id) {
+        *out = e.addr;
+        return QLIN_OK;
+      }
+  }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // also makes the context current
+  if (e != cudaSuccess || p == nullptr) {
+    int dev = -1;
+    cudaGetDevice(&dev);
+    set_error("qlin_gguf_linear_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
     return QLIN_ECUDA;
   }
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      set_error("qlin_gguf_linear_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
-      return QLIN_ECUDA;
-    }
-    addr[dev] = p;
+  if (id == 0) id = current_context_id();
+  if (id != 0) {
+    cache[next] = Entry{id, p};
+    next = (next + 1) % 64;
   }
-  *out = addr[dev];
+  *out = p;
   return QLIN_OK;
 }
 
@@ -703,10 +744,41 @@ int qlin_peer_close(void* ptr) {
   return QLIN_OK;
 }
 
+namespace {
+// One thread: the bounded wait of the flag protocol, without computing or publishing anything.
+__global__ void peer_wait_kernel(const PeerOut po, DeviceStatus* status) {
+  if (threadIdx.x == 0) peer_wait(po, status, 9);
+}
+}  // namespace
+
+int qlin_peer_wait(int world, int rank, void* const* sync_ranks, uint32_t timeout_ms, void* stream) {
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || sync_ranks == nullptr) {
+    set_error("peer_wait: 1 <= world <= %d, 0 <= rank < world and one flag pad per rank", kMaxPeers);
+    return QLIN_EINVAL;
+  }
+  PeerOut po;
+  memset(&po, 0, sizeof(po));
+  po.world = world;
+  po.self = rank;
+  po.timeout_ms = timeout_ms;
+  for (int r = 0; r < world; ++r) {
+    if (sync_ranks[r] == nullptr) {
+      set_error("peer_wait: null flag pad for rank %d", r);
+      return QLIN_EINVAL;
+    }
+    po.sync[r] = reinterpret_cast<PeerSync*>(sync_ranks[r]);
+  }
+  po.own = po.sync[rank];
+  peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      po, reinterpret_cast<DeviceStatus*>(device_status_ptr()));
+  return check_cuda("peer wait launch");
+}
+
 // Same computation as qlin_gguf_linear, with the workspace taken from the library's static device
 // scratch instead of the caller.  Nothing is allocated, so it suits callers that cannot allocate
-// device memory at call time.  The first call on a device looks up the scratch address (make it
-// before any stream capture).  All calls on a device share one scratch: calls that overlap on
+// device memory at call time.  The first call in a CUDA context (once per device, again after a
+// reset or under another context) looks up the scratch address (make it before any stream
+// capture).  All calls on a device share one scratch: calls that overlap on
 // the GPU (different streams, or other threads) race and must be ordered by the caller.
 // Every scratch byte a call reads is written earlier in the same call, so stale contents from a
 // previous call are never read and nothing needs clearing.

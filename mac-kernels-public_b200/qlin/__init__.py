@@ -23,7 +23,7 @@ import torch
 from . import _lib
 from ._lib import QlinDecline, QlinError, check, lib
 
-__all__ = ["int8_linear", "int8_linear_streamed", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear", "dequantize_w4a8_int8_weight",
+__all__ = ["int8_linear", "int8_linear_streamed", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "peer_wait", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear", "dequantize_w4a8_int8_weight",
            "quantize_int8_rowwise", "prologue_f16", "repack_gguf", "GGUF_TYPES", "QlinDecline", "QlinError",
            "device_status", "int8_linear_grad_input", "w4a8_linear_grad_input", "int8_linear_trainable",
            "w4a8_linear_trainable"]
@@ -317,6 +317,16 @@ def gguf_linear_allgather(x_slabs, packed, row_exp, qtype, n, y_ranks, sync_rank
                                          None if b is None else b.data_ptr(), 0 if b is None else _DT[b.dtype],
                                          world, rank, ys, 1, n, syncs, int(timeout_ms), ws.data_ptr(), ws_bytes,
                                          _stream(x_slabs.device)), "qlin_gguf_linear_allgather")
+
+
+def peer_wait(sync_ranks, rank, timeout_ms=0, device=None):
+    """Stream-ordered wait until every rank has finished as many gguf_linear_allgather calls as this
+    one: afterwards this rank's gathered buffers hold every rank's output of those calls."""
+    import ctypes
+    world = len(sync_ranks)
+    syncs = (ctypes.c_void_p * world)(*sync_ranks)
+    check(lib.qlin_peer_wait(world, rank, syncs, int(timeout_ms), _stream(device or torch.cuda.current_device())),
+          "qlin_peer_wait")
 
 
 def dequantize_gguf(weight, qtype, shape, out_dtype=torch.float32):

@@ -31,11 +31,12 @@ _GRAD_WEIGHT_CACHE: dict = {}
 _DT = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 
-def grad_weight(qdata):
-    """The transposed int8 copy of `qdata` [N, K] the gradient GEMM reads (cached per tensor version)."""
+def grad_weight(qdata, cache=True):
+    """The transposed int8 copy of `qdata` [N, K] the gradient GEMM reads (cached per tensor version
+    unless cache=False, for a transient weight such as a decoded kitchen grid)."""
     n, k = qdata.shape
     key = (qdata.data_ptr(), qdata.device.index, n, k, qdata._version)
-    hit = _GRAD_WEIGHT_CACHE.get(key)
+    hit = _GRAD_WEIGHT_CACHE.get(key) if cache else None
     if hit is not None:
         return hit
     nbytes = lib.qlin_int8_grad_weight_bytes(n, k)
@@ -43,6 +44,8 @@ def grad_weight(qdata):
     q = qdata.contiguous()
     check(lib.qlin_int8_grad_weight(q.data_ptr(), n, k, qt.data_ptr(), nbytes,
                                     torch.cuda.current_stream(qdata.device).cuda_stream), "qlin_int8_grad_weight")
+    if not cache:
+        return qt
     _GRAD_WEIGHT_CACHE[key] = qt
     try:
         weakref.finalize(qdata, _GRAD_WEIGHT_CACHE.pop, key, None)
@@ -51,9 +54,12 @@ def grad_weight(qdata):
     return qt
 
 
-def int8_linear_grad_input(dy, qdata, scale, convrot=False, convrot_groupsize=256, out_dtype=None):
+def int8_linear_grad_input(dy, qdata, scale, convrot=False, convrot_groupsize=256, out_dtype=None, *,
+                           _transient_weight=False):
     """dx = dy . W for the frozen INT8 (ConvRot) weight W = (qdata * scale) un-rotated per block;
-    dy [..., N] float, returns [..., K] in out_dtype (default dy's dtype)."""
+    dy [..., N] float, returns [..., K] in out_dtype (default dy's dtype).  The transposed weight
+    copy is cached per weight tensor, except for a weight decoded for this call only
+    (_transient_weight, the kitchen grid)."""
     for t in (dy, qdata):
         if not t.is_cuda:
             raise NotImplementedError("qlin runs on CUDA tensors only (there is no CPU path)")
@@ -79,7 +85,7 @@ def int8_linear_grad_input(dy, qdata, scale, convrot=False, convrot_groupsize=25
         sc = sc.float()
     sc = sc.contiguous()
     group = convrot_groupsize if convrot else 0
-    qt = grad_weight(qdata) if n > 0 else None
+    qt = grad_weight(qdata, cache=not _transient_weight) if n > 0 else None
     nws = lib.qlin_int8_linear_grad_input_workspace(m, n, k, group)
     ws = torch.empty(nws, dtype=torch.uint8, device=dy.device) if nws else None
     check(lib.qlin_int8_linear_grad_input(dy2.data_ptr() if n > 0 else None, _DT[dy2.dtype], m, n,
@@ -98,9 +104,9 @@ def w4a8_linear_grad_input(dy, qdata, s_rel, s_channel, codebook=None, correctio
     if correction is not None:
         raise QlinDecline(1, "w4a8_linear_grad_input: the asymmetric correction term is not supported")
     from ._w4a8 import kitchen_grid
-    grid = kitchen_grid(qdata, s_rel, codebook, group_size)
+    grid = kitchen_grid(qdata, s_rel, codebook, group_size)  # transient, like the forward's
     return int8_linear_grad_input(dy, grid, s_channel.float().reshape(-1), convrot_groupsize > 0,
-                                  convrot_groupsize, out_dtype)
+                                  convrot_groupsize, out_dtype, _transient_weight=True)
 
 
 class _Int8Trainable(torch.autograd.Function):
@@ -108,10 +114,11 @@ class _Int8Trainable(torch.autograd.Function):
     the packed weight stays frozen."""
 
     @staticmethod
-    def forward(ctx, x, qdata, scale, bias, convrot, convrot_groupsize):
+    def forward(ctx, x, qdata, scale, bias, convrot, convrot_groupsize, transient=False):
         from . import int8_linear
         ctx.save_for_backward(qdata, scale)
         ctx.rot = (convrot, convrot_groupsize)
+        ctx.transient = transient
         ctx.x_dtype = x.dtype
         ctx.bias_dtype = None if bias is None else bias.dtype
         return int8_linear(x, qdata, scale, bias, out_dtype=x.dtype, convrot=convrot,
@@ -122,10 +129,11 @@ class _Int8Trainable(torch.autograd.Function):
         qdata, scale = ctx.saved_tensors
         gx = gb = None
         if ctx.needs_input_grad[0]:
-            gx = int8_linear_grad_input(gy, qdata, scale, ctx.rot[0], ctx.rot[1], out_dtype=ctx.x_dtype)
+            gx = int8_linear_grad_input(gy, qdata, scale, ctx.rot[0], ctx.rot[1], out_dtype=ctx.x_dtype,
+                                        _transient_weight=ctx.transient)
         if ctx.bias_dtype is not None and ctx.needs_input_grad[3]:
             gb = gy.reshape(-1, gy.shape[-1]).float().sum(0).to(ctx.bias_dtype)
-        return gx, None, None, gb, None, None
+        return gx, None, None, gb, None, None, None
 
 
 def int8_linear_trainable(x, qdata, scale, bias=None, convrot=False, convrot_groupsize=256):
@@ -135,10 +143,11 @@ def int8_linear_trainable(x, qdata, scale, bias=None, convrot=False, convrot_gro
 
 def w4a8_linear_trainable(x, qdata, s_rel, s_channel, codebook=None, correction=None, bias=None, group_size=16,
                           convrot_groupsize=256):
-    """w4a8_int8_linear with autograd, through the kitchen layout's int8 grid."""
+    """w4a8_int8_linear with autograd, through the kitchen layout's int8 grid (decoded for this call
+    and kept by autograd until the backward pass, like an activation)."""
     if correction is not None:
         raise QlinDecline(1, "w4a8_linear_trainable: the asymmetric correction term is not supported")
     from ._w4a8 import kitchen_grid
     grid = kitchen_grid(qdata, s_rel, codebook, group_size)
     return _Int8Trainable.apply(x, grid, s_channel.float().reshape(-1), bias, convrot_groupsize > 0,
-                                convrot_groupsize)
+                                convrot_groupsize, True)

@@ -52,6 +52,7 @@ SIGNATURES = {
     "qlin_peer_export": (_i, [_p, _p]),
     "qlin_peer_import": (_i, [_p, ctypes.POINTER(_p)]),
     "qlin_peer_close": (_i, [_p]),
+    "qlin_peer_wait": (_i, [_i, _i, ctypes.POINTER(_p), ctypes.c_uint32, _p]),
     "qlin_gguf_linear_noalloc": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p]),
     "qlin_gguf_dequantize": (_i, [_p, _i, _i64, _i64, _p, _i, _p]),
     "qlin_kitchen_w4a8_grid": (_i, [_p, _i, _p, _p, _i, _i64, _i64, _p, _p]),

@@ -95,11 +95,14 @@ def _hadamard(g, device):
     return (h / math.sqrt(g)).to(device=device, dtype=torch.float32)
 
 
-_GRID_CACHE: dict = {}
-
-
 def kitchen_grid(qdata, s_rel, codebook=None, group_size=16):
-    """The int8 weight grid [N, K] of a kitchen W4A8 / W6A8 weight (cached per tensor version)."""
+    """The int8 weight grid [N, K] of a kitchen W4A8 / W6A8 weight, decoded on the GPU (bit-exact).
+
+    The grid is transient: every linear decodes it from the packed codes into a fresh tensor that
+    the caching allocator takes back after the call, so what stays resident per weight is only the
+    caller's packed codes and scales (N*K*bits/8 + N*K/group bytes), as the format intends.  The
+    decode costs one pass writing N*K bytes per call (most of which the following GEMM then reads
+    back from L2)."""
     if not qdata.is_cuda or not s_rel.is_cuda:
         raise NotImplementedError("qlin runs on CUDA tensors only (there is no CPU path)")
     n = qdata.shape[0]
@@ -107,11 +110,6 @@ def kitchen_grid(qdata, s_rel, codebook=None, group_size=16):
     bits = qdata.shape[1] * 8 // k
     if bits not in (4, 6) or qdata.shape[1] * 8 != bits * k:
         raise QlinDecline(1, "w4a8_int8_linear: qdata width matches neither 4 nor 6 bits")
-    key = (qdata.data_ptr(), qdata._version, s_rel.data_ptr(), s_rel._version,
-           None if codebook is None else (codebook.data_ptr(), codebook._version), group_size, n, k)
-    hit = _GRID_CACHE.get(key)
-    if hit is not None:
-        return hit
     cb = None
     if codebook is not None:
         cb = codebook.to(device=qdata.device, dtype=torch.float32).contiguous()
@@ -123,11 +121,6 @@ def kitchen_grid(qdata, s_rel, codebook=None, group_size=16):
     check(lib.qlin_kitchen_w4a8_grid(q.data_ptr(), bits, sr.data_ptr(), None if cb is None else cb.data_ptr(),
                                      group_size, n, k, out.data_ptr(),
                                      torch.cuda.current_stream(qdata.device).cuda_stream), "qlin_kitchen_w4a8_grid")
-    _GRID_CACHE[key] = out
-    try:
-        weakref.finalize(qdata, _GRID_CACHE.pop, key, None)
-    except TypeError:
-        pass
     return out
 
 
@@ -135,13 +128,14 @@ def w4a8_int8_linear(x, qdata, s_rel, s_channel, codebook=None, correction=None,
                      convrot_groupsize=256, out_dtype=None, lora_down=None, lora_up=None, lora_scale=None):
     """comfy-kitchen AsymW4A8Int8Layout linear (bench/bench_lora_fused_rank.py:42-44;
     bench/bench_w4a8_linear.py:83), symmetric form.  Like the reference backend it is weight-only
-    (docs/upstream/comfy-kitchen-mps-backend.md:42): the stored codes decode once to the exact int8
-    grid, and the linear is the INT8 ConvRot linear with s_channel per output channel.  An
+    (docs/upstream/comfy-kitchen-mps-backend.md:42): the stored codes decode per call to the exact
+    int8 grid (a transient tensor), and the linear is the INT8 ConvRot linear with s_channel per
+    output channel.  An
     asymmetric `correction` declines (QlinDecline), as an unsupported layout does in the kitchen."""
     if correction is not None:
         raise QlinDecline(1, "w4a8_int8_linear: the asymmetric correction term is not supported")
     from . import int8_linear
-    grid = kitchen_grid(qdata, s_rel, codebook, group_size)
+    grid = kitchen_grid(qdata, s_rel, codebook, group_size)  # transient: freed when the call returns
     return int8_linear(x, grid, s_channel.float().reshape(-1), bias, out_dtype=out_dtype,
                        convrot=convrot_groupsize > 0, convrot_groupsize=convrot_groupsize,
                        lora_down=lora_down, lora_up=lora_up, lora_scale=lora_scale)

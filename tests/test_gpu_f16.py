@@ -294,3 +294,38 @@ def test_int8_linear_streamed_from_host_memory(qlin):
         assert O.max_abs_rel(got.float().numpy(), want.float().numpy()) <= 1e-3
     with pytest.raises(NotImplementedError):
         qlin.int8_linear_streamed(x.cuda(), q.cuda(), s.cuda())
+
+
+def _small_m_k(qtype, i):
+    qk = O.GGUF_TYPES[qtype][1]
+    return (800, 96, 576, 1024, 2080)[i] if qk == 32 else (768, 256, 1280, 2048, 512)[i]
+
+
+@pytest.mark.parametrize("qtype", ALL_TYPES)
+@pytest.mark.parametrize("m,n,ki", [(1, 200, 0), (2, 384, 1), (9, 130, 2), (31, 256, 3), (64, 384, 4)])
+def test_small_m_kernel_matches_fp64(qlin, qtype, m, n, ki):
+    """Small M (text tokens, adapter side paths: the weight-streaming kernel for M <= 2, the
+    tensor-core GEMM with its K split above): odd stage counts, ragged N, K not a multiple of 64,
+    and calls repeated bit for bit (the K-split partials are reduced in a fixed order)."""
+    k = _small_m_k(qtype, ki)
+    x, raw, b, ref = _gguf_case(qtype, m, n, k, seed=m * 13 + qtype + ki)
+    raw_d = torch.from_numpy(raw).cuda()
+    y = qlin.gguf_linear(x.cuda(), raw_d, qtype, (n, k), bias=b.cuda())
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.max_abs_rel(got, ref) <= 2e-3, O.max_abs_rel(got, ref)
+    y2 = qlin.gguf_linear(x.cuda(), raw_d, qtype, (n, k), bias=b.cuda())
+    assert torch.equal(y, y2)
+    _check_status(qlin)
+
+
+@pytest.mark.parametrize("m", [1, 3, 16, 40, 64])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_small_m_int8_matches_fp64(qlin, m, out_dtype):
+    n, k = 300, 1088  # 17 stages of 64, a ragged last weight tile
+    x, q, s, b = O.cfg_int8_convrot(m, k, n, seed=m)
+    ref = O.int8_convrot_linear_ref(x.float().numpy(), q.numpy(), s.float().numpy(), b.float().numpy(), convrot=False)
+    y = qlin.int8_linear(x.cuda(), q.cuda(), s.cuda(), b.cuda(), out_dtype)
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.max_abs_rel(got, ref) <= TOL[out_dtype], O.max_abs_rel(got, ref)

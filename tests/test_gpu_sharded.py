@@ -33,24 +33,23 @@ def test_slab_operand_equals_row_major(qlin, qtype, slabs):
     assert torch.equal(got, want)
 
 
-def test_stack_on_one_gpu_equals_linear_chain(qlin):
-    from qlin.sharded import ShardedStack, random_gguf_rows, layers
+@pytest.mark.parametrize("gather", ["consumed", "all"])
+def test_stack_on_one_gpu_equals_linear_chain(qlin, gather):
+    from qlin.sharded import ShardedStack, base_weight, layers
     dev = torch.device("cuda", 0)
     hidden, tokens = 256, 384
-    st = ShardedStack(blocks=2, tokens=tokens, hidden=hidden, chunks=2, device=dev, seed=3)
+    st = ShardedStack(blocks=2, tokens=tokens, hidden=hidden, chunks=2, device=dev, seed=3, gather=gather)
     x = torch.randn(tokens, hidden, generator=torch.Generator().manual_seed(1)).to(torch.float16).to(dev)
     outs = st.forward(x)
     got = torch.cat([o[0] for o in outs], dim=0)
     h = x
     for b in range(2):
-        res = {}
-        for li, (name, qtype, n, k) in enumerate(layers(hidden)):
-            gen = torch.Generator(device=dev)
-            gen.manual_seed(3 * 100003 + b * 16 + li)
-            raw = random_gguf_rows(qtype, n, k, gen, dev)
-            src = {"qkv": h, "out": h, "up": res.get("out"), "down": res.get("up")}[name]
+        res = {"x": h}
+        for name, base, qtype, n, k, src, col0, _ in layers(hidden, gather, 1):
+            raw = base_weight(3, b, base, hidden, dev)
             # chunk by chunk, as the stack runs it (the same GEMM plan, hence identical sums)
-            res[name] = torch.cat([qlin.gguf_linear(c, raw, qtype, (n, k)) for c in src.split(tokens // 2)])
+            inp = res[src][:, col0:col0 + k]
+            res[name] = torch.cat([qlin.gguf_linear(c, raw, qtype, (n, k)) for c in inp.split(tokens // 2)])
         h = res["down"]
     assert torch.isfinite(got).all()
     assert torch.equal(got, h)

@@ -12,11 +12,16 @@ import torch.multiprocessing as mp
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _weights_dense(b, name, qtype, n, k, r, p):
-    g = torch.Generator().manual_seed(b * 16 + ("qkv", "out", "up", "down").index(name))
-    w = torch.randn(n, k, generator=g) / k ** 0.5
-    n_loc = n // p
-    return w[r * n_loc:(r + 1) * n_loc].contiguous(), None
+def _base_dense(b, base, hidden):
+    rows, cols = {"qkv": (3, 1), "out": (1, 1), "up": (4, 1), "down": (1, 4)}[base]
+    g = torch.Generator().manual_seed(b * 16 + ("qkv", "out", "up", "down").index(base))
+    return torch.randn(rows * hidden, cols * hidden, generator=g) / (cols * hidden) ** 0.5
+
+
+def _weights_dense(b, name, base, qtype, n_loc, k, rows):
+    w = _base_dense(b, base, k if base != "down" else k // 4)[rows]
+    assert w.shape == (n_loc, k)
+    return w.contiguous(), None
 
 
 def _stand_in(x_slabs, packed, row_exp, qtype, n, out):
@@ -25,7 +30,7 @@ def _stand_in(x_slabs, packed, row_exp, qtype, n, out):
     return out
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, gather):
     sys.path[:0] = [ROOT, os.path.join(ROOT, "mac-kernels-public_b200")]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -34,7 +39,7 @@ def _worker(rank, world, port, q):
         torch.manual_seed(0)
         x = torch.randn(64, 128).to(torch.float16)
         st = ShardedStack(blocks=2, tokens=64, hidden=128, chunks=2, device=torch.device("cpu"), op=_stand_in,
-                          weights=_weights_dense)
+                          weights=_weights_dense, gather=gather)
         outs = st.forward(x)
         y = torch.cat([torch.cat(list(o.float()), dim=1) for o in outs], dim=0)  # [tokens, hidden]
         q.put((rank, y))
@@ -42,24 +47,27 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def _dense_reference(x):
-    from qlin.sharded import layers
+def _dense_reference(x, gather):
+    """The block chain on one device: QKV, out (reading V for attention's output, or the block input
+    when every output is gathered), MLP up and down."""
     h = x
+    hid = x.shape[1]
     for b in range(2):
-        outs = {}
-        for name, qtype, n, k in layers(128):
-            w, _ = _weights_dense(b, name, qtype, n, k, 0, 1)
-            src = {"qkv": h, "out": h, "up": outs.get("out"), "down": outs.get("up")}[name]
-            outs[name] = (src.float() @ w.T).to(torch.float16)
-        h = outs["down"]
+        w = {base: _base_dense(b, base, hid) for base in ("qkv", "out", "up", "down")}
+        qkv = (h.float() @ w["qkv"].T).to(torch.float16)
+        attn = qkv[:, 2 * hid:] if gather == "consumed" else h
+        out = (attn.float() @ w["out"].T).to(torch.float16)
+        up = (out.float() @ w["up"].T).to(torch.float16)
+        h = (up.float() @ w["down"].T).to(torch.float16)
     return h.float()
 
 
-def test_two_rank_sharded_stack_matches_dense():
+@pytest.mark.parametrize("gather", ["consumed", "all"])
+def test_two_rank_sharded_stack_matches_dense(gather):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + os.getpid() % 1000
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29500 + os.getpid() % 1000 + (gather == "all")
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, gather)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=120) for _ in procs)
@@ -68,7 +76,26 @@ def test_two_rank_sharded_stack_matches_dense():
         assert p.exitcode == 0
     torch.manual_seed(0)
     x = torch.randn(64, 128).to(torch.float16)
-    ref = _dense_reference(x)
+    ref = _dense_reference(x, gather)
     for r in (0, 1):
         assert torch.allclose(got[r], ref, rtol=2e-2, atol=2e-2), (got[r] - ref).abs().max()
     assert torch.equal(got[0], got[1])
+
+
+def test_head_grouped_qkv_rows():
+    """Rank r of p holds the Q, K and V rows of its own heads; the shards of all ranks together
+    hold every row once."""
+    from qlin.sharded import layers, shard_rows
+    hid, p = 128, 4
+    for gather in ("consumed", "all"):
+        seen = []
+        for r in range(p):
+            for name, base, _, n, _, _, _, _ in layers(hid, gather, p):
+                rows = shard_rows(name, base, hid, r, p)
+                assert len(rows) == n // p
+                if base == "qkv":
+                    seen.append(rows)
+        rows = torch.cat(seen)
+        assert torch.equal(rows.sort().values, torch.arange(3 * hid))
+    v = shard_rows("v", "qkv", hid, 1, p)
+    assert torch.equal(v, torch.arange(2 * hid + 32, 2 * hid + 64))
