@@ -432,6 +432,7 @@ def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
     st = ShardedStack(blocks=blocks, tokens=tokens, hidden=hidden, chunks=chunks, device=dev, transport=transport,
                       gather=args.mmdit_gather)
     graphed(st)
+    finite = all(bool(torch.isfinite(o).all()) for o in st.graph_output)
     if clk is not None:
         clk.__enter__()
     ms = _timed_replays(st.replay, steps, warmup, flush, stream, dev, world)
@@ -440,7 +441,7 @@ def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
     out = {"tflops": st.flops() / (ms * 1e-3) / 1e12, "ms_per_forward": ms, "blocks": blocks, "chunks": chunks,
            "n_gpus": world, "scaling": "strong", "timing": "cuda graph replay, max over ranks",
            "transport": st.transport if world > 1 else "none", "gather": args.mmdit_gather,
-           "launches_per_forward": st.launches_per_forward(),
+           "launches_per_forward": st.launches_per_forward(), "output_finite": finite,
            "nvlink_bytes_in_per_rank_per_forward": st.gathered_bytes_per_forward(),
            "config": f"{tokens} tokens, hidden {hidden}, QKV/out/up Q4_K + down Q6_K, N-sharded over {world} GPUs, "
                      f"gathered outputs: {args.mmdit_gather}"}

@@ -5,6 +5,7 @@
 #include <algorithm>
 
 #include "qlin_gemm_i8.cuh"
+#include "qlin_gemm_i8p.cuh"
 #include "qlin_internal.h"
 
 namespace qlin {
@@ -68,13 +69,15 @@ __global__ void w6_repack_kernel(const uint8_t* __restrict__ src, int layout, in
         make_uint4(T[4 * j], T[4 * j + 1], T[4 * j + 2], T[4 * j + 3]);
 }
 
+// Stage chunks for whole pairs of 128-row tiles (the CTA-pair kernel reads both tiles of a pair);
+// rows past N are zero.
 void launch_w6_repack(const uint8_t* src, int layout, int N, int K, uint8_t* out, cudaStream_t s) {
-  const int kst = K / 128, nt = (N + 127) / 128;
+  const int kst = K / 128, nt = (N + 255) / 256 * 2;
   if (kst == 0 || nt == 0) return;
   w6_repack_kernel<<<dim3(kst, nt), 128, 0, s>>>(src, layout, N, K, kst, out);
 }
 
-size_t w6_repacked_bytes(int N, int K) { return (size_t)((N + 127) / 128) * (K / 128) * 128 * 96; }
+size_t w6_repacked_bytes(int N, int K) { return (size_t)((N + 255) / 256 * 2) * (K / 128) * 128 * 96; }
 
 template <class Dec, int TM, int STAGES>
 static int launch_i8(const CUtensorMap& tx, const CUtensorMap& tw, const GemmI8Params& p, cudaStream_t stream) {
@@ -112,6 +115,63 @@ static int dispatch_i8(int tm, const CUtensorMap& tx, const CUtensorMap& tw, con
   }
 }
 
+template <class Dec, int TN, int GPS>
+static int launch_i8p(const CUtensorMap& tx, const CUtensorMap& tw, const GemmI8Params& p, cudaStream_t stream) {
+  constexpr int STAGES = qgemm_i8p_stages<Dec, TN>();
+  constexpr int smem = qgemm_i8p_smem_bytes<Dec, TN, STAGES>();
+  static_assert(smem <= 232448, "shared memory per CTA");
+  auto kern = qgemm_i8p_kernel<Dec, TN, GPS, STAGES>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(max dynamic smem %d) failed", smem);
+      return 3;
+    }
+    attr_done[dev] = true;
+  }
+  const int tiles = p.m_tiles * ((p.N + 255) / 256);
+  const int grid = 2 * std::min(tiles, sm_count() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(I8PCfg<TN, GPS>::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, p);
+  if (e != cudaSuccess) {
+    set_error("qgemm_i8p launch failed: %s", cudaGetErrorString(e));
+    return 3;
+  }
+  return 0;
+}
+
+// The CTA-pair kernel takes token counts above 64 with groups of 64 or whole multiples of 128
+// values (per-channel scales included): 256-token tiles above 128 tokens, else 128.
+// Tuning knob: QLIN_I8_PAIR=0 keeps the single-CTA kernel for A/B runs.
+static int plan_i8_pair(int M, int group) {
+  static const bool enabled = [] {
+    const char* e = getenv("QLIN_I8_PAIR");
+    return !(e && atoi(e) == 0);
+  }();
+  if (!enabled || M <= 64) return 0;
+  if (group == 64) return 128;
+  if (group % 128 != 0) return 0;
+  static const int forced = [] {
+    const char* e = getenv("QLIN_I8_TN");  // tuning knob: force the pair kernel's token tile
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 128 || forced == 256) return forced;
+  return M > 128 ? 256 : 128;
+}
+
 int plan_i8_tm(int M) {
   static const int forced = [] {
     const char* e = getenv("QLIN_TM_I8");
@@ -128,7 +188,8 @@ int run_i8_gemm(int bits, const void* xq, long long kp, const float* sx, int M, 
                 const void* scales, int scale_kind, const void* bias, int bias_kind, void* y, int y_dtype,
                 long long ldy, cudaStream_t stream) {
   if (M == 0 || N == 0) return 0;
-  const int tm = plan_i8_tm(M);
+  const int tn = plan_i8_pair(M, group);
+  const int tm = tn ? tn : plan_i8_tm(M);
   GemmI8Params p{};
   p.M = M;
   p.N = N;
@@ -150,16 +211,21 @@ int run_i8_gemm(int bits, const void* xq, long long kp, const float* sx, int M, 
   p.ldy = ldy;
   p.status = reinterpret_cast<DeviceStatus*>(device_status_ptr());
   CUtensorMap tx, tw;
+  // activation box: the token tile (the pair kernel: half of it per CTA)
   int rc = make_tmap_2d(&tx, xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)kp, (uint64_t)M, (uint64_t)kp, 128,
-                        (uint32_t)tm, CU_TENSOR_MAP_SWIZZLE_128B);
+                        (uint32_t)(tn ? tn / 2 : tm), CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (bits == 4) {
     rc = make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 64,
                       128, CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
+    if (tn == 256) return launch_i8p<DecW4, 256, 1>(tx, tw, p, stream);
+    if (tn == 128) return group == 64 ? launch_i8p<DecW4, 128, 2>(tx, tw, p, stream) : launch_i8p<DecW4, 128, 1>(tx, tw, p, stream);
     return dispatch_i8<DecW4>(tm, tx, tw, p, stream);
   }
   tw = tx;
+  if (tn == 256) return launch_i8p<DecW6, 256, 1>(tx, tw, p, stream);
+  if (tn == 128) return group == 64 ? launch_i8p<DecW6, 128, 2>(tx, tw, p, stream) : launch_i8p<DecW6, 128, 1>(tx, tw, p, stream);
   return dispatch_i8<DecW6>(tm, tx, tw, p, stream);
 }
 

@@ -28,6 +28,8 @@ Transports for the gathers:
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 import qlin
@@ -74,11 +76,16 @@ def shard_rows(name, base, hidden, rank, world):
 
 
 _FIELDS = {12: ([0, 2], 5e-5), 14: ([208], 3e-5), 8: ([0], 0.02 / 127), 2: ([0], 0.02 / 7)}
+# byte offsets of the fp16 block-scale fields (d, dmin) per type
+_SCALE_OFFSETS = {12: [0, 2], 14: [208], 8: [0], 2: [0]}
 
 
 def random_gguf_rows(qtype, n, k, gen, device):
     """Random legal blocks for an [n, k] weight: uniform bytes with the fp16 scale fields replaced by
-    |N(0, 1)| * magnitude, on the device."""
+    |N(0, 1)| * magnitude, on the device.  Q4_K blocks get dmin = 7.5 * d, so that with uniform codes
+    and sub-block scales a block's weights d * sc * q - dmin * m average zero; otherwise every weight
+    shares a positive offset that amplifies any common component of the activations about K-fold
+    per layer."""
     name, qk, ts = qlin.GGUF_TYPES[qtype]
     nb = n * (k // qk)
     raw = torch.randint(0, 256, (nb, ts), dtype=torch.uint8, device=device, generator=gen)
@@ -86,15 +93,39 @@ def random_gguf_rows(qtype, n, k, gen, device):
     for off in offs:
         d = (torch.randn(nb, device=device, generator=gen).abs() * mag).to(torch.float16)
         raw[:, off:off + 2] = d.view(torch.uint8).view(nb, 2)
+    if qtype == 12:
+        d = raw[:, 0:2].contiguous().view(torch.float16).float()
+        raw[:, 2:4] = (d * 7.5).to(torch.float16).view(torch.uint8)
     return raw.view(n, (k // qk) * ts)
 
 
 def base_weight(seed, block, base, hidden, device):
-    """The full raw GGUF weight `base` of block `block` (the same on every rank)."""
+    """The full raw GGUF weight `base` of block `block` (the same on every rank).
+
+    Random blocks amplify or damp activations by a layer-dependent factor (a 12288-wide Q6_K
+    down projection about 3x), which over 60 blocks would run the stack's activations out of the
+    fp16 range.  On a CUDA device each weight is therefore calibrated once: its gain on a fixed
+    random probe, rms(x . W^T) / rms(x), is divided out of the fp16 block-scale fields (d, and dmin
+    where the type has one; each rounded to fp16 again), so the stack keeps its activations in
+    range over all 60 blocks.  The weights stay legal random GGUF blocks of the configuration's
+    types."""
     qtype, rn, ck = _BASE[base]
+    n, k = rn * hidden, ck * hidden
     gen = torch.Generator(device=device)
     gen.manual_seed(seed * 100003 + block * 16 + _BASE_INDEX[base])
-    return random_gguf_rows(qtype, rn * hidden, ck * hidden, gen, device)
+    raw = random_gguf_rows(qtype, n, k, gen, device)
+    if torch.device(device).type != "cuda":
+        return raw
+    probe = torch.randn(64, k, generator=torch.Generator().manual_seed(11)).to(torch.float16).to(device)
+    y = qlin.gguf_linear(probe, raw, qtype, (n, k), out_dtype=torch.float32)
+    gain = (y.square().mean().sqrt() / probe.float().square().mean().sqrt()).item()
+    if gain > 0 and math.isfinite(gain) and abs(math.log2(gain)) > 0.01:
+        name, qk, ts = qlin.GGUF_TYPES[qtype]
+        rows = raw.view(-1, ts)
+        for off in _SCALE_OFFSETS[qtype]:
+            field = rows[:, off:off + 2].contiguous().view(torch.float16)
+            rows[:, off:off + 2] = (field.float() / gain).to(torch.float16).view(torch.uint8)
+    return raw
 
 
 class ShardedStack:

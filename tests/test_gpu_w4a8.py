@@ -109,3 +109,37 @@ def test_rejects_bad_shapes(qlin):
     w = torch.zeros(128, 50, dtype=torch.uint8, device="cuda")
     with pytest.raises(NotImplementedError):
         qlin.w4a8_linear(x, w, torch.ones(128, 1, dtype=torch.float16, device="cuda"), bits=4, group_size=100)
+
+
+@pytest.mark.parametrize("bits,layout", [(4, 0), (6, 0), (6, 1)])
+@pytest.mark.parametrize("group", [64, 128, 256, 0])
+@pytest.mark.parametrize("m", [100, 300])
+def test_pair_kernel_int32_exact(qlin, bits, layout, group, m):
+    """Token counts above 64 run on CTA pairs (256 weight rows, 128- or 256-token tiles, decoded
+    weights in shared memory): every group's int32 sum exact through its power-of-two scale, for
+    groups of 64 (two per 128-deep stage), 128, 256 (two stages per group) and per-channel scales;
+    N = 320 leaves the odd CTA of the last pair past the last weight row."""
+    n, k = 320, 1024
+    rng = np.random.default_rng(bits * 1000 + group + m)
+    x = rng.integers(-127, 128, (m, k)).astype(np.float32)
+    x[:, 3] = 127.0  # activation scale exactly 1
+    lo, hi = (-8, 8) if bits == 4 else (-32, 32)
+    wq = rng.integers(lo, hi, (n, k)).astype(np.int8)
+    if group:
+        groups = k // group
+        s = np.ldexp(1.0, -((np.arange(n)[:, None] + np.arange(groups)[None, :]) % 3)).astype(np.float16)
+        want = np.zeros((m, n))
+        p = O.int_group_partials(x.astype(np.int64), wq, group)
+        for g in range(groups):
+            want += p[g] * s[:, g][None, :].astype(np.float64)
+    else:
+        s = np.ldexp(1.0, -rng.integers(0, 4, n)).astype(np.float32)
+        want = (x.astype(np.int64) @ wq.astype(np.int64).T).astype(np.float64) * s[None, :]
+    y = qlin.w4a8_linear(torch.from_numpy(x).half().cuda(), torch.from_numpy(_pack(wq, bits, layout).copy()).cuda(),
+                         torch.from_numpy(s).cuda(), bits=bits, group_size=group, layout=layout,
+                         out_dtype=torch.float32)
+    got = y.cpu().numpy().astype(np.float64)
+    assert np.isfinite(got).all()
+    assert np.array_equal(got, want), np.abs(got - want).max()
+    code, where = qlin.device_status()
+    assert code == 0, where
