@@ -79,6 +79,21 @@ int qlin_int8_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int6
                           int64_t ldu, int64_t rank, float lora_scale, void* y, int y_dtype, int64_t ldy,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* The INT8 LoRA linear with the down factor itself instead of t: down [rank, k] with row pitch ldd
+ * (f32 / f16 / bf16), rank <= 256.  t = x . down^T is computed inside the library by the same
+ * tensor-core GEMM on the rotated, per-row normalized fp16 activation against the down factor put
+ * through the same prologue (x . down^T = rot(x) . rot(down)^T for the orthonormal block rotation),
+ * fp32 accumulation; then the fused up-projection stages as in qlin_int8_linear_lora.  No library
+ * GEMM runs.  Replaces the reference backend's fused LoRA, whose down factor rides along the main
+ * GEMM (docs/upstream/comfy-kitchen-mps-backend.md:52-53). */
+size_t qlin_int8_linear_lora_down_workspace(int64_t m, int64_t n, int64_t k, int64_t rank);
+int qlin_int8_linear_lora_down(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
+                               int64_t n, const void* scale, int scale_dtype, const void* bias, int bias_dtype,
+                               int convrot_group, const void* lora_down, int lora_down_dtype, int64_t ldd,
+                               const void* lora_up, int lora_up_dtype, int64_t ldu, int64_t rank, float lora_scale,
+                               void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Input gradient of the INT8 ConvRot linear for a frozen weight: dx = dy . W, where
  * W = (q * scale) un-rotated per block (W = W_rot . H; H symmetric, the forward's rotation).
@@ -135,6 +150,14 @@ int qlin_gguf_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int6
                           const void* lora_t, int lora_t_dtype, int64_t ldt, const void* lora_up, int lora_up_dtype,
                           int64_t ldu, int64_t rank, float lora_scale, void* y, int y_dtype, int64_t ldy,
                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* The GGUF LoRA linear with the down factor itself (as qlin_int8_linear_lora_down, no rotation). */
+size_t qlin_gguf_linear_lora_down_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, int64_t ldx, int64_t rank);
+int qlin_gguf_linear_lora_down(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                               const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype,
+                               const void* lora_down, int lora_down_dtype, int64_t ldd, const void* lora_up,
+                               int lora_up_dtype, int64_t ldu, int64_t rank, float lora_scale, void* y, int y_dtype,
+                               int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
 /* The GGUF linear with the fp16 activation given as x_slabs column slabs, [x_slabs][m][k / x_slabs]
  * (slab i holds columns i*k/x_slabs ...; rows ldx apart, slabs x_slab_stride elements apart) —

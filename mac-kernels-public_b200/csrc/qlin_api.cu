@@ -241,6 +241,70 @@ static size_t lora_bytes(int64_t m, int64_t n, const LoraArgs* l) {
   return rk == 0 ? 0 : align256((size_t)m * rk * 2) + align256((size_t)round_up(n, 128) * rk * 2);
 }
 
+// The LoRA down factor given instead of t = x . down^T: t is computed here, by the same tensor-core
+// GEMM on the activation operand (rotated, per-row normalized fp16) against the down factor put
+// through the same prologue (x . down^T = rot(x) . rot(down)^T for the orthonormal rotation).
+struct LoraDown {
+  const void* down;  // [rank, k], row pitch ldd
+  int dtype;
+  int64_t ldd;
+};
+
+static size_t lora_down_bytes(int64_t m, int64_t k, int64_t rank) {
+  const int64_t kp = round_up(k, 64);
+  return align256((size_t)rank * kp * 2) + align256((size_t)rank * 4) + align256((size_t)m * rank * 4) +
+         align256(f16_gemm_partial_bytes((int)m, (int)rank, (int)k, WF_F16, 0, 0));
+}
+
+// t [m, rank] fp32 into the workspace; returns QLIN_OK and *t_out, or an error.
+static int compute_lora_t(const void* x, int64_t ldx, const int32_t* x_row_exp, int64_t m, int64_t k, int group,
+                          const LoraDown& d, int64_t rank, Carver& ws, cudaStream_t stream, float** t_out) {
+  if (rank <= 0 || rank > 256 || d.down == nullptr || !is_float_dtype(d.dtype) || d.ldd < k) {
+    set_error("lora: rank 1..256 and a float down factor [rank, k]");
+    return QLIN_EDECLINE;
+  }
+  const int64_t kp = round_up(k, 64);
+  void* dn = ws.take((size_t)rank * kp * 2);
+  int32_t* dexp = reinterpret_cast<int32_t*>(ws.take((size_t)rank * 4));
+  float* t = reinterpret_cast<float*>(ws.take((size_t)m * rank * 4));
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)rank, (int)k, WF_F16, 0, 0);
+  float* part = reinterpret_cast<float*>(ws.take(pb));
+  if (ws.off > ws.cap) {
+    set_error("workspace too small: need %zu bytes", ws.off);
+    return QLIN_EINVAL;
+  }
+  if (launch_prologue(d.down, d.dtype, d.ldd, (int)rank, (int)k, (int)kp, group, 0, dn, dexp, nullptr, 0, stream) != 0) {
+    set_error("lora: unsupported rotation group %d", group);
+    return QLIN_EDECLINE;
+  }
+  int rc = check_cuda("lora down prologue launch");
+  if (rc) return rc;
+  F16GemmArgs b{};
+  b.fmt = WF_F16;
+  b.x = x;
+  b.ldx = ldx;
+  b.M = (int)m;
+  b.N = (int)rank;
+  b.K = (int)k;
+  b.w = dn;
+  b.ldw = kp;
+  b.w_row_exp = dexp;
+  b.col_scale = nullptr;
+  b.col_scale_kind = CS_EXP2;
+  b.x_row_exp = x_row_exp;
+  b.bias = nullptr;
+  b.bias_kind = 0;
+  b.y = t;
+  b.y_dtype = OUT_F32;
+  b.ldy = rank;
+  b.partial = part;
+  b.partial_bytes = pb;
+  rc = run_f16_gemm(b, stream);
+  if (rc) return rc;
+  *t_out = t;
+  return QLIN_OK;
+}
+
 static int attach_lora(const LoraArgs* l, F16GemmArgs& a, Carver& ws, cudaStream_t stream) {
   if (l == nullptr) return QLIN_OK;
   if (l->rank <= 0 || l->rank > 256 || !is_float_dtype(l->t_dtype) || !is_float_dtype(l->up_dtype) ||
@@ -296,7 +360,8 @@ size_t qlin_int8_linear_workspace(int64_t m, int64_t n, int64_t k) {
 static int int8_linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
                             int64_t n, const void* scale, int scale_dtype, const void* bias, int bias_dtype,
                             int convrot_group, void* y, int y_dtype, int64_t ldy, void* workspace,
-                            size_t workspace_bytes, void* stream_, const LoraArgs* lora) {
+                            size_t workspace_bytes, void* stream_, const LoraArgs* lora,
+                            const LoraDown* down = nullptr) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (m < 0 || n < 0 || k < 0 || ldx < k || ldy < n) {
     set_error("bad sizes m=%lld n=%lld k=%lld ldx=%lld ldy=%lld", (long long)m, (long long)n, (long long)k,
@@ -347,6 +412,17 @@ static int int8_linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, in
     set_error("workspace too small: need %zu bytes", ws.off);
     return QLIN_EINVAL;
   }
+  LoraArgs with_t;
+  if (down != nullptr && lora != nullptr) {
+    float* t = nullptr;
+    rc = compute_lora_t(op.x, op.ldx, op.row_exp, m, k, convrot_group, *down, lora->rank, ws, stream, &t);
+    if (rc) return rc;
+    with_t = *lora;
+    with_t.t = t;
+    with_t.t_dtype = QLIN_F32;
+    with_t.ldt = lora->rank;
+    lora = &with_t;
+  }
   rc = attach_lora(lora, a, ws, stream);
   if (rc) return rc;
   return run_f16_gemm(a, stream);
@@ -365,6 +441,23 @@ size_t qlin_int8_linear_lora_workspace(int64_t m, int64_t n, int64_t k, int64_t 
   return f16_operand_bytes(m, k) +
          align256(f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(&l)), WF_INT8, 0, 0)) +
          lora_bytes(m, n, &l);
+}
+
+size_t qlin_int8_linear_lora_down_workspace(int64_t m, int64_t n, int64_t k, int64_t rank) {
+  return qlin_int8_linear_lora_workspace(m, n, k, rank) + lora_down_bytes(m, k, rank);
+}
+
+int qlin_int8_linear_lora_down(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
+                               int64_t n, const void* scale, int scale_dtype, const void* bias, int bias_dtype,
+                               int convrot_group, const void* lora_down, int lora_down_dtype, int64_t ldd,
+                               const void* lora_up, int lora_up_dtype, int64_t ldu, int64_t rank, float lora_scale,
+                               void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  // t is filled in by the impl; the LoraArgs carry up, rank and scale
+  const LoraArgs l{lora_down, QLIN_F32, rank, lora_up, lora_up_dtype, ldu, rank, lora_scale};
+  const LoraDown d{lora_down, lora_down_dtype, ldd};
+  return int8_linear_impl(x, x_dtype, m, k, ldx, q, n, scale, scale_dtype, bias, bias_dtype, convrot_group, y, y_dtype,
+                          ldy, workspace, workspace_bytes, stream, &l, &d);
 }
 
 int qlin_int8_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const int8_t* q, int64_t n,
@@ -494,12 +587,18 @@ int qlin_gguf_repacked_bytes(int qtype, int64_t n, int64_t k, size_t* bytes, int
     return QLIN_EDECLINE;
   }
   const int qk = gguf_block_values(qtype);
-  if (n < 0 || k <= 0 || k % qk != 0) {
-    set_error("k=%lld is not a whole number of %d-value blocks", (long long)k, qk);
+  if (n < 0 || k <= 0 || (n * k) % qk != 0 || k % 8 != 0) {
+    set_error("n*k=%lld is not a whole number of %d-value blocks (or k is not a multiple of 8)", (long long)(n * k),
+              qk);
     return QLIN_EDECLINE;
   }
   const int64_t nt = (n + 127) / 128;
-  if (bytes) *bytes = (size_t)nt * ((k + 63) / 64) * sb;
+  if (k % qk != 0) {
+    // rows straddle blocks: plain fp16 rows w * 2^-e, pitch roundup(k, 64)
+    if (bytes) *bytes = (size_t)nt * 128 * (size_t)round_up(k, 64) * 2;
+  } else {
+    if (bytes) *bytes = (size_t)nt * ((k + 63) / 64) * sb;
+  }
   if (padded_n) *padded_n = nt * 128;
   return QLIN_OK;
 }
@@ -516,6 +615,11 @@ int qlin_gguf_repack(const void* raw, int qtype, int64_t n, int64_t k, void* pac
     set_error("repack buffers: need %zu bytes (16-byte aligned) and %lld exponents", need, (long long)npad);
     return QLIN_EINVAL;
   }
+  if (k % gguf_block_values(qtype) != 0) {
+    launch_gguf_straddle_repack(reinterpret_cast<const uint8_t*>(raw), qtype, (int)n, (int)k, (int)npad,
+                                (int)round_up(k, 64), packed, row_exp, stream);
+    return check_cuda("gguf straddle repack launch");
+  }
   int P = 0, S = 0;
   const uint32_t sb = gguf_stage_bytes(qtype, &P, &S);
   launch_gguf_repack(reinterpret_cast<const uint8_t*>(raw), qtype, (int)n, (int)k, (int)((k + 63) / 64),
@@ -524,7 +628,7 @@ int qlin_gguf_repack(const void* raw, int qtype, int64_t n, int64_t k, void* pac
   return check_cuda("gguf repack launch");
 }
 
-static constexpr int kGgufFormats[] = {WF_Q4_0, WF_Q4_1, WF_Q5_0, WF_Q5_1, WF_Q8_0, WF_Q2_K,
+static constexpr int kGgufFormats[] = {WF_F16, WF_Q4_0, WF_Q4_1, WF_Q5_0, WF_Q5_1, WF_Q8_0, WF_Q2_K,
                                        WF_Q3_K, WF_Q4_K, WF_Q5_K, WF_Q6_K, WF_IQ4_NL, WF_IQ4_XS};
 
 // Workspace of the GGUF linear for any of the supported types (the largest plan's partials).
@@ -540,18 +644,20 @@ size_t qlin_gguf_linear_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, 
 static int gguf_linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
                             const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype, void* y,
                             int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream_,
-                            const LoraArgs* lora) {
+                            const LoraArgs* lora, const LoraDown* down = nullptr) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (m < 0 || n < 0 || k < 0 || ldx < k || ldy < n) {
     set_error("bad sizes");
     return QLIN_EINVAL;
   }
   if (m == 0 || n == 0) return QLIN_OK;
-  if (gguf_stage_bytes(qtype, nullptr, nullptr) == 0 || k % gguf_block_values(qtype) != 0 ||
+  if (gguf_stage_bytes(qtype, nullptr, nullptr) == 0 || (k % gguf_block_values(qtype) != 0 && k % 8 != 0) ||
       !is_float_dtype(x_dtype) || out_kind_of(y_dtype) < 0 || bias_kind_of(bias, bias_dtype) < 0) {
     set_error("unsupported GGUF type/shape/dtype (type %d, k %lld)", qtype, (long long)k);
     return QLIN_EDECLINE;
   }
+  // rows that straddle blocks were repacked to plain fp16 rows (qlin_gguf_repack)
+  const bool straddle = k % gguf_block_values(qtype) != 0;
   if (x == nullptr || packed == nullptr || row_exp == nullptr || y == nullptr) {
     set_error("null pointer");
     return QLIN_EINVAL;
@@ -561,7 +667,8 @@ static int gguf_linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, in
   int rc = make_f16_operand(x, x_dtype, m, k, ldx, 0, ws, stream, &op);
   if (rc) return rc;
   F16GemmArgs a{};
-  a.fmt = qtype;
+  a.fmt = straddle ? (int)WF_F16 : qtype;
+  a.ldw = straddle ? round_up(k, 64) : 0;
   a.x = op.x;
   a.ldx = op.ldx;
   a.M = (int)m;
@@ -577,12 +684,23 @@ static int gguf_linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, in
   a.y = y;
   a.y_dtype = out_kind_of(y_dtype);
   a.ldy = ldy;
-  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(lora)), qtype, 0, 0);
+  const size_t pb = f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(lora)), a.fmt, 0, 0);
   a.partial = reinterpret_cast<float*>(ws.take(pb));
   a.partial_bytes = pb;
   if (ws.off > ws.cap && pb > 0) {
     set_error("workspace too small: need %zu bytes", ws.off);
     return QLIN_EINVAL;
+  }
+  LoraArgs with_t;
+  if (down != nullptr && lora != nullptr) {
+    float* t = nullptr;
+    rc = compute_lora_t(op.x, op.ldx, op.row_exp, m, k, 0, *down, lora->rank, ws, stream, &t);
+    if (rc) return rc;
+    with_t = *lora;
+    with_t.t = t;
+    with_t.t_dtype = QLIN_F32;
+    with_t.ldt = lora->rank;
+    lora = &with_t;
   }
   rc = attach_lora(lora, a, ws, stream);
   if (rc) return rc;
@@ -605,6 +723,21 @@ size_t qlin_gguf_linear_lora_workspace(int64_t m, int64_t n, int64_t k, int x_dt
   for (int fmt : kGgufFormats)
     pb = std::max(pb, f16_gemm_partial_bytes((int)m, (int)n, (int)(k + lora_k_of(&l)), fmt, 0, 0));
   return f16_operand_bytes(m, k) + align256(pb) + lora_bytes(m, n, &l);
+}
+
+size_t qlin_gguf_linear_lora_down_workspace(int64_t m, int64_t n, int64_t k, int x_dtype, int64_t ldx, int64_t rank) {
+  return qlin_gguf_linear_lora_workspace(m, n, k, x_dtype, ldx, rank) + lora_down_bytes(m, k, rank);
+}
+
+int qlin_gguf_linear_lora_down(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,
+                               const int32_t* row_exp, int qtype, int64_t n, const void* bias, int bias_dtype,
+                               const void* lora_down, int lora_down_dtype, int64_t ldd, const void* lora_up,
+                               int lora_up_dtype, int64_t ldu, int64_t rank, float lora_scale, void* y, int y_dtype,
+                               int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  const LoraArgs l{lora_down, QLIN_F32, rank, lora_up, lora_up_dtype, ldu, rank, lora_scale};
+  const LoraDown d{lora_down, lora_down_dtype, ldd};
+  return gguf_linear_impl(x, x_dtype, m, k, ldx, packed, row_exp, qtype, n, bias, bias_dtype, y, y_dtype, ldy,
+                          workspace, workspace_bytes, stream, &l, &d);
 }
 
 int qlin_gguf_linear_lora(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, const void* packed,

@@ -1223,6 +1223,44 @@ int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int
   return 0;
 }
 
+// GGUF weights whose rows straddle blocks (K not a whole number of blocks; the blocks run over
+// the flattened [N, K] tensor): decoded once by flat element into plain fp16 rows w * 2^-e, [n_pad,
+// ldw] (zeros past K and past N), with e the row exponent of the row's largest |w| (as for the
+// other layouts: that weight lands in [2^14, 2^15)).  One CTA per row: a max pass, then the writes.
+__global__ void gguf_straddle_repack_kernel(const uint8_t* __restrict__ raw, int qtype, int N, int K, int ldw,
+                                            __half* __restrict__ out, int32_t* __restrict__ row_exp) {
+  const int n = blockIdx.x;
+  __shared__ float red[32];
+  __shared__ int e_row;
+  float mx = 0.f;
+  if (n < N)
+    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(gguf_value(raw, qtype, (long long)n * K + k)));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+    int ex = 0;
+    if (m > 0.f) frexpf(m, &ex);
+    e_row = m > 0.f ? ex - 15 : 0;
+    row_exp[n] = e_row;
+  }
+  __syncthreads();
+  const float sc = exp2i(-e_row);
+  for (int k = threadIdx.x; k < ldw; k += blockDim.x) {
+    float v = 0.f;
+    if (n < N && k < K) v = __fmul_rn(gguf_value(raw, qtype, (long long)n * K + k), sc);
+    out[(size_t)n * ldw + k] = __float2half_rn(v);
+  }
+}
+
+void launch_gguf_straddle_repack(const uint8_t* raw, int qtype, int N, int K, int n_pad, int ldw, void* out,
+                                 int32_t* row_exp, cudaStream_t s) {
+  if (n_pad == 0) return;
+  gguf_straddle_repack_kernel<<<n_pad, 256, 0, s>>>(raw, qtype, N, K, ldw, reinterpret_cast<__half*>(out), row_exp);
+}
+
 void launch_gguf_dequant(const uint8_t* raw, int qtype, long long total, void* out, int out_dtype, cudaStream_t s) {
   if (total == 0) return;
   const long long threads = (total + 3) / 4;

@@ -109,6 +109,26 @@ struct DecInt8 {
   }
 };
 
+// Plain fp16 weights (the LoRA down factor after the activation prologue, and GGUF rows that
+// straddle blocks after their one-time decode to w * 2^-e): [N, ldw] row-major via a TMA box
+// {64 values, 128 rows} with 128-byte swizzle, so 16-byte chunk j of row r sits at
+// r * 128 + 16 * (j ^ (r & 7)).  The values are the operand already: the decode is a copy.
+struct DecF16 {
+  static constexpr uint32_t kStageBytes = 128 * 128;
+  static constexpr bool kTma = true;
+  __device__ __forceinline__ static void decode(const uint8_t* st, int r, float /*row_scale*/, uint32_t (&out)[32]) {
+    const uint8_t* row = st + r * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(row + ((j ^ (r & 7)) << 4));
+      out[4 * j] = v.x;
+      out[4 * j + 1] = v.y;
+      out[4 * j + 2] = v.z;
+      out[4 * j + 3] = v.w;
+    }
+  }
+};
+
 template <int P, int S>
 struct PlaneStage {
   static constexpr uint32_t kStageBytes = 128 * (16 * P + S);

@@ -407,6 +407,11 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
     rc = make_tmap_2d(&tw, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, 64,
                       128, CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
+  } else if (a.fmt == WF_F16) {
+    const long long ldw = a.ldw > 0 ? a.ldw : a.K;
+    rc = make_tmap_2d(&tw, a.w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)ldw * 2,
+                      64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
   } else {
     tw = tx;  // unused by bulk-copy decoders
   }
@@ -434,6 +439,7 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
         rc = dispatch_tm<DecInt8>(tx, tw, tp, tt, maps, p, tm, pair, stream);
       }
       break;
+    case WF_F16: rc = dispatch_tm<DecF16>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     case WF_Q8_0: rc = dispatch_tm<DecQ8_0>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     case WF_Q4_0: rc = dispatch_tm<DecQ4_0>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;
     case WF_IQ4_NL: rc = dispatch_tm<DecIQ4<false>>(tx, tw, tp, tt, maps, p, tm, pair, stream); break;

@@ -14,6 +14,8 @@ int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int
                     int32_t* row_exp, float* row_scale, int perm, cudaStream_t stream);
 void launch_gguf_dequant(const uint8_t* raw, int qtype, long long total, void* out, int out_dtype, cudaStream_t s);
 void launch_gguf_row_exp(const uint8_t* raw, int qtype, int N, int K, int n_pad, int32_t* row_exp, cudaStream_t s);
+void launch_gguf_straddle_repack(const uint8_t* raw, int qtype, int N, int K, int n_pad, int ldw, void* out,
+                                 int32_t* row_exp, cudaStream_t s);
 void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_stages, int n_tiles, uint8_t* out,
                         uint32_t stage_bytes, int P, int S, cudaStream_t s);
 void launch_splitk_finalize(const float* partial, int splits, int M, int N, int Mp, const void* col_scale,
@@ -40,7 +42,7 @@ void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* co
 
 // Weight formats of the f16 (weight-only) GEMM family.
 enum WFormat : int {
-  WF_INT8 = 0, WF_Q4_0 = 2, WF_Q4_1 = 3, WF_Q5_0 = 6, WF_Q5_1 = 7, WF_Q8_0 = 8, WF_Q2_K = 10, WF_Q3_K = 11,
+  WF_INT8 = 0, WF_F16 = 1, WF_Q4_0 = 2, WF_Q4_1 = 3, WF_Q5_0 = 6, WF_Q5_1 = 7, WF_Q8_0 = 8, WF_Q2_K = 10, WF_Q3_K = 11,
   WF_Q4_K = 12, WF_Q5_K = 13, WF_Q6_K = 14, WF_IQ4_NL = 20, WF_IQ4_XS = 23
 };
 
@@ -51,7 +53,8 @@ struct F16GemmArgs {
   int x_slabs = 1;             // > 1: X is [x_slabs][M][K / x_slabs] (e.g. an all-gather of column shards)
   long long x_slab_stride = 0;  // elements between slabs
   int M, N, K;
-  const void* w;  // INT8: raw int8 [N, K]; GGUF: repacked stages
+  const void* w;  // INT8: raw int8 [N, K]; F16: fp16 [N, ldw]; GGUF: repacked stages
+  long long ldw = 0;  // F16 weights: row pitch in elements (0: K)
   const int32_t* w_row_exp;
   const void* col_scale;
   int col_scale_kind;

@@ -109,14 +109,14 @@ def int8_linear(x, qdata, scale, bias=None, out_dtype=None, convrot=False, convr
     y2 = y.view(m, n)
     lora = _lora_fused_args(x2, lora_down, lora_up, lora_scale) if lora_down is not None else None
     if lora is not None:
-        t, u, rank, ls = lora
-        ws, wsb = _workspace(lib.qlin_int8_linear_lora_workspace(m, n, k, rank), x.device)
-        check(lib.qlin_int8_linear_lora(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), q.data_ptr(), n,
-                                        sc.data_ptr(), _DT[sc.dtype], None if b is None else b.data_ptr(),
-                                        0 if b is None else _DT[b.dtype], group, t.data_ptr(), _DT[t.dtype],
-                                        t.stride(0), u.data_ptr(), _DT[u.dtype], u.stride(0), rank, ls,
-                                        y2.data_ptr(), _DT[y2.dtype], n, None if ws is None else ws.data_ptr(), wsb,
-                                        _stream(x.device)), "qlin_int8_linear_lora")
+        d, u, rank, ls = lora
+        ws, wsb = _workspace(lib.qlin_int8_linear_lora_down_workspace(m, n, k, rank), x.device)
+        check(lib.qlin_int8_linear_lora_down(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), q.data_ptr(), n,
+                                             sc.data_ptr(), _DT[sc.dtype], None if b is None else b.data_ptr(),
+                                             0 if b is None else _DT[b.dtype], group, d.data_ptr(), _DT[d.dtype],
+                                             d.stride(0), u.data_ptr(), _DT[u.dtype], u.stride(0), rank, ls,
+                                             y2.data_ptr(), _DT[y2.dtype], n, None if ws is None else ws.data_ptr(),
+                                             wsb, _stream(x.device)), "qlin_int8_linear_lora_down")
         return y
     ws, wsb = _workspace(lib.qlin_int8_linear_workspace(m, n, k), x.device)
     check(lib.qlin_int8_linear(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), q.data_ptr(), n, sc.data_ptr(),
@@ -182,19 +182,18 @@ def _lora_beside(y, x, down, up, scale):
 
 
 def _lora_fused_args(x2, down, up, scale):
-    """Operands of the fused LoRA (extra K stages of the GEMM): t = x . down^T in fp32 (a plain
-    cuBLAS GEMM with fp32 accumulation), up as stored, the rank and the scale; None when the LoRA
-    must run beside the layer (rank above 256, shapes that do not match)."""
+    """Operands of the fused LoRA: the down factor [rank, K] and up [N, rank] as stored (float, unit
+    inner stride), the rank and the scale; the library computes t = x . down^T with its own GEMM and
+    runs the up-projection as extra K stages of the linear's GEMM.  None when the LoRA must run
+    beside the layer (rank above 256, shapes that do not match)."""
     if up is None or down.dim() != 2 or up.dim() != 2 or down.shape[0] != up.shape[1] or down.shape[0] > 256:
         return None
     if down.shape[1] != x2.shape[1] or not down.is_cuda or not up.is_cuda:
         return None
-    if x2.dtype in (torch.float16, torch.bfloat16):
-        t = torch.mm(x2, down.to(x2.dtype).t(), out_dtype=torch.float32)
-    else:
-        t = torch.mm(x2.float(), down.float().t())
-    u = up if (up.dtype in (torch.float16, torch.bfloat16, torch.float32) and up.stride(-1) == 1) else up.float().contiguous()
-    return t, u, int(down.shape[0]), 1.0 if scale is None else float(scale)
+    fl = (torch.float16, torch.bfloat16, torch.float32)
+    d = down if (down.dtype in fl and down.stride(-1) == 1) else down.float().contiguous()
+    u = up if (up.dtype in fl and up.stride(-1) == 1) else up.float().contiguous()
+    return d, u, int(down.shape[0]), 1.0 if scale is None else float(scale)
 
 
 # ---------------------------------------------------------------------------------------------- GGUF
@@ -254,14 +253,15 @@ def gguf_linear(x, weight, qtype, shape, bias=None, out_dtype=None, lora_down=No
     y2 = y.view(m, n)
     lora = _lora_fused_args(x2, lora_down, lora_up, lora_scale) if lora_down is not None else None
     if lora is not None:
-        t, u, rank, ls = lora
-        ws, wsb = _workspace(lib.qlin_gguf_linear_lora_workspace(m, n, k, _DT[x2.dtype], x2.stride(0), rank), x.device)
-        check(lib.qlin_gguf_linear_lora(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), packed.data_ptr(),
-                                        row_exp.data_ptr(), qtype, n, None if b is None else b.data_ptr(),
-                                        0 if b is None else _DT[b.dtype], t.data_ptr(), _DT[t.dtype], t.stride(0),
-                                        u.data_ptr(), _DT[u.dtype], u.stride(0), rank, ls, y2.data_ptr(),
-                                        _DT[y2.dtype], n, None if ws is None else ws.data_ptr(), wsb,
-                                        _stream(x.device)), "qlin_gguf_linear_lora")
+        d, u, rank, ls = lora
+        ws, wsb = _workspace(lib.qlin_gguf_linear_lora_down_workspace(m, n, k, _DT[x2.dtype], x2.stride(0), rank),
+                             x.device)
+        check(lib.qlin_gguf_linear_lora_down(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), packed.data_ptr(),
+                                             row_exp.data_ptr(), qtype, n, None if b is None else b.data_ptr(),
+                                             0 if b is None else _DT[b.dtype], d.data_ptr(), _DT[d.dtype], d.stride(0),
+                                             u.data_ptr(), _DT[u.dtype], u.stride(0), rank, ls, y2.data_ptr(),
+                                             _DT[y2.dtype], n, None if ws is None else ws.data_ptr(), wsb,
+                                             _stream(x.device)), "qlin_gguf_linear_lora_down")
         return y
     ws, wsb = _workspace(lib.qlin_gguf_linear_workspace(m, n, k, _DT[x2.dtype], x2.stride(0)), x.device)
     check(lib.qlin_gguf_linear(x2.data_ptr(), _DT[x2.dtype], m, k, x2.stride(0), packed.data_ptr(),

@@ -30,6 +30,9 @@ SIGNATURES = {
     "qlin_int8_linear_lora_workspace": (_sz, [_i64, _i64, _i64, _i64]),
     "qlin_int8_linear_lora": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i, _p, _i, _i, _p, _i, _i64, _p, _i, _i64,
                                    _i64, ctypes.c_float, _p, _i, _i64, _p, _sz, _p]),
+    "qlin_int8_linear_lora_down_workspace": (_sz, [_i64, _i64, _i64, _i64]),
+    "qlin_int8_linear_lora_down": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i, _p, _i, _i, _p, _i, _i64, _p, _i,
+                                        _i64, _i64, ctypes.c_float, _p, _i, _i64, _p, _sz, _p]),
     "qlin_int8_grad_weight_bytes": (_sz, [_i64, _i64]),
     "qlin_int8_grad_weight": (_i, [_p, _i64, _i64, _p, _sz, _p]),
     "qlin_int8_linear_grad_input_workspace": (_sz, [_i64, _i64, _i64, _i]),
@@ -41,6 +44,9 @@ SIGNATURES = {
     "qlin_gguf_linear_lora_workspace": (_sz, [_i64, _i64, _i64, _i, _i64, _i64]),
     "qlin_gguf_linear_lora": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _i, _i64,
                                    _i64, ctypes.c_float, _p, _i, _i64, _p, _sz, _p]),
+    "qlin_gguf_linear_lora_down_workspace": (_sz, [_i64, _i64, _i64, _i, _i64, _i64]),
+    "qlin_gguf_linear_lora_down": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _i, _i64,
+                                        _i64, ctypes.c_float, _p, _i, _i64, _p, _sz, _p]),
     "qlin_gguf_linear_slabs": (_i, [_p, _i64, _i64, _i64, _i, _i64, _p, _p, _i, _i64, _p, _i, _p, _i, _i64, _p, _sz,
                                     _p]),
     "qlin_gguf_linear_allgather": (_i, [_p, _i64, _i64, _i64, _i, _i64, _p, _p, _i, _i64, _p, _i, _i, _i,

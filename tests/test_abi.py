@@ -34,6 +34,9 @@ def test_version_and_host_side_declines_without_gpu():
     for unsupported in (9, 15, 16, 21):  # Q8_1, Q8_K, IQ2_XXS, IQ3_S
         assert lib.qlin_gguf_repacked_bytes(unsupported, 10, 256, ctypes.byref(size), ctypes.byref(npad)) == 1
     assert lib.qlin_gguf_repacked_bytes(12, 10, 300, ctypes.byref(size), ctypes.byref(npad)) == 1
+    # rows that straddle blocks (the flattened tensor is whole blocks): plain fp16 rows, pitch 64-aligned
+    assert lib.qlin_gguf_repacked_bytes(12, 64, 1152, ctypes.byref(size), ctypes.byref(npad)) == 0
+    assert npad.value == 128 and size.value == 128 * 1152 * 2
     assert lib.qlin_gguf_repacked_bytes(12, 130, 512, ctypes.byref(size), ctypes.byref(npad)) == 0
     assert npad.value == 256 and size.value == 2 * 8 * 128 * 40
     # every supported type: bytes per 64-value stage of a 128-row tile (16 B planes + side record)

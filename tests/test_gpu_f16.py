@@ -329,3 +329,42 @@ def test_small_m_int8_matches_fp64(qlin, m, out_dtype):
     got = y.float().cpu().numpy()
     assert np.isfinite(got).all()
     assert O.max_abs_rel(got, ref) <= TOL[out_dtype], O.max_abs_rel(got, ref)
+
+
+STRADDLE = [(8, 128, 1040), (2, 70, 1104), (12, 64, 1152), (14, 130, 640), (11, 40, 1600), (23, 96, 1920),
+            (20, 200, 336)]
+
+
+@pytest.mark.parametrize("qtype,n,k", STRADDLE)
+@pytest.mark.parametrize("m", [1, 45, 300])
+def test_gguf_linear_rows_straddling_blocks(qlin, qtype, n, k, m):
+    """Weights whose rows are not whole blocks (ComfyUI-GGUF's orig_shape layers: the blocks run
+    over the flattened [N, K] tensor) run the linear too: decoded once by flat element to fp16
+    w * 2^-e per row, then the same tensor-core GEMM.  Against gguf-py's decode in float64."""
+    qk = O.GGUF_TYPES[qtype][1]
+    assert k % qk != 0 and (n * k) % qk == 0
+    raw = O.random_gguf_blocks(qtype, 1, n * k, seed=qtype + m)  # one flat run of blocks
+    w = O.gguf_dequantize(raw, qtype, 1, n * k).reshape(n, k)
+    g = torch.Generator().manual_seed(m + k)
+    x = torch.randn(m, k, generator=g).to(torch.float16)
+    b = (torch.randn(n, generator=g) * 0.1).to(torch.float16)
+    ref = O.linear_f64(x.float().numpy(), w, b.float().numpy())
+    y = qlin.gguf_linear(x.cuda(), torch.from_numpy(raw).cuda(), qtype, (n, k), bias=b.cuda())
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.max_abs_rel(got, ref) <= 2e-3, O.max_abs_rel(got, ref)
+    _check_status(qlin)
+
+
+@pytest.mark.parametrize("qtype,n,k", STRADDLE[:3])
+def test_straddling_rows_decoded_exactly_once_rounded(qlin, qtype, n, k):
+    """One-hot activation rows pull single weights through the straddle path: each equals the
+    exact decode rounded once to fp16 at its row's power of two, RN16(w * 2^-e) * 2^e."""
+    raw = O.random_gguf_blocks(qtype, 1, n * k, seed=3)
+    w = O.gguf_dequantize(raw, qtype, 1, n * k).reshape(n, k).astype(np.float64)
+    amax = np.abs(w).max(axis=1)
+    e = np.where(amax > 0, np.frexp(amax)[1] - 15, 0)
+    exact = (np.ldexp(w, -e[:, None]).astype(np.float16).astype(np.float64) * np.ldexp(1.0, e)[:, None]).T
+    eye = torch.eye(k, dtype=torch.float16).cuda()
+    y = qlin.gguf_linear(eye, torch.from_numpy(raw).cuda(), qtype, (n, k), out_dtype=torch.float32).cpu().numpy()
+    assert np.array_equal(y.astype(np.float64), exact)

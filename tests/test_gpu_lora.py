@@ -71,3 +71,42 @@ def test_rank_above_256_runs_beside(qlin):
     y = qlin.int8_linear(x.cuda(), q.cuda(), s.cuda(), b.cuda(), torch.float16, convrot=True, convrot_groupsize=128,
                          lora_down=down.cuda(), lora_up=up.cuda(), lora_scale=0.5)
     assert O.max_abs_rel(y.float().cpu().numpy(), ref) <= 3e-3
+
+
+@pytest.mark.parametrize("path", ["int8", "gguf"])
+def test_fused_lora_launches_no_library_gemm(qlin, path, monkeypatch):
+    """The fused LoRA computes t = x . down^T itself: no torch / cuBLAS / CUTLASS GEMM is called or
+    launched, every GEMM-like kernel of the call belongs to libqlin."""
+    m, n, k, rank = 300, 512, 1024, 64
+    x, q, s, b = O.cfg_int8_convrot(m, k, n, seed=4)
+    down, up = _lora(n, k, rank, 5, torch.bfloat16)
+    raw = torch.from_numpy(O.random_gguf_blocks(8, n, k, seed=6)).cuda()
+    xd, qd, sd, bd, dd, ud = x.cuda().bfloat16(), q.cuda(), s.cuda(), b.cuda(), down.cuda(), up.cuda()
+
+    def call():
+        if path == "int8":
+            return qlin.int8_linear(xd, qd, sd, bd, torch.bfloat16, convrot=True, convrot_groupsize=128,
+                                    lora_down=dd, lora_up=ud, lora_scale=0.5)
+        return qlin.gguf_linear(xd, raw, 8, (n, k), bias=bd, lora_down=dd, lora_up=ud, lora_scale=0.5)
+
+    call()  # repack / warm-up outside the profiled call
+    torch.cuda.synchronize()
+
+    def forbidden(*a, **kw):
+        raise AssertionError("library GEMM called on the fused LoRA path")
+
+    monkeypatch.setattr(torch, "mm", forbidden)
+    monkeypatch.setattr(torch, "matmul", forbidden)
+    monkeypatch.setattr(torch.nn.functional, "linear", forbidden)
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        y = call()
+        torch.cuda.synchronize()
+    monkeypatch.undo()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    gemmish = [nm for nm in names if any(t in nm.lower() for t in ("gemm", "cutlass", "cublas", "xmma", "nvjet"))]
+    assert gemmish and all("qlin" in nm for nm in gemmish), gemmish
+    ref = O.int8_convrot_linear_ref(x.bfloat16().float().numpy(), q.numpy(), s.float().numpy(), b.float().numpy(),
+                                    group=128) if path == "int8" else \
+        O.linear_f64(x.bfloat16().float().numpy(), O.gguf_dequantize(raw.cpu().numpy(), 8, n, k), b.float().numpy())
+    ref = ref + _side(x.bfloat16(), down, up, 0.5)
+    assert O.max_abs_rel(y.float().cpu().numpy(), ref) <= 8e-3
