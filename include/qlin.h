@@ -48,6 +48,16 @@ const char* qlin_last_error(void);
  * clears it. */
 int qlin_device_status(int reset, uint32_t* where);
 
+/* Bounds record of the library built with -DQLIN_CHECKS (libqlin_checked.so; the library is
+ * otherwise the same).  That build tests every global access the hardware does not bound by
+ * itself, and every computed shared-memory index, against limits the host derives from the
+ * arguments of each call; a failed check skips the access and is recorded, never trapped.
+ * Writes the number of failed checks since the last reset to *count and the first failure's site
+ * (see qlin_checks.cuh), index, limit and block.  Returns QLIN_OK, or QLIN_EDECLINE from a library
+ * built without checks.  reset != 0 clears the record.  Synchronizes the device.  No counterpart
+ * in the reference (it has no such build). */
+int qlin_bounds_check(int reset, uint32_t* count, uint32_t* site, int64_t* index, int64_t* limit, uint32_t* block);
+
 /* ------------------------------------------------------------------------------------------
  * INT8 ConvRot weight-only linear.
  * Replaces comfy-kitchen `int8_linear(x, qdata, scale, bias, out_dtype, convrot, convrot_groupsize)`

@@ -170,6 +170,9 @@ static int noalloc_scratch(void** out) {
   return QLIN_OK;
 }
 
+// This translation unit's bounds record (QLIN_CHECKS build).
+QLIN_BOUNDS_READER(bounds_read_api)
+
 }  // namespace qlin
 
 using namespace qlin;
@@ -202,6 +205,10 @@ static int gguf_slabs_impl(const void* x, int64_t m, int64_t k, int64_t ldx, int
   a.N = (int)n;
   a.K = (int)k;
   a.w = packed;
+  {
+    size_t wb = 0;
+    if (qlin_gguf_repacked_bytes(qtype, n, k, &wb, nullptr) == QLIN_OK) a.w_bytes = (long long)wb;
+  }
   a.w_row_exp = row_exp;
   a.col_scale_kind = CS_EXP2;
   a.bias = bias;
@@ -335,6 +342,30 @@ extern "C" {
 const char* qlin_version(void) { return "qlin 0.1 (sm_100a, tcgen05)"; }
 
 const char* qlin_last_error(void) { return g_err; }
+
+int qlin_bounds_check(int reset, uint32_t* count, uint32_t* site, int64_t* index, int64_t* limit, uint32_t* block) {
+  int (*const readers[])(BoundsRecord*, int) = {bounds_read_api, bounds_read_aux,  bounds_read_f16, bounds_read_f16_blk,
+                                                bounds_read_f16_kq, bounds_read_gemv, bounds_read_i8};
+  uint32_t total = 0;
+  BoundsRecord first{};
+  for (auto rd : readers) {
+    BoundsRecord r{};
+    const int rc = rd(&r, reset);
+    if (rc < 0) return check_cuda("bounds record read");
+    if (rc > 0) {
+      set_error("this library was built without QLIN_CHECKS");
+      return QLIN_EDECLINE;
+    }
+    if (r.count > 0 && total == 0) first = r;
+    total += r.count;
+  }
+  if (count) *count = total;
+  if (site) *site = first.site;
+  if (index) *index = first.index;
+  if (limit) *limit = first.limit;
+  if (block) *block = first.block;
+  return QLIN_OK;
+}
 
 int qlin_device_status(int reset, uint32_t* where) {
   void* p = device_status_ptr();
@@ -617,13 +648,13 @@ int qlin_gguf_repack(const void* raw, int qtype, int64_t n, int64_t k, void* pac
   }
   if (k % gguf_block_values(qtype) != 0) {
     launch_gguf_straddle_repack(reinterpret_cast<const uint8_t*>(raw), qtype, (int)n, (int)k, (int)npad,
-                                (int)round_up(k, 64), packed, row_exp, stream);
+                                (int)round_up(k, 64), packed, packed_bytes, row_exp, stream);
     return check_cuda("gguf straddle repack launch");
   }
   int P = 0, S = 0;
   const uint32_t sb = gguf_stage_bytes(qtype, &P, &S);
   launch_gguf_repack(reinterpret_cast<const uint8_t*>(raw), qtype, (int)n, (int)k, (int)((k + 63) / 64),
-                     (int)(npad / 128), reinterpret_cast<uint8_t*>(packed), sb, P, S, stream);
+                     (int)(npad / 128), reinterpret_cast<uint8_t*>(packed), packed_bytes, sb, P, S, stream);
   launch_gguf_row_exp(reinterpret_cast<const uint8_t*>(raw), qtype, (int)n, (int)k, (int)npad, row_exp, stream);
   return check_cuda("gguf repack launch");
 }
@@ -675,6 +706,10 @@ static int gguf_linear_impl(const void* x, int x_dtype, int64_t m, int64_t k, in
   a.N = (int)n;
   a.K = (int)k;
   a.w = packed;
+  {
+    size_t wb = 0;
+    if (qlin_gguf_repacked_bytes(qtype, n, k, &wb, nullptr) == QLIN_OK) a.w_bytes = (long long)wb;
+  }
   a.w_row_exp = row_exp;
   a.col_scale = nullptr;
   a.col_scale_kind = CS_EXP2;

@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
   extern __shared__ float srow[];
   __shared__ float red[33];
   const int row = blockIdx.x;
+  if (!qchk(BS_PRO_X, row, M)) return;  // the whole block: row is uniform
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   constexpr int G = 32 * E;
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
     for (int e = 0; e < E; ++e) {
       float t = (MODE == 1) ? round_to(v[e], x_dtype) : v[e];
       amax = fmaxf(amax, fabsf(t));
-      if (staged) srow[c + e] = v[e];
+      if (staged && qchk_smem(BS_PRO_OUT, srow, srow + c + e, 4)) srow[c + e] = v[e];
     }
   }
   amax = block_max(amax, red);  // contains __syncthreads, so srow is complete afterwards
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
   auto value_at = [&](int c, float (&v8)[8]) {
     if (staged) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v8[e] = srow[c + e];
+      for (int e = 0; e < 8; ++e) v8[e] = qchk_smem(BS_PRO_OUT, srow, srow + c + e, 4) ? srow[c + e] : 0.f;
     }
   };
   if (MODE == 0) {
@@ -160,7 +161,7 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
         uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
         for (int e = 0; e < 4; ++e) pw[e] = pack_f16x2(scale_pow2(v8[2 * e], f), scale_pow2(v8[2 * e + 1], f));
-        *reinterpret_cast<uint4*>(o + c) = pk;
+        if (qchk_span(BS_PRO_OUT, (long long)row * Kp + c, 8, (long long)M * Kp)) *reinterpret_cast<uint4*>(o + c) = pk;
       }
     } else {
       for (int b = warp; b < nblk; b += nwarps) {
@@ -201,7 +202,8 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
           lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
           hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
         }
-        *reinterpret_cast<uint2*>(o + c) = make_uint2(lo, hi);
+        if (qchk_span(BS_PRO_OUT, (long long)row * Kp + c, 8, (long long)M * Kp))
+          *reinterpret_cast<uint2*>(o + c) = make_uint2(lo, hi);
       }
     } else {
       for (int b = warp; b < nblk; b += nwarps) {
@@ -213,7 +215,8 @@ __global__ void __launch_bounds__(256) prologue_kernel(const void* __restrict__ 
         for (int e = 0; e < E; ++e) {
           const int col = c + e;
           const int dst = perm ? ((col & ~7) | ((col & 1) ? 4 + ((col & 7) >> 1) : ((col & 7) >> 1))) : col;
-          if (col < Kp) o[dst] = (col < K) ? static_cast<int8_t>(quant(v[e])) : 0;
+          if (col < Kp && qchk(BS_PRO_OUT, (long long)row * Kp + dst, (long long)M * Kp))
+            o[dst] = (col < K) ? static_cast<int8_t>(quant(v[e])) : 0;
         }
       }
     }
@@ -230,6 +233,7 @@ __global__ void __launch_bounds__(512) prologue_reg_kernel(const void* __restric
                                                             float* __restrict__ row_scale, int perm, int vec) {
   __shared__ float red[33];
   const int row = blockIdx.x;
+  if (!qchk(BS_PRO_X, row, M)) return;  // the whole block: row is uniform
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5;
   constexpr int G = 32 * E;
@@ -265,7 +269,7 @@ __global__ void __launch_bounds__(512) prologue_reg_kernel(const void* __restric
       const int b = warp + nw * i;
       if (b < nblk) {
         const int c = b * G + lane * E;
-        if (c + E <= Kp) {
+        if (c + E <= Kp && qchk_span(BS_PRO_OUT, (long long)row * Kp + c, E, (long long)M * Kp)) {
           uint32_t w[(E + 1) / 2];
 #pragma unroll
           for (int e = 0; e < E; e += 2)
@@ -303,13 +307,15 @@ __global__ void __launch_bounds__(512) prologue_reg_kernel(const void* __restric
             lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
             hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
           }
-          if (c + 8 <= Kp) *reinterpret_cast<uint2*>(o + c) = make_uint2(lo, hi);
+          if (c + 8 <= Kp && qchk_span(BS_PRO_OUT, (long long)row * Kp + c, 8, (long long)M * Kp))
+            *reinterpret_cast<uint2*>(o + c) = make_uint2(lo, hi);
         } else {
 #pragma unroll
           for (int e = 0; e < E; ++e) {
             const int col = c + e;
             const int dst = perm ? ((col & ~7) | ((col & 1) ? 4 + ((col & 7) >> 1) : ((col & 7) >> 1))) : col;
-            if (col < Kp) o[dst] = static_cast<int8_t>(q[e]);
+            if (col < Kp && qchk(BS_PRO_OUT, (long long)row * Kp + dst, (long long)M * Kp))
+              o[dst] = static_cast<int8_t>(q[e]);
           }
         }
       }
@@ -470,6 +476,8 @@ __global__ void gguf_dequant_kernel(const uint8_t* __restrict__ raw, int qtype, 
   for (int t = 0; t < 4; ++t) {
     const long long i = i0 + t;
     if (i >= total) return;
+    const int qk = gguf_qk(qtype), ts = gguf_ts(qtype);
+    if (!qchk_span(BS_REPACK_SRC, (i / qk) * ts, ts, (total + qk - 1) / qk * ts)) return;
     const float v = gguf_value(raw, qtype, i);
     if (out_dtype == 0) reinterpret_cast<float*>(out)[i] = v;
     else if (out_dtype == 1) reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
@@ -538,11 +546,13 @@ __global__ void gguf_row_exp_kernel(const uint8_t* __restrict__ raw, int qtype, 
     const int qk = gguf_qk(qtype), ts = gguf_ts(qtype);
     const int nb = K / qk;
     const uint8_t* r = raw + (long long)row * nb * ts;
-    for (int blk = lane; blk < nb; blk += 32) bound = fmax(bound, gguf_block_bound(r + (long long)blk * ts, qtype));
+    for (int blk = lane; blk < nb; blk += 32)
+      if (qchk_span(BS_REPACK_SRC, ((long long)row * nb + blk) * ts, ts, (long long)N * nb * ts))
+        bound = fmax(bound, gguf_block_bound(r + (long long)blk * ts, qtype));
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) bound = fmax(bound, __shfl_xor_sync(0xffffffffu, bound, o));
-  if (lane == 0) {
+  if (lane == 0 && qchk(BS_REPACK_DST, row, n_pad)) {
     int e = 0;
     if (bound > 0.0 && bound < 1e300) {
       int ex;
@@ -584,7 +594,7 @@ __device__ __forceinline__ void iq4_selector_order(const uint8_t* qs, uint8_t* o
 // One-time repack of raw GGUF rows into the pipeline-stage layout documented in qlin_decode.cuh.
 // grid = (num_k_stages, n_tiles), block = 128 (one thread per weight row of the tile).
 __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, int N, int K, int num_k_stages,
-                                   uint8_t* __restrict__ out, uint32_t stage_bytes, int P, int S) {
+                                   uint8_t* __restrict__ out, uint32_t stage_bytes, int P, int S, long long out_bytes) {
   const int kst = blockIdx.x, nt = blockIdx.y, r = threadIdx.x;
   const int n = nt * 128 + r;
   uint8_t* st = out + ((size_t)nt * num_k_stages + kst) * stage_bytes;
@@ -603,6 +613,7 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
         const int kb = k0 / 32 + blk;
         if (kb * 32 >= K) break;
         const uint8_t* b = row + (long long)kb * ts;
+        if (!qchk_span(BS_REPACK_SRC, ((long long)n * (K / 32) + kb) * ts, ts, (long long)N * (K / 32) * ts)) break;
         switch (qtype) {
           case GGUF_Q8_0:
           case GGUF_Q4_0: {
@@ -637,7 +648,9 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
     } else {
       const uint8_t* b = raw + ((long long)n * (K / 256) + k0 / 256) * ts;
       const int c = (k0 % 256) / 64;  // the stage holds superblock values 64c .. 64c+63
-      switch (qtype) {
+      const bool b_in =
+          qchk_span(BS_REPACK_SRC, ((long long)n * (K / 256) + k0 / 256) * ts, ts, (long long)N * (K / 256) * ts);
+      switch (b_in ? qtype : -1) {
         case GGUF_Q2_K:
         case GGUF_Q3_K: {
           const uint8_t* qs = b + (qtype == GGUF_Q2_K ? 16 : 32);
@@ -706,9 +719,16 @@ __global__ void gguf_repack_kernel(const uint8_t* __restrict__ raw, int qtype, i
       }
     }
   }
+  const long long st_off = ((long long)nt * num_k_stages + kst) * stage_bytes;
   for (int j = 0; j < P; ++j)
-    for (int i = 0; i < 16; ++i) st[(j * 128 + r) * 16 + i] = payload[j * 16 + i];
-  for (int i = 0; i < S; ++i) st[128 * 16 * P + r * S + i] = side[i];
+    for (int i = 0; i < 16; ++i)
+      if (qchk(BS_REPACK_DST, (j * 128 + r) * 16 + i, stage_bytes) &&
+          qchk(BS_REPACK_DST, st_off + (j * 128 + r) * 16 + i, out_bytes))
+        st[(j * 128 + r) * 16 + i] = payload[j * 16 + i];
+  for (int i = 0; i < S; ++i)
+    if (qchk(BS_REPACK_DST, 128 * 16 * P + r * S + i, stage_bytes) &&
+        qchk(BS_REPACK_DST, st_off + 128 * 16 * P + r * S + i, out_bytes))
+      st[128 * 16 * P + r * S + i] = side[i];
 }
 
 // Split-K: y[m,n] = (sum_s partial[s][n][m]) * colscale[n] * 2^f[m] + bias[n], summed in split
@@ -719,7 +739,7 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int sp
                                        const void* col_scale, int col_scale_kind, const int32_t* w_row_exp,
                                        const int32_t* x_row_exp, const float* x_row_scale, const void* bias,
                                        int bias_kind, void* y, int y_dtype, long long ldy, const PeerOut po,
-                                       int lora) {
+                                       int lora, long long lim_partial) {
   __shared__ float tile[32][33];
   const int m0 = blockIdx.x * 32, n0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
@@ -729,7 +749,8 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int sp
     float acc = 0.f;
     if (n < N && m < M) {
       const float* pp = partial + (size_t)n * Mp + m;
-      for (int s = 0; s < splits; ++s) acc = __fadd_rn(acc, pp[s * plane]);
+      for (int s = 0; s < splits; ++s)
+        if (qchk(BS_FINAL, (long long)s * plane + (long long)n * Mp + m, lim_partial)) acc = __fadd_rn(acc, pp[s * plane]);
     }
     tile[i][tx] = acc;
   }
@@ -751,6 +772,7 @@ __global__ void splitk_finalize_kernel(const float* __restrict__ partial, int sp
     else if (bias_kind == 3) b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
     o = __fadd_rn(o, b);
     const long long oi = (long long)m * ldy + n;
+    if (!qchk(BS_FINAL, oi, (long long)(M - 1) * ldy + N)) continue;
     if (po.ndst > 0) {
       // 2-byte output to every destination (this rank's slab in each rank's gathered buffer)
       const uint16_t bits = y_dtype == 2 ? __bfloat16_as_ushort(__float2bfloat16_rn(o)) : __half_as_ushort(__float2half_rn(o));
@@ -917,9 +939,13 @@ __global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restric
         if (++r >= 16) break;
       }
       uint8_t* dst = tile + r * pitch + (c0 + c) * 16;
-      if (row0 + r < M)
-        cp_async16(dst, reinterpret_cast<const uint8_t*>(x) + ((long long)(row0 + r) * ldx + (c0 + c) * 8) * 2);
-      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      if (!qchk_smem(BS_PRO_OUT, psm, dst, 16)) continue;
+      if (row0 + r < M) {
+        if (qchk_span(BS_PRO_X, (long long)(row0 + r) * ldx + (c0 + c) * 8, 8, (long long)(M - 1) * ldx + K))
+          cp_async16(dst, reinterpret_cast<const uint8_t*>(x) + ((long long)(row0 + r) * ldx + (c0 + c) * 8) * 2);
+      } else {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
@@ -958,7 +984,7 @@ __global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restric
       // max |z * kNorm| = RN(max|z| * kNorm): rounding is monotonic
       const float a_lo = __fmul_rn(m_lo, kNorm), a_hi = __fmul_rn(m_hi, kNorm);
       const int f_lo = pow2_exponent(a_lo), f_hi = pow2_exponent(a_hi);
-      if ((lane & 3) == 0) {
+      if ((lane & 3) == 0 && qchk_smem(BS_PRO_OUT, psm, gexp + ((lane >> 2) + 8) * groups + g, 4)) {
         gexp[(lane >> 2) * groups + g] = group_exponent_code(a_lo, f_lo);
         gexp[((lane >> 2) + 8) * groups + g] = group_exponent_code(a_hi, f_hi);
       }
@@ -972,6 +998,7 @@ __global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restric
 #pragma unroll
           for (int nb = 0; nb < 2; ++nb) {
             const int col = g * kGroupCols + 16 * a + 8 * nb + 2 * (lane & 3);
+            if (!qchk_smem(BS_PRO_OUT, psm, tile + ((lane >> 2) + 8) * pitch + col * 2, 4)) continue;
             *reinterpret_cast<uint32_t*>(tile + (lane >> 2) * pitch + col * 2) =
                 pack_f16x2(__fmul_rn(z[a][nb][0], s_lo), __fmul_rn(z[a][nb][1], s_lo));
             *reinterpret_cast<uint32_t*>(tile + ((lane >> 2) + 8) * pitch + col * 2) =
@@ -983,6 +1010,7 @@ __global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restric
 #pragma unroll
           for (int nb = 0; nb < 2; ++nb) {
             const int col = g * kGroupCols + 16 * a + 8 * nb + 2 * (lane & 3);
+            if (!qchk_smem(BS_PRO_OUT, psm, tile + ((lane >> 2) + 8) * pitch + col * 2, 4)) continue;
             *reinterpret_cast<uint32_t*>(tile + (lane >> 2) * pitch + col * 2) =
                 pack_f16x2(scale_pow2(__fmul_rn(z[a][nb][0], kNorm), f_lo), scale_pow2(__fmul_rn(z[a][nb][1], kNorm), f_lo));
             *reinterpret_cast<uint32_t*>(tile + ((lane >> 2) + 8) * pitch + col * 2) =
@@ -998,7 +1026,7 @@ __global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restric
     int f = kGroupZero;
     for (int g = 0; g < groups; ++g) f = max(f, gexp[tid * groups + g]);
     if (f == kGroupZero || f == kGroupNonFinite) f = 0;
-    rexp[tid] = f;
+    if (qchk_smem(BS_PRO_OUT, psm, rexp + tid, 4)) rexp[tid] = f;
     if (row0 + tid < M) row_exp[row0 + tid] = f;
   }
   __syncthreads();
@@ -1011,6 +1039,9 @@ __global__ void __launch_bounds__(256) prologue_mma_kernel(const void* __restric
       if (++r >= 16) break;
     }
     if (row0 + r >= M) break;
+    if (!qchk_smem(BS_PRO_OUT, psm, tile + r * pitch + c * 16, 16) ||
+        !qchk_span(BS_PRO_OUT, (long long)(row0 + r) * ldo + c * 8, 8, (long long)M * ldo))
+      continue;
     uint4 v = *reinterpret_cast<const uint4*>(tile + r * pitch + c * 16);
     const int code = gexp[r * groups + (c * 8) / kGroupCols];
     const int d = (code == kGroupZero ? rexp[r] : code == kGroupNonFinite ? 0 : code) - rexp[r];
@@ -1092,7 +1123,8 @@ __global__ void kitchen_grid_kernel(const uint8_t* __restrict__ q, const uint8_t
                                     int8_t* __restrict__ out) {
   __shared__ float levels[64];
   const int nlev = 1 << bits;
-  if (threadIdx.x < nlev) levels[threadIdx.x] = codebook ? codebook[threadIdx.x] : (float)((int)threadIdx.x - nlev / 2);
+  if (threadIdx.x < nlev && qchk(BS_KITCHEN, threadIdx.x, 64))
+    levels[threadIdx.x] = codebook ? codebook[threadIdx.x] : (float)((int)threadIdx.x - nlev / 2);
   __syncthreads();
   const int gpr = K / 16;
   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1100,6 +1132,11 @@ __global__ void kitchen_grid_kernel(const uint8_t* __restrict__ q, const uint8_t
   const int row = (int)(t / gpr), c0 = (int)(t - (long long)row * gpr) * 16;
   const long long pitch = (long long)K * bits / 8;
   const uint8_t* qr = q + row * pitch;
+  if (!qchk_span(BS_KITCHEN, row * pitch + c0 / 2, 8, (long long)N * pitch) ||
+      (bits == 6 && !qchk_span(BS_KITCHEN, row * pitch + K / 2 + c0 / 4, 4, (long long)N * pitch)) ||
+      !qchk(BS_KITCHEN, (long long)row * (K / group) + c0 / group, (long long)N * (K / group)) ||
+      !qchk_span(BS_KITCHEN, (long long)row * K + c0, 16, (long long)N * K))
+    return;
   const uint2 lo = *reinterpret_cast<const uint2*>(qr + c0 / 2);
   uint32_t hi = 0;
   if (bits == 6) hi = *reinterpret_cast<const uint32_t*>(qr + K / 2 + c0 / 4);
@@ -1110,7 +1147,7 @@ __global__ void kitchen_grid_kernel(const uint8_t* __restrict__ q, const uint8_t
     const uint32_t byte = ((i < 8 ? lo.x : lo.y) >> (8 * ((i >> 1) & 3))) & 0xFF;
     uint32_t code = (i & 1) ? (byte >> 4) : (byte & 0xF);
     if (bits == 6) code |= ((hi >> (2 * i)) & 3) << 4;
-    const float v = fminf(fmaxf(rintf(__fmul_rn(levels[code], sc)), -127.f), 127.f);
+    const float v = qchk(BS_KITCHEN, code, nlev) ? fminf(fmaxf(rintf(__fmul_rn(levels[code], sc)), -127.f), 127.f) : 0.f;
     w[i >> 2] |= ((uint32_t)(int)v & 0xFF) << (8 * (i & 3));
   }
   *reinterpret_cast<uint4*>(out + (long long)row * K + c0) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -1126,8 +1163,9 @@ __global__ void lora_t_kernel(const void* __restrict__ t, int t_dtype, long long
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)M * rk) return;
   const int m = (int)(i / rk), r = (int)(i - (long long)m * rk);
-  float v = r < R ? load_x(t, t_dtype, (long long)m * ldt + r) : 0.f;
-  if (x_row_exp != nullptr) v = scale_pow2(v, x_row_exp[m]);
+  float v = (r < R && qchk(BS_LORA, (long long)m * ldt + r, (long long)(M - 1) * ldt + R))
+                ? load_x(t, t_dtype, (long long)m * ldt + r) : 0.f;
+  if (x_row_exp != nullptr && qchk(BS_LORA, m, M)) v = scale_pow2(v, x_row_exp[m]);
   out[i] = __float2bfloat16_rn(v);
 }
 
@@ -1138,7 +1176,7 @@ __global__ void lora_u_kernel(const void* __restrict__ up, int up_dtype, long lo
   if (i >= (long long)n_pad * rk) return;
   const int n = (int)(i / rk), r = (int)(i - (long long)n * rk);
   float v = 0.f;
-  if (n < N && r < R) {
+  if (n < N && r < R && qchk(BS_LORA, (long long)n * ldu + r, (long long)(N - 1) * ldu + R)) {
     v = __fmul_rn(load_x(up, up_dtype, (long long)n * ldu + r), scale);
     if (cs_kind == 1) v = __fdiv_rn(v, lora_safe_scale(__half2float(reinterpret_cast<const __half*>(cs)[n])));
     else if (cs_kind == 2) v = __fdiv_rn(v, lora_safe_scale(reinterpret_cast<const float*>(cs)[n]));
@@ -1228,13 +1266,18 @@ int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int
 // ldw] (zeros past K and past N), with e the row exponent of the row's largest |w| (as for the
 // other layouts: that weight lands in [2^14, 2^15)).  One CTA per row: a max pass, then the writes.
 __global__ void gguf_straddle_repack_kernel(const uint8_t* __restrict__ raw, int qtype, int N, int K, int ldw,
-                                            __half* __restrict__ out, int32_t* __restrict__ row_exp) {
+                                            __half* __restrict__ out, int32_t* __restrict__ row_exp,
+                                            long long out_elems) {
   const int n = blockIdx.x;
   __shared__ float red[32];
   __shared__ int e_row;
+  const int qk = gguf_qk(qtype), ts = gguf_ts(qtype);
+  const long long raw_bytes = (long long)N * K / qk * ts;
   float mx = 0.f;
   if (n < N)
-    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(gguf_value(raw, qtype, (long long)n * K + k)));
+    for (int k = threadIdx.x; k < K; k += blockDim.x)
+      if (qchk_span(BS_REPACK_SRC, ((long long)n * K + k) / qk * ts, ts, raw_bytes))
+        mx = fmaxf(mx, fabsf(gguf_value(raw, qtype, (long long)n * K + k)));
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
   __syncthreads();
@@ -1244,21 +1287,23 @@ __global__ void gguf_straddle_repack_kernel(const uint8_t* __restrict__ raw, int
     int ex = 0;
     if (m > 0.f) frexpf(m, &ex);
     e_row = m > 0.f ? ex - 15 : 0;
-    row_exp[n] = e_row;
+    if (qchk(BS_REPACK_DST, n, gridDim.x)) row_exp[n] = e_row;
   }
   __syncthreads();
   const float sc = exp2i(-e_row);
   for (int k = threadIdx.x; k < ldw; k += blockDim.x) {
     float v = 0.f;
-    if (n < N && k < K) v = __fmul_rn(gguf_value(raw, qtype, (long long)n * K + k), sc);
-    out[(size_t)n * ldw + k] = __float2half_rn(v);
+    if (n < N && k < K && qchk_span(BS_REPACK_SRC, ((long long)n * K + k) / qk * ts, ts, raw_bytes))
+      v = __fmul_rn(gguf_value(raw, qtype, (long long)n * K + k), sc);
+    if (qchk(BS_REPACK_DST, (long long)n * ldw + k, out_elems)) out[(size_t)n * ldw + k] = __float2half_rn(v);
   }
 }
 
 void launch_gguf_straddle_repack(const uint8_t* raw, int qtype, int N, int K, int n_pad, int ldw, void* out,
-                                 int32_t* row_exp, cudaStream_t s) {
+                                 size_t out_bytes, int32_t* row_exp, cudaStream_t s) {
   if (n_pad == 0) return;
-  gguf_straddle_repack_kernel<<<n_pad, 256, 0, s>>>(raw, qtype, N, K, ldw, reinterpret_cast<__half*>(out), row_exp);
+  gguf_straddle_repack_kernel<<<n_pad, 256, 0, s>>>(raw, qtype, N, K, ldw, reinterpret_cast<__half*>(out), row_exp,
+                                                    (long long)(out_bytes / 2));
 }
 
 void launch_gguf_dequant(const uint8_t* raw, int qtype, long long total, void* out, int out_dtype, cudaStream_t s) {
@@ -1273,16 +1318,16 @@ void launch_gguf_row_exp(const uint8_t* raw, int qtype, int N, int K, int n_pad,
 }
 
 void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_stages, int n_tiles, uint8_t* out,
-                        uint32_t stage_bytes, int P, int S, cudaStream_t s) {
+                        size_t out_bytes, uint32_t stage_bytes, int P, int S, cudaStream_t s) {
   if (num_k_stages == 0 || n_tiles == 0) return;
   dim3 grid(num_k_stages, n_tiles);
-  gguf_repack_kernel<<<grid, 128, 0, s>>>(raw, qtype, N, K, num_k_stages, out, stage_bytes, P, S);
+  gguf_repack_kernel<<<grid, 128, 0, s>>>(raw, qtype, N, K, num_k_stages, out, stage_bytes, P, S, (long long)out_bytes);
 }
 
 void launch_splitk_finalize(const float* partial, int splits, int M, int N, int Mp, const void* col_scale,
                             int cs_kind, const int32_t* w_row_exp, const int32_t* x_row_exp,
                             const float* x_row_scale, const void* bias, int bias_kind, void* y, int y_dtype,
-                            long long ldy, cudaStream_t s, const PeerOut* out, int lora) {
+                            long long ldy, cudaStream_t s, const PeerOut* out, int lora, size_t partial_bytes) {
   if (M == 0 || N == 0) return;
   dim3 grid((M + 31) / 32, (N + 31) / 32);
   PeerOut po{};
@@ -1292,7 +1337,9 @@ void launch_splitk_finalize(const float* partial, int splits, int M, int N, int 
   }
   splitk_finalize_kernel<<<grid, dim3(32, 8), 0, s>>>(partial, splits, M, N, Mp, col_scale, cs_kind, w_row_exp,
                                                       x_row_exp, x_row_scale, bias, bias_kind, y, y_dtype, ldy, po,
-                                                      lora);
+                                                      lora,
+                                                      partial_bytes ? (long long)(partial_bytes / sizeof(float))
+                                                                    : (long long)splits * N * Mp);
 }
 
 void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* codebook, int bits, int group, int N,
@@ -1336,7 +1383,8 @@ __global__ void __launch_bounds__(256) int8_transpose_kernel(const int8_t* __res
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int k = k0 + c + i;
-      tile[r][c + i] = (n < N && k < K) ? (uint8_t)q[(size_t)n * K + k] : 0;
+      tile[r][c + i] = (n < N && k < K && qchk(BS_GRAD, (long long)n * K + k, (long long)N * K))
+                           ? (uint8_t)q[(size_t)n * K + k] : 0;
     }
   }
   __syncthreads();
@@ -1348,7 +1396,8 @@ __global__ void __launch_bounds__(256) int8_transpose_kernel(const int8_t* __res
   for (int j = 0; j < 4; ++j)
     w[j] = (uint32_t)tile[c + 4 * j][r] | ((uint32_t)tile[c + 4 * j + 1][r] << 8) |
            ((uint32_t)tile[c + 4 * j + 2][r] << 16) | ((uint32_t)tile[c + 4 * j + 3][r] << 24);
-  *reinterpret_cast<uint4*>(qt + (size_t)k * ldt + n0 + c) = make_uint4(w[0], w[1], w[2], w[3]);
+  if (qchk_span(BS_GRAD, (long long)k * ldt + n0 + c, 16, (long long)K * ldt))
+    *reinterpret_cast<uint4*>(qt + (size_t)k * ldt + n0 + c) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // dY' = dY * s per column, normalized per row like the forward's activation operand: a power of
@@ -1359,7 +1408,9 @@ __global__ void __launch_bounds__(256) grad_prologue_kernel(const void* __restri
                                                             __half* __restrict__ out, int32_t* __restrict__ row_exp) {
   __shared__ float red[33];
   const int row = blockIdx.x;
+  const long long lim_dy = (long long)(gridDim.x - 1) * lddy + N;  // one CTA per row of dY [M, lddy]
   auto value = [&](int c) {
+    if (!qchk(BS_GRAD, c, N) || !qchk(BS_GRAD, (long long)row * lddy + c, lim_dy)) return 0.f;
     const float sc = s_f16 ? __half2float(reinterpret_cast<const __half*>(s)[c]) : reinterpret_cast<const float*>(s)[c];
     return __fmul_rn(load_x(dy, dy_dtype, (long long)row * lddy + c), sc);
   };
@@ -1377,7 +1428,8 @@ __global__ void __launch_bounds__(256) grad_prologue_kernel(const void* __restri
   for (int c = 2 * threadIdx.x; c < Np; c += 2 * blockDim.x) {
     const float v0 = c < N ? scale_pow2(value(c), f) : 0.f;
     const float v1 = c + 1 < N ? scale_pow2(value(c + 1), f) : 0.f;
-    *reinterpret_cast<__half2*>(o + c) = __floats2half2_rn(v0, v1);
+    if (qchk_span(BS_GRAD, (long long)row * Np + c, 2, (long long)gridDim.x * Np))
+      *reinterpret_cast<__half2*>(o + c) = __floats2half2_rn(v0, v1);
   }
 }
 
@@ -1425,8 +1477,8 @@ __global__ void __launch_bounds__(512) grad_prologue_vec_kernel(const void* __re
         v[2 * e + 1] = dy_dtype == 1 ? __half2float(__ushort_as_half(hi)) : __bfloat162float(__ushort_as_bfloat16(hi));
       }
     }
-    float sc[8];
-    load8(s, s_f16 ? 1 : 0, c, sc);
+    float sc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (qchk_span(BS_GRAD, c, 8, N)) load8(s, s_f16 ? 1 : 0, c, sc);
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], sc[e]);
   };
@@ -1434,7 +1486,7 @@ __global__ void __launch_bounds__(512) grad_prologue_vec_kernel(const void* __re
 #pragma unroll
   for (int j = 0; j < CH; ++j) {
     const int c = (j * (int)blockDim.x + (int)threadIdx.x) * 8;
-    if (c < N) {
+    if (c < N && qchk_span(BS_GRAD, (long long)row * lddy + c, 8, (long long)(gridDim.x - 1) * lddy + N)) {
       if constexpr (F32) {
         const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(dy) + (long long)row * lddy + c);
         const uint4 a = src[0], b = src[1];
@@ -1468,7 +1520,8 @@ __global__ void __launch_bounds__(512) grad_prologue_vec_kernel(const void* __re
       uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
       for (int e = 0; e < 4; ++e) pw[e] = pack_f16x2(scale_pow2(v[2 * e], f), scale_pow2(v[2 * e + 1], f));
-      *reinterpret_cast<uint4*>(out + (long long)row * Np + c) = pk;
+      if (qchk_span(BS_GRAD, (long long)row * Np + c, 8, (long long)gridDim.x * Np))
+        *reinterpret_cast<uint4*>(out + (long long)row * Np + c) = pk;
     }
   }
 }
@@ -1490,7 +1543,7 @@ __global__ void __launch_bounds__(256) grad_rotate_kernel(const float* __restric
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const long long wg = w0 + r;
-    if (wg < total) {
+    if (wg < total && qchk_span(BS_GRAD, (wg / nblk) * K + (wg % nblk) * G + lane * E, E, (long long)M * K)) {
       const float* src = in + (size_t)(wg / nblk) * K + (int)(wg % nblk) * G + lane * E;
       if constexpr (E >= 4) {
 #pragma unroll
@@ -1514,6 +1567,7 @@ __global__ void __launch_bounds__(256) grad_rotate_kernel(const float* __restric
     const long long wg = w0 + r;
     if (wg >= total) break;
     const long long o = (long long)(wg / nblk) * ldo + (int)(wg % nblk) * G + lane * E;
+    if (!qchk_span(BS_GRAD, o, E, (long long)(M - 1) * ldo + K)) continue;
     bool done = false;
     if constexpr (E >= 4) {
       if (vec && out_dtype != OUT_F32) {
@@ -1590,5 +1644,8 @@ int launch_grad_rotate(const float* in, int M, int K, int group, void* out, int 
     default: return -1;
   }
 }
+
+// This translation unit's bounds record (QLIN_CHECKS build).
+QLIN_BOUNDS_READER(bounds_read_aux)
 
 }  // namespace qlin

@@ -364,6 +364,10 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   p.partial = nullptr;
   p.status = reinterpret_cast<DeviceStatus*>(device_status_ptr());
   p.Mp = p.m_tiles * tm;
+  p.lim_y = (long long)(a.M - 1) * a.ldy + a.N;
+  p.lim_w_bytes = a.w_bytes;
+  p.lim_partial = (long long)(a.partial_bytes / sizeof(float));
+  p.lim_lora_u = (long long)p.n_tiles * 128 * a.lora_k;
   PeerMaps maps;
   memset(&maps, 0, sizeof(maps));
   if (a.out != nullptr) {
@@ -455,7 +459,7 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   if (splits > 1) {
     launch_splitk_finalize(p.partial, splits, a.M, a.N, p.Mp, a.col_scale, a.col_scale_kind, a.w_row_exp,
                            a.x_row_exp, nullptr, a.bias, a.bias_kind, a.y, a.y_dtype, a.ldy, stream, a.out,
-                           a.lora_k > 0);
+                           a.lora_k > 0, a.partial_bytes);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       set_error("split-K finalize launch failed: %s", cudaGetErrorString(e));
@@ -464,5 +468,8 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   }
   return 0;
 }
+
+// This translation unit's bounds record (QLIN_CHECKS build).
+QLIN_BOUNDS_READER(bounds_read_f16)
 
 }  // namespace qlin

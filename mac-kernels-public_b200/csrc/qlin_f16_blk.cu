@@ -1,5 +1,7 @@
 // Instantiations of the weight-only (kind::f16) fused dequantize + GEMM for the 32-value block formats
 // Q4_1, Q5_0, Q5_1 and IQ4_XS.
+#include <cuda_runtime.h>
+
 #include "qlin_f16_launch.cuh"
 
 namespace qlin {
@@ -14,5 +16,8 @@ int dispatch_f16_blk(int fmt, const CUtensorMap& tx, const CUtensorMap& tw, cons
     default: return -1;
   }
 }
+
+// This translation unit's bounds record (QLIN_CHECKS build).
+QLIN_BOUNDS_READER(bounds_read_f16_blk)
 
 }  // namespace qlin

@@ -1,5 +1,7 @@
 // Instantiations of the weight-only (kind::f16) fused dequantize + GEMM for the K-quant formats Q2_K,
 // Q3_K, Q4_K, Q5_K and Q6_K.
+#include <cuda_runtime.h>
+
 #include "qlin_f16_launch.cuh"
 
 namespace qlin {
@@ -15,5 +17,8 @@ int dispatch_f16_kq(int fmt, const CUtensorMap& tx, const CUtensorMap& tw, const
     default: return -1;
   }
 }
+
+// This translation unit's bounds record (QLIN_CHECKS build).
+QLIN_BOUNDS_READER(bounds_read_f16_kq)
 
 }  // namespace qlin

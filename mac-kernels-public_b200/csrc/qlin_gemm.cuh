@@ -59,6 +59,12 @@ struct GemmParams {
   // 128) channels, in fp32, before its one rounding (the staged 2-byte output path, no K split).
   int rot_group;
   DeviceStatus* status;
+  // Element counts of the caller's buffers, derived on the host from the C-ABI arguments; the
+  // QLIN_CHECKS build tests every plain access against them (unused otherwise).
+  long long lim_y;        // output elements reachable from y (and from each out.dst[d])
+  long long lim_w_bytes;  // bytes of w_stages (bulk-copied weight stages)
+  long long lim_partial;  // fp32 elements of partial
+  long long lim_lora_u;   // bf16 elements of lora_u
   // Staged 2-byte output: out.ndst > 0 writes each finished 32-token chunk through shared memory
   // with 16-byte stores to every destination (this rank's slab in each rank's gathered buffer);
   // out.wait / out.signal run the cross-rank flag protocol of qlin_peer.cuh.
@@ -89,7 +95,8 @@ struct F16Cfg {
   static_assert(kASlots >= 2, "at least two decoded-weight slots");
 };
 
-__device__ __forceinline__ float load_bias(const void* bias, int kind, int n) {
+__device__ __forceinline__ float load_bias(const void* bias, int kind, int n, int lim) {
+  if (kind != 0 && !qchk(BS_GEMM_BIAS, n, lim)) return 0.f;
   if (kind == 1) return __half2float(reinterpret_cast<const __half*>(bias)[n]);
   if (kind == 2) return reinterpret_cast<const float*>(bias)[n];
   if (kind == 3) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
@@ -97,6 +104,7 @@ __device__ __forceinline__ float load_bias(const void* bias, int kind, int n) {
 }
 
 __device__ __forceinline__ float load_colscale(const GemmParams& p, int n) {
+  if (!qchk(BS_GEMM_BIAS, n, p.N)) return 1.f;
   switch (p.col_scale_kind) {
     case CS_F16: return __half2float(reinterpret_cast<const __half*>(p.col_scale)[n]);
     case CS_F32: return reinterpret_cast<const float*>(p.col_scale)[n];
@@ -105,7 +113,8 @@ __device__ __forceinline__ float load_colscale(const GemmParams& p, int n) {
   }
 }
 
-__device__ __forceinline__ void store_out(void* y, int dtype, long long idx, float v) {
+__device__ __forceinline__ void store_out(void* y, int dtype, long long idx, float v, long long lim) {
+  if (!qchk(BS_GEMM_Y, idx, lim)) return;
   if (dtype == OUT_F16) reinterpret_cast<__half*>(y)[idx] = __float2half_rn(v);
   else if (dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v);
   else reinterpret_cast<float*>(y)[idx] = v;
@@ -182,6 +191,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     mbar_init(drain, 1);
     mbar_init(epi_bar, 4);
     *abort_flag = 0;
+    // the carve-out (rings, barriers, epilogue staging) lies inside the launch's shared memory
+    if (!qchk_smem(BS_GEMM_SMEM, smem_raw, sepi, 2 * 16384)) *abort_flag = 1;
     // Before any activation is read: every rank finished the previous output-writing kernel.
     if (p.out.wait && !peer_wait(p.out, p.status, 6)) *abort_flag = 1;
     fence_mbar_init();
@@ -227,14 +238,19 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           {
             const int k0 = kst * 64;
             const int slab = k0 / p.k_slab;
-            tma_load_3d(sx + s * Cfg::kXStageBytes, &tmap_x, &full[s], k0 - slab * p.k_slab,
-                        mt * TM + (int)rank * Cfg::kXRows, slab);
+            // fp16 x coordinate: 8 elements per 16 bytes (a misaligned copy is skipped and the
+            // stage's barrier then runs out its bounded wait)
+            if (qchk_align(BS_TMA_ALIGN, (long long)(k0 - slab * p.k_slab) * 2, 16))
+              tma_load_3d(sx + s * Cfg::kXStageBytes, &tmap_x, &full[s], k0 - slab * p.k_slab,
+                          mt * TM + (int)rank * Cfg::kXRows, slab);
           }
           if constexpr (Dec::kTma) {
             tma_load_2d(sw + s * kWStage, &tmap_w, &full[s], kst * 64, nt * 128);
           } else {
-            const uint8_t* src = p.w_stages + ((size_t)nt * p.main_k_stages + kst) * Dec::kStageBytes;
-            bulk_load(sw + s * kWStage, src, Dec::kStageBytes, &full[s]);
+            const long long off = ((long long)nt * p.main_k_stages + kst) * Dec::kStageBytes;
+            // out of range: copy stage 0 instead, so the pipeline keeps its byte count
+            const bool in = qchk_span(BS_GEMM_WBULK, off, Dec::kStageBytes, p.lim_w_bytes);
+            bulk_load(sw + s * kWStage, p.w_stages + (in ? off : 0), Dec::kStageBytes, &full[s]);
           }
         }
         for (int kst = max(s0, p.main_k_stages); kst < s1 && ok; ++kst, ++it) {  // LoRA: T' only
@@ -242,8 +258,9 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[s], Cfg::kXStageBytes);
-          tma_load_2d(sx + s * Cfg::kXStageBytes, &tmap_t, &full[s], (kst - p.main_k_stages) * 64,
-                      mt * TM + (int)rank * Cfg::kXRows);
+          if (qchk_align(BS_TMA_ALIGN, (long long)(kst - p.main_k_stages) * 64 * 2, 16))
+            tma_load_2d(sx + s * Cfg::kXStageBytes, &tmap_t, &full[s], (kst - p.main_k_stages) * 64,
+                        mt * TM + (int)rank * Cfg::kXRows);
         }
       }
       if (!ok) {
@@ -330,7 +347,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       const int s1 = min(p.num_k_stages, s0 + p.stages_per_split);
       const int n = nt * 128 + r;
       float rscale = 1.f;
-      if (p.w_row_exp != nullptr && p.col_scale_kind == CS_EXP2) rscale = exp2i(-p.w_row_exp[min(n, p.N - 1)]);
+      if (p.w_row_exp != nullptr && p.col_scale_kind == CS_EXP2 && qchk(BS_GEMM_BIAS, min(n, p.N - 1), p.N))
+        rscale = exp2i(-p.w_row_exp[min(n, p.N - 1)]);
       const int s_main = min(s1, p.main_k_stages);
       for (int kst = s0; kst < s_main; ++kst, ++it) {
         if ((int)(it % Cfg::kDecGroups) != group) continue;
@@ -355,10 +373,12 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         const uint32_t ph = (it / STAGES) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag, p.status, 4)) { ok = false; break; }
         uint32_t a[32];  // LoRA stage: 64 bf16 values of this row of U', as stored
-        const uint4* u = reinterpret_cast<const uint4*>(p.lora_u + (size_t)n * p.lora_k + (kst - p.main_k_stages) * 64);
+        const long long uoff = (long long)n * p.lora_k + (kst - p.main_k_stages) * 64;
+        const uint4* u = reinterpret_cast<const uint4*>(p.lora_u + uoff);
+        const bool u_in = qchk_span(BS_GEMM_LORA_U, uoff, 64, p.lim_lora_u);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const uint4 v = __ldg(u + j);
+          const uint4 v = u_in ? __ldg(u + j) : make_uint4(0u, 0u, 0u, 0u);
           a[4 * j] = v.x; a[4 * j + 1] = v.y; a[4 * j + 2] = v.z; a[4 * j + 3] = v.w;
         }
         const int as = it % Cfg::kASlots;
@@ -403,7 +423,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       if (p.k_splits == 1 && n_ok) {
         cs = load_colscale(p, n);
         if (p.lora_k > 0) cs = lora_safe_scale(cs);
-        bias = load_bias(p.bias, p.bias_kind, n);
+        bias = load_bias(p.bias, p.bias_kind, n, p.N);
       }
 #pragma unroll 1
       for (int c0 = 0; c0 < TM; c0 += 32) {
@@ -427,12 +447,13 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             fence_proxy_async_smem();
             if (!(epi_ok = epi_sync())) break;
             if (issuer) {
-              tma_store_3d(&tmap_p, buf, mt * TM + c0, nt * 128, ks);
+              if (qchk_align(BS_TMA_ALIGN, (long long)(mt * TM + c0) * 4, 16))
+                tma_store_3d(&tmap_p, buf, mt * TM + c0, nt * 128, ks);
               bulk_commit();
             }
             ++epi_chunk;
           } else {
-            if (n_ok) {
+            if (n_ok && qchk_span(BS_GEMM_PARTIAL, ((long long)ks * p.N + n) * p.Mp + mt * TM + c0, TM, p.lim_partial)) {
               float4* dst = reinterpret_cast<float4*>(p.partial + ((size_t)ks * p.N + n) * p.Mp + mt * TM + c0);
 #pragma unroll
               for (int j = 0; j < TM / 4; ++j)
@@ -445,7 +466,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         // per-token power of two for the 32 columns of this chunk: lane j holds column j's
         constexpr int kCh = TM < 32 ? TM : 32;  // tokens of this tile in the chunk
         const int mj = mt * TM + c0 + lane;
-        const float rs_lane = (p.x_row_exp != nullptr && mj < p.M && lane < kCh) ? exp2i(__ldg(&p.x_row_exp[mj])) : 1.f;
+        const float rs_lane = (p.x_row_exp != nullptr && mj < p.M && lane < kCh && qchk(BS_GEMM_XEXP, mj, p.M))
+                                  ? exp2i(__ldg(&p.x_row_exp[mj])) : 1.f;
         tmem_wait_ld();
         if (p.out.ndst > 0) {
           // Stage the chunk as [kCh tokens][128 channels] 2-byte values, then copy whole 16-byte
@@ -467,7 +489,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
 #pragma unroll
             for (int j = 0; j < kCh; ++j) {
               const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
-              frot[j * 128 + r] = __fadd_rn(__fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs), bias);
+              if (qchk(BS_GEMM_SMEM, j * 128 + r, 4096)) frot[j * 128 + r] = __fadd_rn(__fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs), bias);
             }
             if (!(epi_ok = epi_sync())) break;
             constexpr int kRows = (kCh + 3) / 4;  // token rows of this warp: quarter, quarter + 4, ...
@@ -486,7 +508,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
               if (j < kCh) {
                 const uint32_t w0 = p.y_dtype == OUT_BF16 ? pack_bf16x2(o4[jj][0], o4[jj][1]) : pack_f16x2(o4[jj][0], o4[jj][1]);
                 const uint32_t w1 = p.y_dtype == OUT_BF16 ? pack_bf16x2(o4[jj][2], o4[jj][3]) : pack_f16x2(o4[jj][2], o4[jj][3]);
-                *reinterpret_cast<uint2*>(buf + j * 128 + 4 * lane) = make_uint2(w0, w1);
+                if (qchk_span(BS_GEMM_SMEM, j * 128 + 4 * lane, 4, 4096))
+                  *reinterpret_cast<uint2*>(buf + j * 128 + 4 * lane) = make_uint2(w0, w1);
               }
             }
           } else {
@@ -495,7 +518,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
               const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
               float o = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs);
               o = __fadd_rn(o, bias);
-              buf[j * 128 + r] = p.y_dtype == OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o))
+              if (qchk(BS_GEMM_SMEM, j * 128 + r, 4096))
+                buf[j * 128 + r] = p.y_dtype == OUT_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o))
                                                        : __half_as_ushort(__float2half_rn(o));
             }
           }
@@ -505,7 +529,8 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             if (issuer) {
 #pragma unroll
               for (int d = 0; d < kMaxPeers; ++d)
-                if (d < p.out.ndst) tma_store_2d(&out_maps.m[d], buf, nt * 128, mt * TM + c0);
+                if (d < p.out.ndst && qchk_align(BS_TMA_ALIGN, (long long)nt * 128 * 2, 16))
+                tma_store_2d(&out_maps.m[d], buf, nt * 128, mt * TM + c0);
               bulk_commit();
             }
             ++epi_chunk;
@@ -519,9 +544,11 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             if (m < p.M && n0 < p.N) {
               const uint4 val = reinterpret_cast<const uint4*>(buf)[i];
               const long long off = (long long)m * p.ldy + n0;
+              if (qchk_span(BS_GEMM_PEER, off, 8, p.lim_y)) {
 #pragma unroll
-              for (int d = 0; d < kMaxPeers; ++d)
-                if (d < p.out.ndst) reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out.dst[d]) + off)[0] = val;
+                for (int d = 0; d < kMaxPeers; ++d)
+                  if (d < p.out.ndst) reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out.dst[d]) + off)[0] = val;
+              }
             }
           }
           ++epi_chunk;
@@ -534,7 +561,7 @@ qgemm_f16_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
           if (n_ok && m < p.M) {
             float o = __fmul_rn(__fmul_rn(__uint_as_float(v[j]), cs), rs);
             o = __fadd_rn(o, bias);
-            store_out(p.y, p.y_dtype, (long long)m * p.ldy + n, o);
+            store_out(p.y, p.y_dtype, (long long)m * p.ldy + n, o, p.lim_y);
           }
         }
       }

@@ -48,9 +48,22 @@ struct GemmI8Params {
   int y_dtype;
   long long ldy;
   DeviceStatus* status;
+  // Element counts of the caller's buffers for the QLIN_CHECKS build (unused otherwise).
+  long long lim_y;        // output elements reachable from y
+  long long lim_w_bytes;  // bytes of w_stages
+  long long lim_scales;   // scale entries (N * groups_per_row, or N per channel)
 };
 
-__device__ __forceinline__ float load_bias_i8(const void* bias, int kind, int n) {
+// Output element idx (checked against the caller's buffer in the QLIN_CHECKS build).
+__device__ __forceinline__ void store_out_i8(const GemmI8Params& p, long long idx, float o) {
+  if (!qchk(BS_I8_Y, idx, p.lim_y)) return;
+  if (p.y_dtype == OUT_F16) reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(o);
+  else if (p.y_dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(p.y)[idx] = __float2bfloat16_rn(o);
+  else reinterpret_cast<float*>(p.y)[idx] = o;
+}
+
+__device__ __forceinline__ float load_bias_i8(const void* bias, int kind, int n, int lim) {
+  if (kind != 0 && !qchk(BS_I8_SCALE, n, lim)) return 0.f;
   if (kind == 1) return __half2float(reinterpret_cast<const __half*>(bias)[n]);
   if (kind == 2) return reinterpret_cast<const float*>(bias)[n];
   if (kind == 3) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
@@ -123,6 +136,10 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    // the carve-out (rings, barriers, flags) lies inside the launch's shared memory
+    if (!qchk_smem(BS_I8_SMEM, smem_raw, bars, reinterpret_cast<volatile uint8_t*>(abort_flag + 1) -
+                                         reinterpret_cast<volatile uint8_t*>(bars)))
+      *abort_flag = 1;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -169,8 +186,10 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           if constexpr (Dec::kTma) {
             tma_load_2d(sw + s * kWStage, &tmap_w, &full[s], kst * 64, nt * 128);
           } else {
-            const uint8_t* src = p.w_stages + ((size_t)nt * p.num_k_stages + kst) * Dec::kStageBytes;
-            bulk_load(sw + s * kWStage, src, Dec::kStageBytes, &full[s]);
+            const long long off = ((long long)nt * p.num_k_stages + kst) * Dec::kStageBytes;
+            // out of range: copy stage 0 instead, so the pipeline keeps its byte count
+            const bool in = qchk_span(BS_I8_WBULK, off, Dec::kStageBytes, p.lim_w_bytes);
+            bulk_load(sw + s * kWStage, p.w_stages + (in ? off : 0), Dec::kStageBytes, &full[s]);
           }
         }
       }
@@ -278,10 +297,14 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       for (int j = 0; j < kCols; ++j) accf[j] = 0.f;
       const __half* gscale = reinterpret_cast<const __half*>(p.scales) + (size_t)min(n, p.N - 1) * p.groups_per_row;
       float s_next = 0.f;
-      if (n_ok) s_next = (p.scale_kind == I8S_GROUP_F16) ? __half2float(gscale[0]) : reinterpret_cast<const float*>(p.scales)[n];
+      const long long gbase = (long long)min(n, p.N - 1) * p.groups_per_row;
+      if (n_ok && qchk(BS_I8_SCALE, p.scale_kind == I8S_GROUP_F16 ? gbase : n, p.lim_scales))
+        s_next = (p.scale_kind == I8S_GROUP_F16) ? __half2float(gscale[0]) : reinterpret_cast<const float*>(p.scales)[n];
       for (int g = 0; g < groups_per_tile; ++g, ++g_all) {
         const float sg = s_next;
-        if (n_ok && p.scale_kind == I8S_GROUP_F16 && g + 1 < groups_per_tile) s_next = __half2float(gscale[g + 1]);
+        if (n_ok && p.scale_kind == I8S_GROUP_F16 && g + 1 < groups_per_tile &&
+            qchk(BS_I8_SCALE, gbase + g + 1, p.lim_scales))
+          s_next = __half2float(gscale[g + 1]);
         const uint32_t b = g_all & 1;
         if (!mbar_wait_sleep(&acc_full[b], (g_all >> 1) & 1, abort_flag, p.status, 15)) { ok = false; break; }
         tc_fence_after();
@@ -310,21 +333,19 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         if (lane == 0) mbar_arrive(&acc_empty[b]);
       }
       if (!ok) break;
-      const float bias = n_ok ? load_bias_i8(p.bias, p.bias_kind, n) : 0.f;
+      const float bias = n_ok ? load_bias_i8(p.bias, p.bias_kind, n, p.N) : 0.f;
 #pragma unroll
       for (int c0 = 0; c0 < kCols; c0 += kChunk) {
         const int m0 = mt * TM + part * kCols + c0;
-        const float sx_lane = (lane < kChunk && m0 + lane < p.M) ? __ldg(&p.x_scale[m0 + lane]) * p.inv_scale : 0.f;
+        const float sx_lane = (lane < kChunk && m0 + lane < p.M && qchk(BS_I8_SCALE, m0 + lane, p.M))
+                                  ? __ldg(&p.x_scale[m0 + lane]) * p.inv_scale : 0.f;
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) {
           const float sxm = __shfl_sync(0xffffffffu, sx_lane, j);
           const int m = m0 + j;
           if (n_ok && m < p.M) {
             const float o = __fadd_rn(__fmul_rn(accf[c0 + j], sxm), bias);
-            const long long idx = (long long)m * p.ldy + n;
-            if (p.y_dtype == OUT_F16) reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(o);
-            else if (p.y_dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(p.y)[idx] = __float2bfloat16_rn(o);
-            else reinterpret_cast<float*>(p.y)[idx] = o;
+            store_out_i8(p, (long long)m * p.ldy + n, o);
           }
         }
       }

@@ -114,6 +114,10 @@ qgemm_i8p_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    // the carve-out (rings, barriers, flags) lies inside the launch's shared memory
+    if (!qchk_smem(BS_I8_SMEM, smem_raw, bars, reinterpret_cast<volatile uint8_t*>(abort_flag + 1) -
+                                         reinterpret_cast<volatile uint8_t*>(bars)))
+      *abort_flag = 1;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -148,8 +152,10 @@ qgemm_i8p_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             if constexpr (Dec::kTma) {
               tma_load_2d(sw + s * kWStage, &tmap_w, &full[s], kst * 64, nt * 128);
             } else {
-              bulk_load(sw + s * kWStage, p.w_stages + ((size_t)nt * nks + kst) * Dec::kStageBytes, Dec::kStageBytes,
-                        &full[s]);
+              const long long off = ((long long)nt * nks + kst) * Dec::kStageBytes;
+              // out of range: copy stage 0 instead, so the pipeline keeps its byte count
+              const bool in = qchk_span(BS_I8_WBULK, off, Dec::kStageBytes, p.lim_w_bytes);
+              bulk_load(sw + s * kWStage, p.w_stages + (in ? off : 0), Dec::kStageBytes, &full[s]);
             }
           }
         }
@@ -224,10 +230,12 @@ qgemm_i8p_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         uint32_t a[32];
         Dec::decode(sw + s * kWStage, r, a);
         uint8_t* row = sa + s * Cfg::kAStage + r * 128;
+        if (qchk_smem(BS_I8_SMEM, smem_raw, row, 128) && qchk(BS_I8_SMEM, (row - sa) + 128, sw - sa + 1)) {
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = make_uint4(a[4 * ch], a[4 * ch + 1], a[4 * ch + 2],
-                                                                            a[4 * ch + 3]);
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<uint4*>(row + ((ch ^ (r & 7)) << 4)) = make_uint4(a[4 * ch], a[4 * ch + 1],
+                                                                              a[4 * ch + 2], a[4 * ch + 3]);
+        }
         fence_proxy_async_smem();  // the MMA reads the tile through the async proxy
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(a_full_leader + (uint32_t)(s * 8));
@@ -259,12 +267,16 @@ qgemm_i8p_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
       const unsigned short* gscale =
           reinterpret_cast<const unsigned short*>(p.scales) + (size_t)min(n, p.N - 1) * p.groups_per_row;
       const bool group_scales = p.scale_kind == I8S_GROUP_F16;
-      const float s_channel = (n_ok && !group_scales) ? reinterpret_cast<const float*>(p.scales)[n] : 0.f;
+      const long long gbase = (long long)min(n, p.N - 1) * p.groups_per_row;
+      const float s_channel =
+          (n_ok && !group_scales && qchk(BS_I8_SCALE, n, p.lim_scales)) ? reinterpret_cast<const float*>(p.scales)[n] : 0.f;
       // the next group's scale stays raw (a load in flight across a whole group) until it is used
-      unsigned short s_raw = (n_ok && group_scales) ? __ldg(gscale) : (unsigned short)0;
+      unsigned short s_raw =
+          (n_ok && group_scales && qchk(BS_I8_SCALE, gbase, p.lim_scales)) ? __ldg(gscale) : (unsigned short)0;
       for (int g = 0; g < groups; ++g) {
         const float sg = group_scales ? __half2float(__ushort_as_half(s_raw)) : s_channel;
-        if (n_ok && group_scales && g + 1 < groups) s_raw = __ldg(gscale + g + 1);
+        if (n_ok && group_scales && g + 1 < groups && qchk(BS_I8_SCALE, gbase + g + 1, p.lim_scales))
+          s_raw = __ldg(gscale + g + 1);
         const uint32_t bt = bc % Cfg::kNBatch;
         const int sub = GPS == 2 ? (g & 1) : 0;
         if (sub == 0) {
@@ -306,21 +318,19 @@ qgemm_i8p_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
         }
       }
       if (!ok) break;
-      const float bias = n_ok ? load_bias_i8(p.bias, p.bias_kind, n) : 0.f;
+      const float bias = n_ok ? load_bias_i8(p.bias, p.bias_kind, n, p.N) : 0.f;
 #pragma unroll
       for (int c0 = 0; c0 < kCols; c0 += 32) {
         const int m0 = mt * TN + part * kCols + c0;
-        const float sx_lane = (m0 + lane < p.M) ? __ldg(&p.x_scale[m0 + lane]) * p.inv_scale : 0.f;
+        const float sx_lane =
+            (m0 + lane < p.M && qchk(BS_I8_SCALE, m0 + lane, p.M)) ? __ldg(&p.x_scale[m0 + lane]) * p.inv_scale : 0.f;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float sxm = __shfl_sync(0xffffffffu, sx_lane, j);
           const int m = m0 + j;
           if (n_ok && m < p.M) {
             const float o = __fadd_rn(__fmul_rn(accf[c0 + j], sxm), bias);
-            const long long idx = (long long)m * p.ldy + n;
-            if (p.y_dtype == OUT_F16) reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(o);
-            else if (p.y_dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(p.y)[idx] = __float2bfloat16_rn(o);
-            else reinterpret_cast<float*>(p.y)[idx] = o;
+            store_out_i8(p, (long long)m * p.ldy + n, o);
           }
         }
       }

@@ -37,9 +37,12 @@ struct GemvParams {
   void* y;
   int y_dtype;
   long long ldy;
+  // Element counts of the caller's buffers for the QLIN_CHECKS build (unused otherwise).
+  long long lim_w_bytes, lim_x, lim_y;
 };
 
 __device__ __forceinline__ float gemv_colscale(const GemvParams& p, int n) {
+  if (!qchk(BS_GEMV_Y, n, p.N)) return 1.f;
   switch (p.col_scale_kind) {
     case CS_F16: return __half2float(reinterpret_cast<const __half*>(p.col_scale)[n]);
     case CS_F32: return reinterpret_cast<const float*>(p.col_scale)[n];
@@ -84,12 +87,15 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const GemvParams 
   const bool n_ok = n < p.N;
   const int nt = n >> 7, r = n & 127;
   float rscale = 1.f;
-  if (!INT8 && p.w_row_exp != nullptr && p.col_scale_kind == CS_EXP2) rscale = exp2i(-p.w_row_exp[min(n, p.N - 1)]);
+  if (!INT8 && p.w_row_exp != nullptr && p.col_scale_kind == CS_EXP2 && qchk(BS_GEMV_Y, min(n, p.N - 1), p.N))
+    rscale = exp2i(-p.w_row_exp[min(n, p.N - 1)]);
   auto decode = [&](int kst, uint32_t (&w)[32]) {
     if constexpr (INT8) {
-      decode_int8_row(p.w + (size_t)n * p.K + kst * 64, w);
+      const long long off = (long long)n * p.K + kst * 64;
+      if (qchk_span(BS_GEMV_W, off, 64, p.lim_w_bytes)) decode_int8_row(p.w + off, w);
     } else {
-      Dec::decode(p.w + ((size_t)nt * p.num_k_stages + kst) * Dec::kStageBytes, r, rscale, w);
+      const long long off = ((long long)nt * p.num_k_stages + kst) * Dec::kStageBytes;
+      if (qchk_span(BS_GEMV_W, off, Dec::kStageBytes, p.lim_w_bytes)) Dec::decode(p.w + off, r, rscale, w);
     }
   };
   // The first stage's weights are fetched and decoded while the activations are staged.
@@ -98,6 +104,9 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const GemvParams 
   if (n_ok && kst0 < p.num_k_stages) decode(kst0, w);
   for (int i = threadIdx.x; i < p.M * (p.K / 2); i += blockDim.x) {
     const int m = i / (p.K / 2), c = i - m * (p.K / 2);
+    if (!qchk_span(BS_GEMV_X, (long long)m * p.ldx + 2 * c, 2, p.lim_x) ||
+        !qchk_smem(BS_GEMV_X, xs, xs + (size_t)m * p.K + 2 * c, 8))
+      continue;
     const float2 v = __half22float2(reinterpret_cast<const __half2*>(p.x + (size_t)m * p.ldx)[c]);
     reinterpret_cast<float2*>(xs + (size_t)m * p.K)[c] = v;
   }
@@ -128,16 +137,19 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const GemvParams 
 #pragma unroll
       for (int w = 0; w < 2 * kGemvWarps; ++w) s = __fadd_rn(s, red[w][m][threadIdx.x & 15]);
       float o = __fmul_rn(s, gemv_colscale(p, nn));
-      if (p.x_row_exp != nullptr) o = __fmul_rn(o, exp2i(p.x_row_exp[m]));
+      if (p.x_row_exp != nullptr && qchk(BS_GEMV_Y, m, p.M)) o = __fmul_rn(o, exp2i(p.x_row_exp[m]));
       float b = 0.f;
-      if (p.bias_kind == 1) b = __half2float(reinterpret_cast<const __half*>(p.bias)[nn]);
+      if (p.bias_kind != 0 && !qchk(BS_GEMV_Y, nn, p.N)) b = 0.f;
+      else if (p.bias_kind == 1) b = __half2float(reinterpret_cast<const __half*>(p.bias)[nn]);
       else if (p.bias_kind == 2) b = reinterpret_cast<const float*>(p.bias)[nn];
       else if (p.bias_kind == 3) b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.bias)[nn]);
       o = __fadd_rn(o, b);
       const long long idx = (long long)m * p.ldy + nn;
-      if (p.y_dtype == OUT_F16) reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(o);
-      else if (p.y_dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(p.y)[idx] = __float2bfloat16_rn(o);
-      else reinterpret_cast<float*>(p.y)[idx] = o;
+      if (qchk(BS_GEMV_Y, idx, p.lim_y)) {
+        if (p.y_dtype == OUT_F16) reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(o);
+        else if (p.y_dtype == OUT_BF16) reinterpret_cast<__nv_bfloat16*>(p.y)[idx] = __float2bfloat16_rn(o);
+        else reinterpret_cast<float*>(p.y)[idx] = o;
+      }
     }
   }
 }
@@ -206,6 +218,9 @@ int run_gemv(const F16GemmArgs& a, cudaStream_t stream) {
   p.y = a.y;
   p.y_dtype = a.y_dtype;
   p.ldy = a.ldy;
+  p.lim_w_bytes = a.fmt == WF_INT8 ? (long long)a.N * a.K : a.w_bytes;
+  p.lim_x = (long long)(a.M - 1) * a.ldx + a.K;
+  p.lim_y = (long long)(a.M - 1) * a.ldy + a.N;
   switch (a.fmt) {
     case WF_INT8: return launch_gemv<DecInt8, true>(p, stream);
     case WF_Q8_0: return launch_gemv<DecQ8_0, false>(p, stream);
@@ -223,5 +238,8 @@ int run_gemv(const F16GemmArgs& a, cudaStream_t stream) {
     default: return -1;
   }
 }
+
+// This translation unit's bounds record (QLIN_CHECKS build).
+QLIN_BOUNDS_READER(bounds_read_gemv)
 
 }  // namespace qlin

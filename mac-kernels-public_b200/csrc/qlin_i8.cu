@@ -19,7 +19,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
 //             bytes of 2-bit high planes; codes are used as stored (u = code)
 // grid = (K/128, n_tiles), block = 128 (one weight row per thread).
 __global__ void w6_repack_kernel(const uint8_t* __restrict__ src, int layout, int N, int K, int num_k_stages,
-                                 uint8_t* __restrict__ out) {
+                                 uint8_t* __restrict__ out, long long out_bytes) {
   const int kst = blockIdx.x, nt = blockIdx.y, r = threadIdx.x;
   const int n = nt * 128 + r;
   uint8_t* st = out + ((size_t)nt * num_k_stages + kst) * (128 * 96);
@@ -35,12 +35,17 @@ __global__ void w6_repack_kernel(const uint8_t* __restrict__ src, int layout, in
       uint32_t code[16];
       for (int i = 0; i < 16; ++i) {
         const int k = kst * 128 + u * 16 + i;
-        uint32_t c;
+        uint32_t c = 0;
+        const long long src_bytes = (long long)N * row_bytes;
         if (layout == 0) {
+          if (!qchk_span(BS_REPACK_SRC, (long long)n * row_bytes + (k / 4) * 3, 3, src_bytes)) continue;
           const uint8_t* w = row + (k / 4) * 3;
           const uint32_t word = w[0] | (w[1] << 8) | (w[2] << 16);
           c = (word >> (6 * (k & 3))) & 0x3F;
         } else {
+          if (!qchk(BS_REPACK_SRC, (long long)n * row_bytes + k / 2, src_bytes) ||
+              !qchk(BS_REPACK_SRC, (long long)n * row_bytes + K / 2 + k / 4, src_bytes))
+            continue;
           const uint32_t lo = (row[k / 2] >> (4 * (k & 1))) & 0xF;
           const uint32_t hi = (row[K / 2 + k / 4] >> (2 * (k & 3))) & 0x3;
           c = lo | (hi << 4);
@@ -62,11 +67,14 @@ __global__ void w6_repack_kernel(const uint8_t* __restrict__ src, int layout, in
       T[u] = t;
     }
   }
+  const long long st_off = ((long long)nt * num_k_stages + kst) * (128 * 96);
   for (int j = 0; j < 4; ++j)
-    *reinterpret_cast<uint4*>(st + (j * 128 + r) * 16) = make_uint4(L[4 * j], L[4 * j + 1], L[4 * j + 2], L[4 * j + 3]);
+    if (qchk_span(BS_REPACK_DST, st_off + (j * 128 + r) * 16, 16, out_bytes))
+      *reinterpret_cast<uint4*>(st + (j * 128 + r) * 16) = make_uint4(L[4 * j], L[4 * j + 1], L[4 * j + 2], L[4 * j + 3]);
   for (int j = 0; j < 2; ++j)
-    *reinterpret_cast<uint4*>(st + ((4 + j) * 128 + r) * 16) =
-        make_uint4(T[4 * j], T[4 * j + 1], T[4 * j + 2], T[4 * j + 3]);
+    if (qchk_span(BS_REPACK_DST, st_off + ((4 + j) * 128 + r) * 16, 16, out_bytes))
+      *reinterpret_cast<uint4*>(st + ((4 + j) * 128 + r) * 16) =
+          make_uint4(T[4 * j], T[4 * j + 1], T[4 * j + 2], T[4 * j + 3]);
 }
 
 // Stage chunks for whole pairs of 128-row tiles (the CTA-pair kernel reads both tiles of a pair);
@@ -74,7 +82,7 @@ __global__ void w6_repack_kernel(const uint8_t* __restrict__ src, int layout, in
 void launch_w6_repack(const uint8_t* src, int layout, int N, int K, uint8_t* out, cudaStream_t s) {
   const int kst = K / 128, nt = (N + 255) / 256 * 2;
   if (kst == 0 || nt == 0) return;
-  w6_repack_kernel<<<dim3(kst, nt), 128, 0, s>>>(src, layout, N, K, kst, out);
+  w6_repack_kernel<<<dim3(kst, nt), 128, 0, s>>>(src, layout, N, K, kst, out, (long long)w6_repacked_bytes(N, K));
 }
 
 size_t w6_repacked_bytes(int N, int K) { return (size_t)((N + 255) / 256 * 2) * (K / 128) * 128 * 96; }
@@ -210,6 +218,9 @@ int run_i8_gemm(int bits, const void* xq, long long kp, const float* sx, int M, 
   p.y_dtype = y_dtype;
   p.ldy = ldy;
   p.status = reinterpret_cast<DeviceStatus*>(device_status_ptr());
+  p.lim_y = (long long)(M - 1) * ldy + N;
+  p.lim_w_bytes = bits == 4 ? (long long)N * K / 2 : (long long)w6_repacked_bytes(N, K);
+  p.lim_scales = scale_kind == I8S_GROUP_F16 ? (long long)N * p.groups_per_row : (long long)N;
   CUtensorMap tx, tw;
   // activation box: the token tile (the pair kernel: half of it per CTA)
   int rc = make_tmap_2d(&tx, xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)kp, (uint64_t)M, (uint64_t)kp, 128,
@@ -228,5 +239,8 @@ int run_i8_gemm(int bits, const void* xq, long long kp, const float* sx, int M, 
   if (tn == 128) return group == 64 ? launch_i8p<DecW6, 128, 2>(tx, tw, p, stream) : launch_i8p<DecW6, 128, 1>(tx, tw, p, stream);
   return dispatch_i8<DecW6>(tm, tx, tw, p, stream);
 }
+
+// This translation unit's bounds record (QLIN_CHECKS build).
+QLIN_BOUNDS_READER(bounds_read_i8)
 
 }  // namespace qlin

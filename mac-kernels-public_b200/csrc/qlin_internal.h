@@ -15,14 +15,14 @@ int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int
 void launch_gguf_dequant(const uint8_t* raw, int qtype, long long total, void* out, int out_dtype, cudaStream_t s);
 void launch_gguf_row_exp(const uint8_t* raw, int qtype, int N, int K, int n_pad, int32_t* row_exp, cudaStream_t s);
 void launch_gguf_straddle_repack(const uint8_t* raw, int qtype, int N, int K, int n_pad, int ldw, void* out,
-                                 int32_t* row_exp, cudaStream_t s);
+                                 size_t out_bytes, int32_t* row_exp, cudaStream_t s);
 void launch_gguf_repack(const uint8_t* raw, int qtype, int N, int K, int num_k_stages, int n_tiles, uint8_t* out,
-                        uint32_t stage_bytes, int P, int S, cudaStream_t s);
+                        size_t out_bytes, uint32_t stage_bytes, int P, int S, cudaStream_t s);
 void launch_splitk_finalize(const float* partial, int splits, int M, int N, int Mp, const void* col_scale,
                             int cs_kind, const int32_t* w_row_exp, const int32_t* x_row_exp,
                             const float* x_row_scale, const void* bias, int bias_kind, void* y, int y_dtype,
                             long long ldy, cudaStream_t s,
-                            const PeerOut* out = nullptr, int lora = 0);
+                            const PeerOut* out = nullptr, int lora = 0, size_t partial_bytes = 0);
 
 // Fused-LoRA operands: T'[m][r] = bf16(t[m][r] * 2^-f[m]) and U'[n][r] = bf16(up[n][r] * scale / cs[n])
 // (cs: the linear's column scale; 2^e[n] for GGUF), zero past r = R and n = N.
@@ -54,6 +54,7 @@ struct F16GemmArgs {
   long long x_slab_stride = 0;  // elements between slabs
   int M, N, K;
   const void* w;  // INT8: raw int8 [N, K]; F16: fp16 [N, ldw]; GGUF: repacked stages
+  long long w_bytes = 0;  // GGUF: bytes of the repacked stages (the bounds-checked build tests copies against it)
   long long ldw = 0;  // F16 weights: row pitch in elements (0: K)
   const int32_t* w_row_exp;
   const void* col_scale;
@@ -107,5 +108,16 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
                  uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz);
 int sm_count();
 void* device_status_ptr();
+
+// Bounds records of the QLIN_CHECKS build, one reader per translation unit that launches
+// kernels (qlin_checks.cuh); each returns 0, 1 in the unchecked build, -1 on a CUDA error.
+struct BoundsRecord;
+int bounds_read_api(BoundsRecord* out, int reset);
+int bounds_read_aux(BoundsRecord* out, int reset);
+int bounds_read_f16(BoundsRecord* out, int reset);
+int bounds_read_f16_blk(BoundsRecord* out, int reset);
+int bounds_read_f16_kq(BoundsRecord* out, int reset);
+int bounds_read_gemv(BoundsRecord* out, int reset);
+int bounds_read_i8(BoundsRecord* out, int reset);
 
 }  // namespace qlin

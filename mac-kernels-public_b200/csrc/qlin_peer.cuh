@@ -71,7 +71,7 @@ __device__ __forceinline__ bool peer_wait(const PeerOut& po, DeviceStatus* statu
   const uint64_t limit = (uint64_t)(po.timeout_ms ? po.timeout_ms : 10000u) * 1000000ull;
   const uint64_t t0 = globaltimer();
   for (int r = 0; r < po.world; ++r) {
-    if (r == po.self) continue;
+    if (r == po.self || !qchk(BS_PEER_FLAG, r, kMaxPeers)) continue;
     while ((int)(ld_acquire_sys(&own->flags[r]) - want) < 0) {
       if (globaltimer() - t0 > limit) {
         if (status != nullptr && atomicExch(&status->timed_out, 1u) == 0u)
@@ -97,7 +97,7 @@ __device__ __forceinline__ void peer_signal_last_cta(const PeerOut& po) {
   own->epoch = e;
 #pragma unroll
   for (int r = 0; r < kMaxPeers; ++r)
-    if (r < po.world) st_release_sys(&po.sync[r]->flags[po.self], e);
+    if (r < po.world && qchk(BS_PEER_FLAG, po.self, kMaxPeers)) st_release_sys(&po.sync[r]->flags[po.self], e);
 }
 
 }  // namespace qlin

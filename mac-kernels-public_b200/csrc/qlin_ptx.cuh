@@ -9,6 +9,8 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
+#include "qlin_checks.cuh"
+
 #ifndef QLIN_WAIT_TIMEOUT_NS
 #define QLIN_WAIT_TIMEOUT_NS 2000000000ull  // 2 s
 #endif

@@ -25,7 +25,7 @@ from ._lib import QlinDecline, QlinError, check, lib
 
 __all__ = ["int8_linear", "int8_linear_streamed", "gguf_linear", "gguf_linear_slabs", "gguf_linear_allgather", "peer_wait", "dequantize_gguf", "w4a8_linear", "w4a8_int8_linear", "dequantize_w4a8_int8_weight",
            "quantize_int8_rowwise", "prologue_f16", "repack_gguf", "GGUF_TYPES", "QlinDecline", "QlinError",
-           "device_status", "int8_linear_grad_input", "w4a8_linear_grad_input", "int8_linear_trainable",
+           "device_status", "bounds_check", "int8_linear_grad_input", "w4a8_linear_grad_input", "int8_linear_trainable",
            "w4a8_linear_trainable"]
 
 # ggml type id -> (name, values per block, bytes per block)
@@ -71,6 +71,35 @@ def device_status(reset=True):
     where = ctypes.c_uint32(0)
     code = lib.qlin_device_status(1 if reset else 0, ctypes.byref(where))
     return code, where.value
+
+
+# Site numbers of the bounds-checked build (enum BoundsSite in csrc/qlin_checks.cuh).
+SITE_NAMES = {
+    1: "gemm output", 2: "gemm bias/scale/exponent", 3: "gemm token exponent", 4: "gemm split-K partial",
+    5: "gemm weight bulk copy", 6: "gemm LoRA up row", 7: "gemm staged/peer store", 8: "gemm shared memory",
+    9: "TMA coordinate alignment", 10: "int8 gemm output", 11: "int8 gemm scale/bias", 12: "int8 gemm weight bulk copy",
+    13: "int8 gemm shared memory", 14: "small-M weights", 15: "small-M activations", 16: "small-M output/bias/scale",
+    17: "prologue input", 18: "prologue output", 19: "repack/decode source", 20: "repack/decode destination",
+    21: "split-K finalize", 22: "LoRA packing", 23: "gradient kernels", 24: "kitchen grid", 25: "peer flags",
+}
+
+
+def bounds_check(reset=True):
+    """Bounds record of the library built with QLIN_CHECKS (libqlin_checked.so, selected with the
+    QLIN_LIB environment variable): None when no check failed since the last reset, else a dict
+    with the number of failures and the first one's site, index, limit and block.  Raises
+    QlinDecline on the ordinary build, which has no checks."""
+    import ctypes
+    count, site, block = ctypes.c_uint32(0), ctypes.c_uint32(0), ctypes.c_uint32(0)
+    index, limit = ctypes.c_int64(0), ctypes.c_int64(0)
+    rc = lib.qlin_bounds_check(1 if reset else 0, ctypes.byref(count), ctypes.byref(site), ctypes.byref(index),
+                               ctypes.byref(limit), ctypes.byref(block))
+    if rc != 0:
+        raise QlinDecline(rc, lib.qlin_last_error().decode())
+    if count.value == 0:
+        return None
+    return {"count": count.value, "site": SITE_NAMES.get(site.value, site.value), "index": index.value,
+            "limit": limit.value, "block": block.value}
 
 
 # ---------------------------------------------------------------------------------------------- INT8

@@ -25,6 +25,8 @@ SIGNATURES = {
     "qlin_version": (ctypes.c_char_p, []),
     "qlin_last_error": (ctypes.c_char_p, []),
     "qlin_device_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint32)]),
+    "qlin_bounds_check": (_i, [_i, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32),
+                               ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_uint32)]),
     "qlin_int8_linear_workspace": (_sz, [_i64, _i64, _i64]),
     "qlin_int8_linear": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i, _p, _i, _i, _p, _i, _i64, _p, _sz, _p]),
     "qlin_int8_linear_lora_workspace": (_sz, [_i64, _i64, _i64, _i64]),

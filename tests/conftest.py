@@ -5,7 +5,8 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "mac-kernels-public_b200")
-for p in (ROOT, PKG):
+TESTS = os.path.join(ROOT, "tests")
+for p in (ROOT, PKG, TESTS):
     if p not in sys.path:
         sys.path.insert(0, p)
 

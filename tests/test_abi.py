@@ -74,3 +74,21 @@ def test_cpu_tensors_are_refused_loudly():
     import qlin
     with pytest.raises(NotImplementedError):
         qlin.int8_linear(torch.zeros(2, 16), torch.zeros(4, 16, dtype=torch.int8), torch.ones(4))
+
+
+def test_bounds_check_entry_point_in_both_builds():
+    """The ordinary library declines qlin_bounds_check (it has no checks) without touching a
+    device; the bounds-checked build (built by build() next to it) loads and exports the same
+    entry points."""
+    from qlin import _lib
+    count, site, block = ctypes.c_uint32(7), ctypes.c_uint32(0), ctypes.c_uint32(0)
+    index, limit = ctypes.c_int64(0), ctypes.c_int64(0)
+    rc = _lib.lib.qlin_bounds_check(1, ctypes.byref(count), ctypes.byref(site), ctypes.byref(index),
+                                    ctypes.byref(limit), ctypes.byref(block))
+    assert rc == 1 and b"QLIN_CHECKS" in _lib.lib.qlin_last_error()
+    checked = os.path.join(ROOT, "mac-kernels-public_b200", "qlin", "libqlin_checked.so")
+    if not os.path.exists(checked):
+        pytest.skip("the bounds-checked build is made by __graft_entry__.build()")
+    lib = ctypes.CDLL(checked)
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing

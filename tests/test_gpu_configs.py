@@ -15,9 +15,11 @@ sampled value must be finite.  Each test prints its max-abs-rel.
   5  MMDiT-stack layers: Q4_K QKV X [4608, 3072] x W [9216, 3072] and Q6_K MLP-down
      X [4608, 12288] x W [3072, 12288]
 
-Configurations 3 and 4 are checked twice: int32-exact (integer activations whose row maximum is
-127 quantize with scale exactly 1; power-of-two group scales; fp32 output must equal the exact
-integer sum bit for bit) and on the configuration's random data, where the GPU's own per-token
+Configuration 1 is also checked integer-exact (Q8_0 blocks of scale 1, integer activations and
+bias, every output equal to the exact integer).  Configurations 3 and 4 are checked twice:
+int32-exact (integer activations whose row maximum is 127 quantize with scale exactly 1;
+power-of-two group scales; an integer bias; fp32 output must equal the exact integer sum bit for
+bit) and on the configuration's random data, where the GPU's own per-token
 int8 activations (bit-identical to the oracle's quantizer on the sampled rows) feed an exact
 integer reference and the fp16 output must be within 2e-3 of it.
 """
@@ -25,11 +27,11 @@ import numpy as np
 import pytest
 import torch
 
+import checks as C
+from checks import finite_and_close as _finite_and_close, group_sums_f64 as _group_sums_f64, sample_rows
 from oracle import qlin_oracle as O
 
 pytestmark = pytest.mark.gpu
-
-TOL_F16 = 2e-3
 
 
 @pytest.fixture(scope="module")
@@ -37,21 +39,6 @@ def qlin():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     import qlin as q
     return q
-
-
-def sample_rows(m):
-    """Rows 61 apart, the last row of every 192-row span and the last row: every token tile of
-    every size the planner picks (16 .. 256) holds at least one sampled row."""
-    return np.array(sorted(set(range(0, m, 61)) | set(range(191, m, 192)) | {m - 1}))
-
-
-def _finite_and_close(name, got, ref, tol=TOL_F16):
-    got = np.asarray(got, dtype=np.float64)
-    assert np.isfinite(got).all(), f"{name}: non-finite outputs (a tile was not written)"
-    err = O.max_abs_rel(got, ref)
-    print(f"{name}: max-abs-rel {err:.3e} over {got.shape[0]} sampled rows x {got.shape[1]} channels")
-    assert err <= tol, (name, err)
-    return err
 
 
 def _status(qlin):
@@ -73,6 +60,20 @@ def test_cfg1_gguf_256x3072x3072(qlin, qtype):
     for mm in (1, 16):
         ys = qlin.gguf_linear(x[:mm].cuda(), torch.from_numpy(raw).cuda(), qtype, (n, k))
         _finite_and_close(f"cfg1 {O.GGUF_TYPES[qtype][0]} M={mm}", ys.float().cpu().numpy(), ref[:mm])
+    _status(qlin)
+
+
+@pytest.mark.parametrize("m", [256, 16, 1])
+def test_cfg1_q8_0_integer_exact(qlin, m):
+    """Q8_0 blocks of scale 1 with integer codes, integer activations and an integer bias: the fp32
+    output must equal the exact integer answer in every row and channel, whatever the tile shape,
+    K split or accumulation order (an fp16 accumulator, a dropped K stage or split, a misplaced
+    tile or a doubled bias all change it)."""
+    k, n = 3072, 3072
+    x, raw, bias, want = C.q8_0_integer_case(m, k, n)
+    y = qlin.gguf_linear(torch.from_numpy(x).cuda(), torch.from_numpy(raw).cuda(), 8, (n, k),
+                         bias=torch.from_numpy(bias).cuda(), out_dtype=torch.float32)
+    C.integer_exact(f"cfg1 Q8_0 integer M={m}", y.cpu().numpy(), want)
     _status(qlin)
 
 
@@ -102,38 +103,16 @@ def _pack(wq, bits):
     return O.pack_w4_uniform(wq).view(np.uint8) if bits == 4 else O.pack_w6_interleaved(wq)
 
 
-def _group_sums_f64(xq, wq, scales, group):
-    """sum_g s[n, g] * P_g[m, n] with every P_g formed exactly (float64 holds these integer dot
-    products exactly: |P_g| < 2^22) and the scaled sum accumulated in float64."""
-    xq = np.asarray(xq, dtype=np.float64)
-    wq = np.asarray(wq, dtype=np.float64)
-    s = np.asarray(scales, dtype=np.float64)
-    y = np.zeros((xq.shape[0], wq.shape[0]))
-    for g in range(wq.shape[1] // group):
-        sl = slice(g * group, (g + 1) * group)
-        y += (xq[:, sl] @ wq[:, sl].T) * s[:, g][None, :]
-    return y
-
-
 @pytest.mark.parametrize("case", sorted(A8_CASES))
 def test_a8_int32_exact_full_shape(qlin, case):
     m, k, n, bits, group = A8_CASES[case]
-    rng = np.random.default_rng(17)
-    x = rng.integers(-127, 128, (m, k), dtype=np.int16).astype(np.float32)
-    x[:, 5] = 127.0  # row absmax 127 -> activation scale exactly 1
-    lo, hi = (-8, 8) if bits == 4 else (-32, 32)
-    wq = rng.integers(lo, hi, (n, k), dtype=np.int8)
-    groups = k // group
-    expo = (np.arange(n)[:, None] + np.arange(groups)[None, :]) % 3
-    s = np.ldexp(1.0, -expo).astype(np.float16)  # 1, 1/2, 1/4 by row and group
+    x, wq, s, bias = C.a8_integer_case(m, k, n, bits, group)
     y = qlin.w4a8_linear(torch.from_numpy(x).to(torch.float16).cuda(), torch.from_numpy(_pack(wq, bits).copy()).cuda(),
-                         torch.from_numpy(s).cuda(), bits=bits, group_size=group, out_dtype=torch.float32)
-    got = y.cpu().numpy()
-    assert np.isfinite(got).all()
+                         torch.from_numpy(s).cuda(), bits=bits, group_size=group, bias=torch.from_numpy(bias).cuda(),
+                         out_dtype=torch.float32)
     rows = sample_rows(m)
-    want = _group_sums_f64(x[rows], wq, s, group)
-    assert np.array_equal(got[rows].astype(np.float64), want), np.abs(got[rows] - want).max()
-    print(f"{case} int32-exact: {len(rows)} sampled rows x {n} channels bit-identical, {groups} groups along K={k}")
+    C.a8_exact(case, y.cpu().numpy(), x, wq, s, group, bias, rows)
+    print(f"{case} int32-exact: {len(rows)} sampled rows x {n} channels bit-identical, {k // group} groups along K={k}")
     _status(qlin)
 
 

@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 import torch
 
+import checks as C
 from oracle import qlin_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -79,15 +80,13 @@ def test_gguf_decoded_weights_through_the_linear(qlin, qtype):
     bit for bit; the others stay within two fp16 rounding steps at the row's largest weight."""
     n, k = 256, 512
     raw = O.random_gguf_blocks(qtype, n, k, seed=70 + qtype)
-    wn, e = O.gguf_normalized_fp16(raw, qtype, n, k)
-    exact = np.ldexp(wn.astype(np.float32), e.reshape(-1, 1)).T  # [k, n]
     w = O.gguf_dequantize(raw, qtype, n, k).T
     raw_d = torch.from_numpy(raw).cuda()
     eye = torch.eye(k, dtype=torch.float16)
     for rows in (slice(0, k), slice(37, 39)):
         y = qlin.gguf_linear(eye[rows].cuda(), raw_d, qtype, (n, k), out_dtype=torch.float32).cpu().numpy()
         if qtype in EXACT_DECODE:
-            assert np.array_equal(y, exact[rows]), qtype  # equal values (+0 and -0 alike)
+            C.onehot_exact(O.GGUF_TYPES[qtype][0], y, raw, qtype, n, k, rows)  # +0 and -0 alike
         else:
             tol = np.abs(w).max(axis=0) * 2.0 ** -9
             assert np.all(np.abs(y - w[rows]) <= tol), (qtype, np.abs(y - w[rows]).max())
