@@ -404,6 +404,57 @@ def _timed_replays(fn, steps, warmup, flush, stream, dev, world):
     return _max_over_ranks(ms, dev, world)
 
 
+def _shard_linear_chain(st, x, dev):
+    """A workload of the rank's shard linears: every block's gguf_linear_slabs calls of the
+    NCCL-transport forward, in its order and shapes, on inputs that stay resident (the block input
+    for linears reading it, random gathered-layout slabs for the others).  It contains no
+    collective, so its time is the compute side of the stack."""
+    import qlin
+    kw = dict(dtype=torch.float16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    ins, outs = {}, {}
+    for name, _, _, n, k, src, _, _ in st.layers:
+        if src == "x":
+            ins[name] = x[:st.mc].unsqueeze(0)
+        else:
+            ins[name] = torch.randn(st.p, st.mc, k // st.p, generator=gen, **kw)
+        outs[name] = torch.empty(st.mc, n // st.p, **kw)
+
+    def run():
+        for layer in st.blocks:
+            for name, _, _, n, _, _, _, _ in st.layers:
+                qtype, _, _, packed, row_exp = layer[name]
+                for _c in range(st.chunks):
+                    qlin.gguf_linear_slabs(ins[name], packed, row_exp, qtype, n // st.p, out=outs[name])
+    return run
+
+
+def _allgather_chain(st, dev):
+    """A workload of NCCL all-gathers alone: every gathered output of the forward, per block and
+    chunk, gathered back to back on the current stream ([mc, n/p] local -> [p, mc, n/p])."""
+    kw = dict(dtype=torch.float16, device=dev)
+    bufs = [(torch.zeros(st.mc, n // st.p, **kw), torch.empty(st.p * st.mc, n // st.p, **kw))
+            for _, _, _, n, _, _, _, g in st.layers if g]
+
+    def run():
+        for _ in st.blocks:
+            for loc, gat in bufs:
+                for _c in range(st.chunks):
+                    torch.distributed.all_gather_into_tensor(gat, loc, group=st.group)
+    return run
+
+
+def _graphed_chain(run):
+    """run() once eagerly (communicators, workspaces), then captured into a CUDA graph."""
+    run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    torch.cuda.synchronize()
+    return g
+
+
 def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
     """Configuration 5: the MMDiT block linear stack (60 blocks of QKV / out / MLP-up Q4_K and
     MLP-down Q6_K GGUF linears, 4608 tokens, hidden 3072), weights sharded along N over the ranks
@@ -411,8 +462,9 @@ def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
     column slabs by the GEMM epilogues' stores into every rank's buffer over NVLink ("peer", the
     default) or by NCCL all-gathers on a side stream ("nccl").  Times are the max over ranks.
 
-    With several GPUs it also reports, per forward: the same stack over NCCL, its GEMMs alone
-    (exchange skipped) and its all-gathers alone (NCCL, back to back), the overlap those imply, the
+    With several GPUs it also reports, per forward: the same stack over NCCL, two workloads of
+    their own that bound it -- the rank's shard linears back to back on resident inputs (compute)
+    and NCCL all-gathers of the same sizes back to back (exchange) -- the overlap those imply, the
     variant that gathers every output (QKV's too), and the M-split replica control (every GPU holds
     all weights and runs 4608 / N tokens, no exchange)."""
     from qlin.sharded import ShardedStack
@@ -473,13 +525,11 @@ def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
         graphed(nc)
         t_nccl = _timed_replays(nc.replay, sub, 2, flush, stream, dev, world)
         nc.release()
-        graphed(nc, exchange=False)
-        t_comp = _timed_replays(nc.replay, sub, 2, flush, stream, dev, world)
-        nc.release()
-        nc.comm_only()
-        torch.cuda.synchronize()
-        nc.capture_comm()
-        t_comm = _timed_replays(nc.replay_comm, sub, 2, flush, stream, dev, world)
+        g_comp = _graphed_chain(_shard_linear_chain(nc, x, dev))
+        t_comp = _timed_replays(g_comp.replay, sub, 2, flush, stream, dev, world)
+        g_comm = _graphed_chain(_allgather_chain(nc, dev))
+        t_comm = _timed_replays(g_comm.replay, sub, 2, flush, stream, dev, world)
+        del g_comp, g_comm  # graphs holding NCCL calls go before the process group
         nc.close()
         del nc
         gbytes = st.gathered_bytes_per_forward()
@@ -490,8 +540,9 @@ def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
             "nvlink_floor_ms": gbytes / 770e9 * 1e3,
             "tensor_floor_ms": st.flops() / world / (peaks()["tflops"] * 1e12) * 1e3,
             "limiter": "nvlink" if gbytes / 770e9 * 1e3 > t_comp else "compute",
-            "note": "compute = the NCCL-transport stack with its exchange skipped; comm = its all-gathers back to "
-                    "back; nvlink floor = bytes each rank receives / 770 GB/s (measured peer copy)"}
+            "note": "compute = this rank's shard linears of every block back to back on resident inputs of their "
+                    "shapes (no collective in that workload); comm = NCCL all-gathers of the forward's sizes back "
+                    "to back; nvlink floor = bytes each rank receives / 770 GB/s (measured peer copy)"}
         # every output gathered (QKV's too)
         if args.mmdit_gather != "all":
             al = ShardedStack(blocks=blocks, tokens=tokens, hidden=hidden, chunks=chunks, device=dev,

@@ -240,23 +240,13 @@ class ShardedStack:
             self.graph_output = self.forward(self.graph_input, **kw)
         return self.graph_output
 
-    def capture_comm(self):
-        """Records comm_only() into a CUDA graph of its own (replay_comm())."""
-        self.comm_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.comm_graph):
-            self.comm_only()
-
     def replay(self):
         self.graph.replay()
         return self.graph_output
 
-    def replay_comm(self):
-        self.comm_graph.replay()
-
     def release(self):
         self.graph = None
         self.graph_output = None
-        self.comm_graph = None
 
     def flops(self):
         return len(self.blocks) * sum(2.0 * self.tokens * n * k for _, _, _, n, k, _, _, _ in self.layers)
@@ -277,15 +267,13 @@ class ShardedStack:
             return self.local[src][c][:, col0:col0 + k].unsqueeze(0)
         return self.gathered[src][c]
 
-    def forward(self, x, exchange=True):
+    def forward(self, x):
         """x: [tokens, hidden] fp16 on this rank's device (the same on every rank).  Returns the
-        last block's output as chunk slabs ([p, mc, hidden/p] each, or [1, mc, hidden] on one GPU).
-        exchange=False (NCCL transport) skips the all-gathers: the GEMMs read whatever the gathered
-        buffers hold, which times the compute alone."""
+        last block's output as chunk slabs ([p, mc, hidden/p] each, or [1, mc, hidden] on one GPU)."""
         if self.transport == "peer":
             return self._forward_peer(x)
         multi = self.comm is not None
-        gather = exchange and self.p > 1
+        gather = self.p > 1
         comp = torch.cuda.current_stream(self.device) if self.cuda else None
         if multi and gather:
             self.comm.wait_stream(comp)  # (forked only when used: a graph capture must rejoin it)
@@ -324,16 +312,6 @@ class ShardedStack:
         if multi and gather:
             comp.wait_stream(self.comm)
         return inp
-
-    def comm_only(self):
-        """The forward's all-gathers alone, back to back on the current stream (NCCL transport):
-        the exchange time that the fused or overlapped forward hides behind its GEMMs."""
-        for _ in self.blocks:
-            for name, _, _, n, _, _, _, gathered in self.layers:
-                if gathered and self.p > 1:
-                    for c in range(self.chunks):
-                        torch.distributed.all_gather_into_tensor(self.gathered[name][c].view(-1, n // self.p),
-                                                                 self.local[name][c], group=self.group)
 
     def _forward_peer(self, x):
         inp = [x[c * self.mc:(c + 1) * self.mc].unsqueeze(0) for c in range(self.chunks)]

@@ -62,11 +62,19 @@ def _dense_reference(x, gather):
     return h.float()
 
 
+def _free_port():
+    """A TCP port on 127.0.0.1 that nothing listens on right now (the OS picks it)."""
+    import socket
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
 @pytest.mark.parametrize("gather", ["consumed", "all"])
 def test_two_rank_sharded_stack_matches_dense(gather):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + os.getpid() % 1000 + (gather == "all")
+    port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q, gather)) for r in range(2)]
     for p in procs:
         p.start()
