@@ -11,11 +11,9 @@
 // the scale in the epilogue.
 //
 // The rescale is the per-group serial step (its cost grows with every value of every group), so
-// it is kept to one packed-fp32 pair of instructions per two values: each accumulator buffer is
-// pre-biased in TMEM with the bit pattern of 1.5*2^23 (0x4B400000) before its group's first MMA,
-// so the int32 result read back IS the float 1.5*2^23 + P (exact while |P| < 2^22: groups of
-// <= 128 values of 8-bit x 8-bit products), and s*P = s*(f - 1.5*2^23) needs no integer add.
-// The rescale warps re-write the bias right after reading a buffer (one tcgen05.st per 32 values).
+// it is kept to one exact int32 -> fp32 conversion per value and one packed fp32 FMA per two
+// values (ffma2_cvt).  The first MMA of a group overwrites its buffer; the rescale warps hand the
+// buffer back as soon as its values are in registers.
 //
 // Warp roles (448 threads, one CTA per SM, persistent):
 //   warp 0        TMA producer            warp 1   TMEM alloc + MMA issuer
@@ -70,19 +68,21 @@ __device__ __forceinline__ float load_bias_i8(const void* bias, int kind, int n,
   return 0.f;
 }
 
-// (a0, a1) += s * ((f0, f1) - 1.5*2^23) with the packed fp32x2 pipe: the subtraction is exact
-// (Sterbenz), so each lane gets s * P rounded once and added once.
-__device__ __forceinline__ void ffma2_sub_magic(float s, float f0, float f1, float& a0, float& a1) {
-  asm("{\n\t.reg .b64 f, m, sc, acc;\n\t"
+// (a0, a1) += s * (float(p0), float(p1)) for int32 group sums p: two exact conversions (|p| <= 2^24
+// for every group of up to 1024 values of these formats; cvt.rn beyond) and one packed fp32 FMA.
+// Measured against the magic-number form (p + the bits of 1.5 * 2^23, an exact fp32 subtraction,
+// then the FMA): 15-25% faster kernels at configurations 3 and 4, the rescale being the FMA-pipe
+// bound part of the loop.
+__device__ __forceinline__ void ffma2_cvt(float s, uint32_t p0, uint32_t p1, float& a0, float& a1) {
+  const float f0 = (float)(int32_t)p0, f1 = (float)(int32_t)p1;
+  asm("{\n\t.reg .b64 f, sc, acc;\n\t"
       "mov.b64 f, {%2, %3};\n\t"
-      "mov.b64 m, {%4, %4};\n\t"
-      "mov.b64 sc, {%5, %5};\n\t"
+      "mov.b64 sc, {%4, %4};\n\t"
       "mov.b64 acc, {%0, %1};\n\t"
-      "sub.rn.f32x2 f, f, m;\n\t"
       "fma.rn.f32x2 acc, sc, f, acc;\n\t"
       "mov.b64 {%0, %1}, acc;\n\t}"
       : "+f"(a0), "+f"(a1)
-      : "f"(f0), "f"(f1), "f"(12582912.0f), "f"(s));
+      : "f"(f0), "f"(f1), "f"(s));
 }
 
 template <int TM, int STAGES>
@@ -154,22 +154,6 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (warp >= 2 + 4 * Cfg::kDecGroups) {
-    // the rescale warps pre-bias both accumulator buffers before the first MMA
-    constexpr int kCols = TM / Cfg::kEpiParts;
-    constexpr int kChunk = kCols < 32 ? kCols : 32;
-    const int part = (warp - (2 + 4 * Cfg::kDecGroups)) >> 2;
-    const uint32_t bias_bits = p.group <= 128 ? 0x4B400000u : 0u;
-#pragma unroll
-    for (int b = 0; b < 2; ++b)
-#pragma unroll
-      for (int c0 = 0; c0 < kCols; c0 += kChunk)
-        tmem_fill_cols<kChunk>(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + b * TM + part * kCols + c0, bias_bits);
-    tmem_wait_st();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   if (warp == 0) {
     if (elect_one()) {
       uint32_t it = 0;
@@ -219,12 +203,12 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           const uint64_t b_desc = smem_desc_sw128(smem_u32(sx + s * Cfg::kXStageBytes));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            if (gk == 0) {  // first MMA of a group: wait for its (re-biased) accumulator buffer
+            if (gk == 0) {  // first MMA of a group: wait for its accumulator buffer, which it overwrites
               b = g_all & 1;
               if (!mbar_wait(&acc_empty[b], ((g_all >> 1) & 1) ^ 1, abort_flag, p.status, 13)) { ok = false; break; }
               tc_fence_after();
             }
-            mma_i8_ts(tmem_base + b * TM, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, 1u);
+            mma_i8_ts(tmem_base + b * TM, a_tmem + kk * 8, b_desc + (uint64_t)(kk * 2), idesc, gk > 0 ? 1u : 0u);
             gk += 32;
             if (gk == p.group) {
               tc_commit(&acc_full[b]);
@@ -280,11 +264,6 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     const int quarter = warp & 3;
     const int part = ew >> 2;
     const int r = quarter * 32 + lane;
-    // Pre-bias (groups of <= 128 values, exact magic-number conversion) or zero (larger groups,
-    // converted with cvt) for the int32 accumulators; both buffers were filled before the roles
-    // started.
-    const bool magic = p.group <= 128;
-    const uint32_t bias_bits = magic ? 0x4B400000u : 0u;
     uint32_t g_all = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -314,20 +293,9 @@ qgemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           uint32_t v[kChunk];
           tmem_ld_cols<kChunk>(taddr + c0, v);
           tmem_wait_ld();
-          if (magic) {
 #pragma unroll
-            for (int j = 0; j < kChunk; j += 2)
-              ffma2_sub_magic(sg, __uint_as_float(v[j]), __uint_as_float(v[j + 1]), accf[c0 + j], accf[c0 + j + 1]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < kChunk; ++j) accf[c0 + j] = fmaf(sg, (float)(int32_t)v[j], accf[c0 + j]);
-          }
-          // re-bias the columns for the buffer's next group, 8 at a time (an x32 store would need
-          // 32 consecutive registers holding the same value)
-#pragma unroll
-          for (int j = 0; j < kChunk; j += 8) tmem_fill_cols<8>(taddr + c0 + j, bias_bits);
+          for (int j = 0; j < kChunk; j += 2) ffma2_cvt(sg, v[j], v[j + 1], accf[c0 + j], accf[c0 + j + 1]);
         }
-        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[b]);

@@ -16,13 +16,13 @@
 //     or more: one observed commit per 4 MMAs of 256 x 256 x 32 per group of 128;
 //   * TN = 128 with four buffers for groups of 64: the two groups of a 128-deep stage go to two
 //     buffers behind one commit.
-// The first MMA of a group overwrites its buffer; the rescale turns each int32 P into the float
-// 1.5 * 2^23 + P with one integer add of the bit pattern 0x4B400000 (exact while |P| < 2^22: groups
-// of <= 128 values; larger groups convert with cvt), hands the buffer back as soon as its last
-// columns are in registers, and folds s[n, g] * P into fp32 registers with one packed subtract and
-// one packed fma per two values.  Re-biasing the buffers in TMEM instead (one store per 32 values
-// in place of the integer adds) measured 1.7x slower: the stores and their completion wait sit on
-// the buffer's round trip back to the issuer.
+// The first MMA of a group overwrites its buffer; the rescale hands the buffer back as soon as
+// its last columns are in registers and folds s[n, g] * P into fp32 registers with one exact
+// int32 -> fp32 conversion per value and one packed fma per two values (ffma2_cvt).  Measured
+// alternatives: the magic-number conversion (P plus the bit pattern of 1.5 * 2^23 with an integer
+// add, then an exact packed subtraction) was 15-25% slower, the extra FMA-pipe subtraction being
+// on the bound path; re-biasing the buffers in TMEM instead of the integer add measured 1.7x slower
+// (the stores and their completion wait sit on the buffer's round trip back to the issuer).
 //
 // Warp roles (512 threads, one CTA per SM, persistent over tiles; registers rebalanced per
 // warpgroup with setmaxnreg: 40 / 72 / 200 / 200 per thread, 65,536 in all):
@@ -249,7 +249,11 @@ qgemm_i8p_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     const int part = (warp - 8) >> 2;
     const int r = quarter * 32 + lane;  // TMEM lane == weight row within this CTA's tile
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-    const bool magic = p.group <= 128;
+    // The same arithmetic either way; at 256 tokens groups above 128 values take the scalar FMA,
+    // a form with which ptxas fits the 128 running sums with fewer spills (measured: 0.33 against
+    // 0.43 ms at configuration 3), while the 128-token kernels run fastest with the packed form
+    // alone (0.66 against 0.72 ms at configuration 4).
+    const bool paired = p.group <= 128;
     const uint32_t acc_empty_leader = cluster_map(acc_empty, 0);
     // release each batch once so its first use can start
     if (lane == 0)
@@ -302,12 +306,9 @@ qgemm_i8p_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc_empty_leader + (uint32_t)(bt * 8));
           }
-          if (magic) {
-            // |P| < 2^22: P + the bit pattern of 1.5 * 2^23 is the float 1.5 * 2^23 + P exactly
+          if (TN == 128 || paired) {
 #pragma unroll
-            for (int j = 0; j < kChunk; j += 2)
-              ffma2_sub_magic(sg, __uint_as_float(v[j] + 0x4B400000u), __uint_as_float(v[j + 1] + 0x4B400000u),
-                              accf[c0 + j], accf[c0 + j + 1]);
+            for (int j = 0; j < kChunk; j += 2) ffma2_cvt(sg, v[j], v[j + 1], accf[c0 + j], accf[c0 + j + 1]);
           } else {
 #pragma unroll
             for (int j = 0; j < kChunk; ++j) accf[c0 + j] = fmaf(sg, (float)(int32_t)v[j], accf[c0 + j]);

@@ -386,22 +386,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
-// N (8, 16 or 32) consecutive columns of the warp's lane quarter all set to one value.
-template <int N>
-__device__ __forceinline__ void tmem_fill_cols(uint32_t taddr, uint32_t v) {
-  static_assert(N == 8 || N == 16 || N == 32, "tcgen05.st widths used here");
-  if constexpr (N == 32) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-                 "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v) : "memory");
-  } else if constexpr (N == 16) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};"
-                 ::"r"(taddr), "r"(v) : "memory");
-  } else {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
-                 : "memory");
-  }
-}
-
 template <int N>
 __device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[N]) {
   static_assert(N == 8 || N == 16 || N == 32, "tcgen05.st widths used here");
