@@ -279,6 +279,24 @@ def graph_steps(fn, steps, warmup, flush, stream):
     return timed_steps(g.replay, steps, 2, flush, stream)
 
 
+def cold_chain_us(make_fn, copies, steps, flush, stream):
+    """Per-call device time (us) of a small op with its weights cold in L2: `copies` calls, each on
+    its own copy of the weights (together larger than L2), captured back to back in one CUDA graph;
+    L2 is flushed before every replay and the replay time is divided by the number of calls.  This
+    is how a model runs a stack of small-M linears (launch gaps inside a graph included), with every
+    weight byte read from HBM."""
+    fns = [make_fn(i) for i in range(copies)]
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    return statistics.mean(timed_steps(g.replay, steps, 2, flush, stream)) * 1e3 / copies
+
+
 def int8_peak_tops(dev):
     """Dense int8 tensor peak measured the way MEASURED_PEAKS.json measures bf16: torch._int_mm at
     8192^3, best of 10 after warm-up."""
@@ -347,7 +365,16 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
         fl = 2.0 * 256 * 3072 * 3072
         nbytes = raw.numel() + 256 * 3072 * 2 * 2
         cfgs[name] = {"tflops": fl / (t * 1e-3) / 1e12, "us": t * 1e3,
-                      "roofline_frac": roofline_time_s(fl, nbytes, pk) / (t * 1e-3), "timing": "cuda graph replay"}
+                      "roofline_frac": roofline_time_s(fl, nbytes, pk) / (t * 1e-3),
+                      "timing": "cuda graph replay of one call, L2 flushed"}
+        # the same linear in a stack: 16 calls on 16 weight copies (160 MB, cold in L2) in one graph
+        raws = [raw.clone() for _ in range(16)]
+        tc = cold_chain_us(lambda i: (lambda: qlin.gguf_linear(xs, raws[i], qt, (3072, 3072))), 16, steps, flush,
+                           stream)
+        cfgs[name]["chain"] = {"us": tc, "tflops": fl / (tc * 1e-6) / 1e12,
+                               "roofline_frac": roofline_time_s(fl, nbytes, pk) / (tc * 1e-6),
+                               "timing": "16 calls on 16 weight copies per CUDA graph, L2 flushed per replay"}
+        del raws
     # Small M (text tokens, adapter side paths): HBM-bound weight streaming, one launch.
     small = [(8, 3072, 3072, m, f"cfg1_small_gguf_q8_0_{m}x3072x3072") for m in (1, 16, 64)]
     small += [(12, 3072, 12288, 1, "small_m_gguf_q4_k_1x3072x12288"), (2, 3072, 3072, 1, "small_m_gguf_q4_0_1x3072x3072")]
@@ -362,8 +389,16 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
         cfgs[name] = {"us": t * 1e3, "weight_stream_gbs": raw.numel() / (t * 1e-3) / 1e9,
                       "algorithmic_gbs": nbytes / (t * 1e-3) / 1e9,
                       "roofline_frac": roofline_time_s(fl, nbytes, pk) / (t * 1e-3), "bound": "hbm",
-                      "timing": "cuda graph replay, L2 flushed"}
-        del raw
+                      "timing": "cuda graph replay of one call, L2 flushed"}
+        copies = max(16, int(3 * 126e6 // raw.numel()) + 1)  # together about three times L2
+        raws = [raw.clone() for _ in range(copies)]
+        tc = cold_chain_us(lambda i: (lambda: qlin.gguf_linear(xs, raws[i], qt, (n, k))), copies, steps, flush,
+                           stream)
+        cfgs[name]["chain"] = {"us": tc, "weight_stream_gbs": raw.numel() / (tc * 1e-6) / 1e9,
+                               "roofline_frac": roofline_time_s(fl, nbytes, pk) / (tc * 1e-6),
+                               "timing": f"{copies} calls on {copies} weight copies per CUDA graph, L2 flushed per "
+                                         "replay (every weight byte from HBM)"}
+        del raw, raws
     for (m, k, n, bits, grp), name in (((4096, 12288, 3072, 4, 128), "cfg3_w4a8_4096x12288x3072"),
                                        ((3240, 5120, 13824, 6, 64), "cfg4_w6a8_fwd_3240x5120x13824"),
                                        ((3240, 13824, 5120, 6, 64), "cfg4_w6a8_rev_3240x13824x5120")):
