@@ -109,7 +109,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 typedef CUresult (*PFN_ctxGetCurrent_t)(CUcontext*);
 typedef CUresult (*PFN_ctxGetId_t)(CUcontext, unsigned long long*);
 
-static unsigned long long current_context_id() {
+unsigned long long current_context_id() {
   static PFN_ctxGetCurrent_t get_current = nullptr;
   static PFN_ctxGetId_t get_id = nullptr;
   static std::once_flag once;

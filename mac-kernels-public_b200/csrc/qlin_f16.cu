@@ -16,18 +16,28 @@ namespace qlin {
 __device__ DeviceStatus g_status;
 
 void* device_status_ptr() {
-  // One address per device; looked up once per device with that device current.
+  // Looked up once per CUDA context (keyed by the context's unique id, so a context created after
+  // cudaDeviceReset, or a non-primary context the caller made current, gets its own lookup).
   static std::mutex mu;
-  static void* addr[64] = {nullptr};
-  int dev = 0;
-  cudaGetDevice(&dev);
+  struct Entry {
+    unsigned long long ctx;
+    void* addr;
+  };
+  static Entry cache[64] = {};
+  static int next = 0;
   std::lock_guard<std::mutex> lock(mu);
-  if (dev < 0 || dev >= 64) return nullptr;
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_status) == cudaSuccess) addr[dev] = p;
+  unsigned long long id = current_context_id();
+  if (id != 0)
+    for (const Entry& e : cache)
+      if (e.ctx == id) return e.addr;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;  // also makes the context current
+  if (id == 0) id = current_context_id();
+  if (id != 0) {
+    cache[next] = Entry{id, p};
+    next = (next + 1) % 64;
   }
-  return addr[dev];
+  return p;
 }
 
 int sm_count() {

@@ -108,6 +108,9 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
                  uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz);
 int sm_count();
 void* device_status_ptr();
+// Unique id of the calling thread's current CUDA context (0 when there is none); the key of the
+// per-context caches of device-symbol addresses.
+unsigned long long current_context_id();
 
 // Bounds records of the QLIN_CHECKS build, one reader per translation unit that launches
 // kernels (qlin_checks.cuh); each returns 0, 1 in the unchecked build, -1 on a CUDA error.
