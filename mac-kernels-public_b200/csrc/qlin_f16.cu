@@ -291,12 +291,23 @@ void plan_f16(int M, int N, int K, int fmt, int* tm_out, int* splits_out) {
     else tm = 256;  // one token tile; the grid is filled by splitting K
   }
   if (splits == 0) {
+    // Fewer output tiles than SMs: split K.  The CTAs are persistent over (tile, split) units, so
+    // the time goes as rounds x stages per split, ceil(tiles * s / sms) * ceil(kst / s), plus a
+    // fixed cost for the finalize pass once s > 1 (about five stages' time).  The plain rule
+    // s = sms / tiles left a third of the SMs idle at 96 tiles (M = 16, N = 12288); measured there:
+    // 20.6 us with one split against ~14 us with three.
     const int tiles = ((N + 127) / 128) * ((M + tm - 1) / tm);
     splits = 1;
     if (tiles < sms) {
-      splits = std::max(1, sms / std::max(tiles, 1));
-      splits = std::min(splits, std::max(1, kst / 4));  // keep >= 4 stages per split
-      splits = std::min(splits, 16);
+      const int max_s = std::min(16, std::max(1, kst / 4));  // keep >= 4 stages per split
+      long best = (long)kst;
+      for (int sp = 2; sp <= max_s; ++sp) {
+        const long cost = (long)((tiles * sp + sms - 1) / sms) * ((kst + sp - 1) / sp) + 5;
+        if (cost < best) {
+          best = cost;
+          splits = sp;
+        }
+      }
     }
   }
   splits = std::max(1, std::min(splits, kst));
@@ -332,7 +343,7 @@ bool f16_gemm_can_rotate(const F16GemmArgs& a) {
     const char* e = getenv("QLIN_NO_ROT_EPILOGUE");  // tuning knob: rotate in a separate pass
     return e && atoi(e) != 0;
   }();
-  if (disabled || a.fmt != WF_INT8 || a.out != nullptr || a.lora_k != 0 || a.M <= 2 || a.N == 0 ||
+  if (disabled || a.fmt != WF_INT8 || a.out != nullptr || a.lora_k != 0 || a.M <= 1 || a.N == 0 ||
       (a.rot_group != 32 && a.rot_group != 64 && a.rot_group != 128) || !staged_output_ok(a))
     return false;
   int tm = a.tm, splits = a.k_splits;
@@ -342,7 +353,7 @@ bool f16_gemm_can_rotate(const F16GemmArgs& a) {
 
 int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return 0;
-  if (a.M <= 2 && a.lora_k == 0 && a.rot_group == 0) {
+  if (a.M == 1 && a.lora_k == 0 && a.rot_group == 0) {
     const int rc = run_gemv(a, stream);
     if (rc >= 0) return rc;
   }

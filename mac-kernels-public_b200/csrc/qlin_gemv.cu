@@ -1,6 +1,6 @@
-// Small-M path (M <= 2 tokens: text tokens, adapter side paths): a weight-streaming kernel on the
-// CUDA cores instead of the tensor-core GEMM, whose fixed costs (pipeline fill, K split and its
-// finalize pass) dominate when the MMA work is a few microseconds.
+// Small-M path (one token, weights of up to 4096 x 8192: text tokens, adapter side paths): a
+// weight-streaming kernel on the CUDA cores instead of the tensor-core GEMM, whose fixed costs
+// (pipeline fill, K split and its finalize pass) dominate when the MMA work is a few microseconds.
 //
 // A CTA takes 16 output rows and 32 half-warps split the K stages between them; every thread
 // decodes its row's 64 values per stage with the same decoders as the GEMM (reading the repacked
@@ -175,11 +175,7 @@ int launch_gemv_mt(const GemvParams& p, cudaStream_t stream) {
 
 template <class Dec, bool INT8>
 int launch_gemv(const GemvParams& p, cudaStream_t stream) {
-  int rc;
-  switch (p.M) {
-    case 1: rc = launch_gemv_mt<Dec, 1, INT8>(p, stream); break;
-    default: rc = launch_gemv_mt<Dec, 2, INT8>(p, stream); break;
-  }
+  const int rc = launch_gemv_mt<Dec, 1, INT8>(p, stream);
   if (rc) return rc;
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -197,7 +193,11 @@ int run_gemv(const F16GemmArgs& a, cudaStream_t stream) {
     const char* e = getenv("QLIN_NO_GEMV");  // tuning knob: force the tensor-core GEMM for small M
     return e && atoi(e) != 0;
   }();
-  if (disabled || a.M < 1 || a.M > 2 || a.out != nullptr || (a.x_slabs > 1) || a.K % 64 != 0 || a.ldx % 8 != 0 ||
+  // Measured against the tensor-core GEMM on weights cold in L2 (graphs of calls over weight copies,
+  // all twelve GGUF types): faster at M = 1 on 3072 x 3072 weights (7.7-8.7 against 10.8-11.6 us),
+  // equal or slower at N = 12288 or K = 12288 (more CTAs than one wave, longer rows per thread),
+  // and slower at M = 2 for every type but Q3_K / Q5_K (15.7 against 11.2 us for most).
+  if (disabled || a.M != 1 || a.N > 4096 || a.K > 8192 || a.out != nullptr || (a.x_slabs > 1) || a.K % 64 != 0 || a.ldx % 8 != 0 ||
       (reinterpret_cast<uintptr_t>(a.x) & 15) || (size_t)a.M * a.K * sizeof(float) > kGemvMaxXBytes)
     return -1;
   if (a.fmt == WF_INT8 && (reinterpret_cast<uintptr_t>(a.w) & 15)) return -1;

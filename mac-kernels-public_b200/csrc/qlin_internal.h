@@ -87,7 +87,7 @@ int run_f16_gemm(const F16GemmArgs& a, cudaStream_t stream);
 // 128 (one 128-row weight tile), no small-M kernel, no K split, the staged 2-byte output path, a
 // plain output.
 bool f16_gemm_can_rotate(const F16GemmArgs& a);
-// Small-M (M <= 2) weight-streaming kernel; -1 when it does not apply.
+// Small-M (M = 1) weight-streaming kernel; -1 when it does not apply.
 int run_gemv(const F16GemmArgs& a, cudaStream_t stream);
 size_t f16_gemm_partial_bytes(int M, int N, int K, int fmt, int tm, int k_splits);
 void plan_f16(int M, int N, int K, int fmt, int* tm, int* k_splits);

@@ -8,7 +8,7 @@ child process that loads the checked library through QLIN_LIB, with fresh alloca
 requires after every call: no failed check, no timed-out wait, and outputs that match the CPU
 oracle.  Cases:
 
-  GGUF linear     all twelve types at M = 1, 2 (small-M kernel), 37, 300 and a K-split shape;
+  GGUF linear     all twelve types at M = 1 (small-M kernel), 2, 37, 300 and a K-split shape;
                   fp32 / bf16 inputs (prologue), fp32 / bf16 outputs, bias; rows straddling blocks
   INT8 linear     ConvRot groups 128 (tensor-core prologue, rotated epilogue) and 256, plain
   W4A8 / W6A8     groups 64 / 128 / per channel, M = 33 (single-CTA kernel) and 100 / 300 (pairs)

@@ -75,15 +75,15 @@ EXACT_DECODE = (2, 6, 8, 20)  # Q4_0, Q5_0, Q8_0, IQ4_NL: RN16(w * 2^-e), one ro
 @pytest.mark.parametrize("qtype", ALL_TYPES)
 def test_gguf_decoded_weights_through_the_linear(qlin, qtype):
     """One-hot activation rows pull single decoded weights through the linear (fp32 output, no
-    bias; adding zeros is exact): the identity over all K columns runs the tensor-core GEMM, two
-    rows run the small-M kernel.  Types decoded with one rounding must give RN16(w * 2^-e) * 2^e
+    bias; adding zeros is exact): the identity over all K columns runs the tensor-core GEMM, one
+    row the small-M kernel and two rows the GEMM's split-K path.  Types decoded with one rounding must give RN16(w * 2^-e) * 2^e
     bit for bit; the others stay within two fp16 rounding steps at the row's largest weight."""
     n, k = 256, 512
     raw = O.random_gguf_blocks(qtype, n, k, seed=70 + qtype)
     w = O.gguf_dequantize(raw, qtype, n, k).T
     raw_d = torch.from_numpy(raw).cuda()
     eye = torch.eye(k, dtype=torch.float16)
-    for rows in (slice(0, k), slice(37, 39)):
+    for rows in (slice(0, k), slice(37, 38), slice(37, 39)):
         y = qlin.gguf_linear(eye[rows].cuda(), raw_d, qtype, (n, k), out_dtype=torch.float32).cpu().numpy()
         if qtype in EXACT_DECODE:
             C.onehot_exact(O.GGUF_TYPES[qtype][0], y, raw, qtype, n, k, rows)  # +0 and -0 alike
@@ -303,7 +303,7 @@ def _small_m_k(qtype, i):
 @pytest.mark.parametrize("qtype", ALL_TYPES)
 @pytest.mark.parametrize("m,n,ki", [(1, 200, 0), (2, 384, 1), (9, 130, 2), (31, 256, 3), (64, 384, 4)])
 def test_small_m_kernel_matches_fp64(qlin, qtype, m, n, ki):
-    """Small M (text tokens, adapter side paths: the weight-streaming kernel for M <= 2, the
+    """Small M (text tokens, adapter side paths: the weight-streaming kernel for M = 1, the
     tensor-core GEMM with its K split above): odd stage counts, ragged N, K not a multiple of 64,
     and calls repeated bit for bit (the K-split partials are reduced in a fixed order)."""
     k = _small_m_k(qtype, ki)
