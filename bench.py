@@ -40,6 +40,8 @@ for _p in (ROOT, PKG):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+import bench_inputs as BI  # noqa: E402
+
 M, K, N = 4096, 3072, 12288
 GROUP = 128
 REF_BUDGET_S = 150.0  # reference arm: bound on the host-side run (warm-up + timed steps), seconds
@@ -167,9 +169,8 @@ KIND = "restatement"  # the reference's CPU path restated in oracle/qlin_oracle.
 
 
 def cpu_baseline(steps=2, rows=M):
-    from oracle import qlin_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
-    x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=0)
+    x, q, s, b = BI.cfg2_int8_convrot(M, K, N, seed=0)
     cpu_reference_step(x, q, s, b, 16)  # warm the BLAS threads
     t0 = time.perf_counter()
     for _ in range(steps):
@@ -192,7 +193,7 @@ class _StackReferenceStep:
         self.O = O
         hid, self.tokens = 3072, 4608
         self.lin = [(12, 3 * hid, hid), (12, hid, hid), (12, 4 * hid, hid), (14, hid, 4 * hid)]
-        self.raw = [O.random_gguf_blocks(qt, n, k, seed=i) for i, (qt, n, k) in enumerate(self.lin)]
+        self.raw = [BI.gguf_blocks(qt, n, k, seed=i) for i, (qt, n, k) in enumerate(self.lin)]
         g = torch.Generator().manual_seed(7)
         self.x = {k: torch.randn(self.tokens, k, generator=g) for k in (hid, 4 * hid)}
         self.frac = frac
@@ -222,9 +223,8 @@ def run_reference(args, rank, world):
         return
     steps, warm = max(1, args.steps), max(0, args.warmup)
     torch.set_num_threads(os.cpu_count() or 1)
-    from oracle import qlin_oracle as O
     if world == 1:
-        x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=0)
+        x, q, s, b = BI.cfg2_int8_convrot(M, K, N, seed=0)
         state = {"rows": M}
         step = lambda: cpu_reference_step(x, q, s, b, state["rows"])  # noqa: E731
         flops = lambda: 2.0 * state["rows"] * K * N  # noqa: E731
@@ -319,12 +319,10 @@ def int8_peak_tops(dev):
 
 
 def _w4a8_case(m, k, n, bits, grp, g, dev):
-    from oracle import qlin_oracle as O
     x = torch.randn(m, k, generator=g).to(torch.float16).to(dev)
     lo, hi = (-8, 8) if bits == 4 else (-32, 32)
-    wq = torch.randint(lo, hi, (n, k), generator=g, dtype=torch.int32).numpy().astype(np.int8)
-    packed = O.pack_w4_uniform(wq) if bits == 4 else O.pack_w6_interleaved(wq)
-    w = torch.from_numpy(packed.view(np.uint8).copy()).to(dev)
+    wq = torch.randint(lo, hi, (n, k), generator=g, dtype=torch.int32)
+    w = (BI.pack_w4(wq) if bits == 4 else BI.pack_w6(wq)).to(dev)
     s = (torch.randn(n, k // grp, generator=g).abs() * 0.02 / (7 if bits == 4 else 31)).to(torch.float16).to(dev)
     return x, w, s
 
@@ -333,12 +331,11 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
     """Every other weight format at the same (M, K, N), and the other benchmark configurations:
     device TFLOP/s (TOPS for the int8 tensor path) and roofline fractions."""
     import qlin
-    from oracle import qlin_oracle as O
     out, cfgs = {}, {}
     g = torch.Generator().manual_seed(1)
     x = torch.randn(M, K, generator=g).to(torch.float16).to(dev)
-    for qt, name in sorted((qt, "gguf_" + v[0].lower()) for qt, v in O.GGUF_TYPES.items()):
-        raw = torch.from_numpy(O.random_gguf_blocks(qt, N, K, seed=qt)).to(dev)
+    for qt, name in sorted((qt, "gguf_" + v[0].lower()) for qt, v in BI.GGUF_TYPES.items()):
+        raw = torch.from_numpy(BI.gguf_blocks(qt, N, K, seed=qt)).to(dev)
         packed, _ = qlin.repack_gguf(raw, qt, (N, K))
         fn = lambda: qlin.gguf_linear(x, raw, qt, (N, K))  # noqa: E731
         t = statistics.mean(timed_steps(fn, steps, warmup, flush, stream))
@@ -357,7 +354,7 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
                      "bound": "tensor (kind::i8, measured int8 peak)"}
     # The other benchmark configurations (reported for completeness; the headline is configuration 2).
     for qt, name in ((8, "cfg1_gguf_q8_0_256x3072x3072"), (2, "cfg1_gguf_q4_0_256x3072x3072")):
-        xs, raw_np = O.cfg_gguf(256, 3072, 3072, qtype=qt, seed=0)
+        xs, raw_np = BI.cfg1_gguf(256, 3072, 3072, qtype=qt, seed=0)
         xs = xs.to(dev)
         raw = torch.from_numpy(raw_np).to(dev)
         fn = lambda: qlin.gguf_linear(xs, raw, qt, (3072, 3072))  # noqa: E731
@@ -379,7 +376,7 @@ def format_sweep(dev, steps, warmup, flush, stream, pk, int8_peak):
     small = [(8, 3072, 3072, m, f"cfg1_small_gguf_q8_0_{m}x3072x3072") for m in (1, 16, 64)]
     small += [(12, 3072, 12288, 1, "small_m_gguf_q4_k_1x3072x12288"), (2, 3072, 3072, 1, "small_m_gguf_q4_0_1x3072x3072")]
     for qt, k, n, m, name in small:
-        xs, raw_np = O.cfg_gguf(m, k, n, qtype=qt, seed=0)
+        xs, raw_np = BI.cfg1_gguf(m, k, n, qtype=qt, seed=0)
         xs = xs.to(dev)
         raw = torch.from_numpy(raw_np).to(dev)
         fn = lambda: qlin.gguf_linear(xs, raw, qt, (n, k))  # noqa: E731
@@ -606,12 +603,11 @@ def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
 
 def run_ours(args, rank, world):
     import qlin
-    from oracle import qlin_oracle as O
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
     pk = peaks()
-    x, q, s, b = O.cfg_int8_convrot(M, K, N, seed=rank)
+    x, q, s, b = BI.cfg2_int8_convrot(M, K, N, seed=rank)
     xd, qd, sd, bd = x.to(dev), q.to(dev), s.to(dev), b.to(dev)
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
@@ -621,7 +617,8 @@ def run_ours(args, rank, world):
     y = step()
     torch.cuda.synchronize()
     # parity before timing on rows from every token tile (61 apart, the last row of every 192-row
-    # span, the last row), all output channels, against the float64 oracle
+    # span, the last row), all output channels, against the float64 oracle (the checker)
+    from oracle import qlin_oracle as O
     rows = sorted(set(range(0, M, 61)) | set(range(191, M, 192)) | {M - 1})
     ref = O.int8_convrot_linear_ref(x[rows].float().numpy(), q.numpy(), s.float().numpy(), b.float().numpy(),
                                     group=GROUP)
@@ -725,7 +722,7 @@ def run_ours(args, rank, world):
         # transient int8 grid, then the INT8 GEMM; against the GEMM on an already decoded grid
         for bits, name in ((4, "kitchen_w4a8_cb_g16"), (6, "kitchen_w6a8_g16")):
             codes = torch.randint(0, 1 << bits, (N, K), generator=gl, dtype=torch.int64)
-            qdata = torch.from_numpy(O.pack_codes_kitchen(codes.numpy(), bits).view(np.int8).copy()).to(dev)
+            qdata = BI.pack_kitchen(codes, bits).to(dev)
             s_rel = (torch.rand(N, K // 16, generator=gl) * 12 + 2).to(torch.float8_e4m3fn).to(dev)
             s_ch = (torch.rand(N, generator=gl) * 1e-3 + 1e-4).to(dev)
             cb = (torch.sort(torch.randn(16, generator=gl)).values * 3).to(dev) if bits == 4 else None

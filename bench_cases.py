@@ -10,6 +10,7 @@ Synthetic seeded inputs with the configurations' shapes and value distributions:
   cfg3                    W4A8, X [4096, 12288], W 4-bit [3072, 12288], group 128
   cfg4_fwd / cfg4_rev     W6A8, X [3240, 5120] / [3240, 13824], W 6-bit, group 64
   cfg5_q4k / cfg5_q6k     MMDiT-block GGUF linears, X [4608, 3072] / [4608, 12288]
+  kitchen_w4a8 / _w6a8    kitchen layouts at the configuration-2 shape (grid decoded per call)
   small_q8_0_m1 / _m16 / _m64   the small-M path: Q8_0 [3072, 3072] with M = 1 / 16 / 64 tokens
   small_q4k_m1            the small-M path: Q4_K [12288, 3072], M = 1
 """
@@ -70,6 +71,23 @@ def build(name, dev):
         dy = torch.randn(m, n, generator=gen).to(torch.float16).to(dev)
         qlin.int8_linear_grad_input(dy, q, s, True, 128)  # the one-time transposed weight copy
         return (lambda: qlin.int8_linear_grad_input(dy, q, s, True, 128)), 2.0 * m * k * n
+    if name in ("kitchen_w4a8", "kitchen_w6a8"):
+        # the kitchen layouts at the configuration-2 shape: codes decoded per call to the int8 grid
+        m, k, n = 4096, 3072, 12288
+        bits = 4 if name == "kitchen_w4a8" else 6
+        x = torch.randn(m, k, generator=gen).to(torch.float16).to(dev)
+        u = torch.randint(0, 1 << bits, (n, k), generator=gen, dtype=torch.int32)
+        # planar kitchen packing: K/2 nibble bytes (even column low), then for 6 bits K/4 bytes of
+        # 2-bit high planes (column 4j+i at bits 2i..2i+1 of byte j)
+        planes = [(u[:, 0::2] & 0xF) | ((u[:, 1::2] & 0xF) << 4)]
+        if bits == 6:
+            planes.append(sum(((u[:, j::4] >> 4) & 3) << (2 * j) for j in range(4)))
+        qdata = torch.cat(planes, dim=1).to(torch.uint8).view(torch.int8).to(dev)
+        s_rel = (torch.rand(n, k // 16, generator=gen) * 12 + 2).to(torch.float8_e4m3fn).to(dev)
+        s_ch = (torch.rand(n, generator=gen) * 1e-3 + 1e-4).to(dev)
+        cb = (torch.sort(torch.randn(16, generator=gen)).values * 3).to(dev) if bits == 4 else None
+        return (lambda: qlin.w4a8_int8_linear(x, qdata, s_rel, s_ch, cb, None, None, 16, 128, torch.float16)), \
+            2.0 * m * k * n
     m, k, n, bits, grp = {"cfg3": (4096, 12288, 3072, 4, 128), "cfg4_fwd": (3240, 5120, 13824, 6, 64),
                           "cfg4_rev": (3240, 13824, 5120, 6, 64)}[name]
     x = torch.randn(m, k, generator=gen).to(torch.float16).to(dev)

@@ -1217,6 +1217,57 @@ __global__ void kitchen_grid_kernel(const uint8_t* __restrict__ q, const uint8_t
   *reinterpret_cast<uint4*>(out + (long long)row * K + c0) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// The same grid for K a multiple of 32 (8-byte aligned code rows), 32 values of a row per thread:
+// 16 code bytes, 8 high-plane bytes for 6 bits and one or two scale bytes in, two 16-byte stores
+// out.  rint + clamp become one round-to-nearest-even float -> int conversion of the clamped
+// product (clamping first gives the same integers: both give +-127 whenever |x| >= 127.5).  Uniform
+// levels (no codebook) are computed, not looked up.  (Two 32-value chunks per thread, with the
+// loads of both issued first, measured ~10 % slower.)
+template <int BITS, bool CB>
+__global__ void __launch_bounds__(256) kitchen_grid32_kernel(const uint8_t* __restrict__ q,
+                                                             const uint8_t* __restrict__ s_rel,
+                                                             const float* __restrict__ codebook, int group, int N,
+                                                             int K, int8_t* __restrict__ out) {
+  constexpr int kLevels = 1 << BITS;
+  __shared__ float levels[kLevels];
+  if (CB && threadIdx.x < kLevels) levels[threadIdx.x] = codebook[threadIdx.x];
+  if (CB) __syncthreads();
+  const int gpr = K / 32;
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (long long)N * gpr) return;
+  const int row = (int)(t / gpr), c0 = (int)(t - (long long)row * gpr) * 32;
+  const long long pitch = (long long)K * BITS / 8;
+  const uint8_t* qr = q + row * pitch;
+  if (!qchk_span(BS_KITCHEN, row * pitch + c0 / 2, 16, (long long)N * pitch) ||
+      (BITS == 6 && !qchk_span(BS_KITCHEN, row * pitch + K / 2 + c0 / 4, 8, (long long)N * pitch)) ||
+      !qchk_span(BS_KITCHEN, (long long)row * (K / group) + c0 / group, group == 16 ? 2 : 1,
+                 (long long)N * (K / group)) ||
+      !qchk_span(BS_KITCHEN, (long long)row * K + c0, 32, (long long)N * K))
+    return;
+  const uint2 lo0 = *reinterpret_cast<const uint2*>(qr + c0 / 2);
+  const uint2 lo1 = *reinterpret_cast<const uint2*>(qr + c0 / 2 + 8);
+  const uint32_t lw[4] = {lo0.x, lo0.y, lo1.x, lo1.y};
+  uint2 hi = make_uint2(0u, 0u);
+  if (BITS == 6) hi = *reinterpret_cast<const uint2*>(qr + K / 2 + c0 / 4);
+  const long long sbase = (long long)row * (K / group) + c0 / group;
+  const float sc0 = e4m3_to_float(s_rel[sbase]);
+  const float sc1 = group == 16 ? e4m3_to_float(s_rel[sbase + 1]) : sc0;
+  uint32_t w[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) w[j] = 0u;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    uint32_t code = (lw[i >> 3] >> (4 * (i & 7))) & 0xF;
+    if (BITS == 6) code |= (((i < 16 ? hi.x : hi.y) >> (2 * (i & 15))) & 3) << 4;
+    const float lv = CB ? levels[code] : (float)((int)code - kLevels / 2);
+    const float v = fminf(fmaxf(__fmul_rn(lv, i < 16 ? sc0 : sc1), -127.f), 127.f);
+    w[i >> 2] |= ((uint32_t)__float2int_rn(v) & 0xFFu) << (8 * (i & 3));
+  }
+  uint4* o = reinterpret_cast<uint4*>(out + (long long)row * K + c0);
+  o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 // ---------------------------------------------------------------------------------------------
 // Fused-LoRA operands (bf16): T'[m][r] = t[m][r] * 2^-f[m] (the activation's row exponent, so the
 // GEMM epilogue's 2^f restores t) and U'[n][r] = up[n][r] * scale / cs[n] (the column scale the
@@ -1410,6 +1461,19 @@ void launch_splitk_finalize(const float* partial, int splits, int M, int N, int 
 
 void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* codebook, int bits, int group, int N,
                          int K, int8_t* out, cudaStream_t s) {
+  if (K % 32 == 0 && (group == 16 || group % 32 == 0) && (bits == 4 || (K * 3 / 4) % 8 == 0)) {
+    const long long threads = (long long)N * (K / 32);
+    if (threads == 0) return;
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    if (bits == 4) {
+      if (codebook) kitchen_grid32_kernel<4, true><<<blocks, 256, 0, s>>>(q, s_rel, codebook, group, N, K, out);
+      else kitchen_grid32_kernel<4, false><<<blocks, 256, 0, s>>>(q, s_rel, codebook, group, N, K, out);
+    } else {
+      if (codebook) kitchen_grid32_kernel<6, true><<<blocks, 256, 0, s>>>(q, s_rel, codebook, group, N, K, out);
+      else kitchen_grid32_kernel<6, false><<<blocks, 256, 0, s>>>(q, s_rel, codebook, group, N, K, out);
+    }
+    return;
+  }
   const long long threads = (long long)N * (K / 16);
   if (threads == 0) return;
   kitchen_grid_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(q, s_rel, codebook, bits, group, N, K, out);

@@ -105,3 +105,23 @@ def test_grid_and_linear_at_checkpoint_widths(qlin, bits, codebook, n, k):
                               torch.from_numpy(s_rel).view(torch.float8_e4m3fn).cuda(),
                               torch.from_numpy(s_ch).cuda(), cb_t, None, None, 16, 256)
     assert O.max_abs_rel(y.float().cpu().numpy(), ref) <= 2e-3
+
+
+@pytest.mark.parametrize("bits,k,group,codebook", [(4, 48, 16, True), (4, 96, 32, False), (6, 64, 16, False),
+                                                   (6, 96, 32, False), (4, 1024, 16, False), (6, 1024, 64, False)])
+def test_grid_every_scale_code_and_both_kernels(qlin, bits, k, group, codebook):
+    """Every finite e4m3 group-scale code (subnormals, +-448, negative scales) and codes over the full
+    range, through both grid kernels (32 values per thread when K is a multiple of 32 and the group 16
+    or a multiple of 32, else 16 per thread): bit-identical with the oracle."""
+    rng = np.random.default_rng(bits * 1000 + k + group)
+    n = 37
+    codes = rng.integers(0, 1 << bits, size=(n, k))
+    q = O.pack_codes_kitchen(codes, bits)
+    finite = np.array([b for b in range(256) if (b & 0x7F) != 0x7F], dtype=np.uint8)
+    s_rel = rng.choice(finite, size=(n, k // group)).astype(np.uint8)
+    cb = np.sort(rng.uniform(-8, 8, 16)).astype(np.float32) if codebook else None
+    from qlin._w4a8 import kitchen_grid
+    grid = kitchen_grid(torch.from_numpy(q).cuda(), torch.from_numpy(s_rel).view(torch.float8_e4m3fn).cuda(),
+                        None if cb is None else torch.from_numpy(cb).cuda(), group)
+    want = O.kitchen_int8_grid(q, s_rel, k, bits, group, cb)
+    assert np.array_equal(grid.cpu().numpy(), want)

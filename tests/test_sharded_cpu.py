@@ -42,7 +42,9 @@ def _worker(rank, world, port, q, gather):
                           weights=_weights_dense, gather=gather)
         outs = st.forward(x)
         y = torch.cat([torch.cat(list(o.float()), dim=1) for o in outs], dim=0)  # [tokens, hidden]
-        q.put((rank, y))
+        # a numpy copy pickles by value: a torch tensor would be passed as a file descriptor that
+        # the parent fetches from this process, which may have exited by then
+        q.put((rank, y.numpy().copy()))
     finally:
         dist.destroy_process_group()
 
@@ -78,7 +80,7 @@ def test_two_rank_sharded_stack_matches_dense(gather):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q, gather)) for r in range(2)]
     for p in procs:
         p.start()
-    got = dict(q.get(timeout=120) for _ in procs)
+    got = {r: torch.from_numpy(y) for r, y in (q.get(timeout=120) for _ in procs)}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
