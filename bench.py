@@ -571,7 +571,10 @@ def run_mmdit(args, world, dev, flush, stream, steps, warmup, clk=None):
             "nccl_allgather_gbs_per_rank_in": gbytes / (t_comm * 1e-3) / 1e9 if t_comm > 0 else None,
             "nvlink_floor_ms": gbytes / 770e9 * 1e3,
             "tensor_floor_ms": st.flops() / world / (peaks()["tflops"] * 1e12) * 1e3,
-            "limiter": "nvlink" if gbytes / 770e9 * 1e3 > t_comp else "compute",
+            # measured, not floors: compute when the stack runs within 10 % of its GEMMs alone; else the
+            # NVLink floor when that is above the GEMMs; else the exchange and its cross-rank waits
+            "limiter": ("compute" if ms <= 1.1 * t_comp else
+                        "nvlink" if gbytes / 770e9 * 1e3 > t_comp else "exchange (not hidden behind the GEMMs)"),
             "note": "compute = this rank's shard linears of every block back to back on resident inputs of their "
                     "shapes (no collective in that workload); comm = NCCL all-gathers of the forward's sizes back "
                     "to back; nvlink floor = bytes each rank receives / 770 GB/s (measured peer copy)"}
