@@ -324,6 +324,138 @@ __global__ void __launch_bounds__(512) prologue_reg_kernel(const void* __restric
 }
 
 // ---------------------------------------------------------------------------------------------
+// Per-token int8 codes of fp16 / bf16 rows without rotation (the A8 activations of the W4A8 /
+// W6A8 linears and quantize_int8_rowwise).  The codes are those of prologue_reg_kernel<E, 1, ..>,
+// with about a quarter of its instructions per value and half its registers, so that several rows
+// are in flight per SM and the pass streams at HBM rate:
+//  * each thread keeps its NV 16-byte vectors (8 values each) of the row in registers as loaded;
+//  * the row maximum is taken on packed pairs (max.f16x2 / max.bf16x2 return the non-NaN operand,
+//    as fmaxf does);
+//  * x / s, the correctly rounded fp32 quotient, comes from Markstein's correction (P. Markstein,
+//    IBM J. Res. Dev. 34(1), 1990): y = RN(1/s) once per row, then q0 = RN(x*y), r = x - s*q0 (one
+//    fma, exact) and q = RN(q0 + r*y), two values per packed fp32 instruction.  Over every fp16 /
+//    bf16 pair that a row can hold (|x| <= 256 s, s >= RN(1e-30)) this equals RN(x/s) wherever
+//    |x/s| >= 1/16 and gives the same code everywhere (tests/quotient_check.c checks every pair);
+//    a row with s > 1e37 (an infinite maximum) divides;
+//  * the quotient is rounded to the input dtype two at a time, clamped to [-128, 127] there and
+//    rounded half-to-even to an integer by adding 1.5 * 2^10 in fp16 (spacing 1 on [1024, 2048))
+//    or 1.5 * 2^23 in fp32 (bf16 rows): the low byte of the sum's bits is the two's-complement code.
+// ---------------------------------------------------------------------------------------------
+template <bool BF16>
+__device__ __forceinline__ uint32_t max2_bits(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (BF16) asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+template <bool BF16>
+__device__ __forceinline__ float bits_lo_f32(uint32_t w) {
+  if constexpr (BF16) return __uint_as_float(w << 16);
+  else return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
+}
+
+template <bool BF16>
+__device__ __forceinline__ float bits_hi_f32(uint32_t w) {
+  if constexpr (BF16) return __uint_as_float(w & 0xFFFF0000u);
+  else return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+
+// (a, b) <- (RN(a/s), RN(b/s)) by Markstein's correction; y = RN(1/s), ns = -s.
+__device__ __forceinline__ void div2_markstein(float& a, float& b, float y, float ns) {
+  asm("{\n\t.reg .b64 x, q, r, yy, nn;\n\t"
+      "mov.b64 x, {%0, %1};\n\t"
+      "mov.b64 yy, {%2, %2};\n\t"
+      "mov.b64 nn, {%3, %3};\n\t"
+      "mul.rn.f32x2 q, x, yy;\n\t"
+      "fma.rn.f32x2 r, q, nn, x;\n\t"
+      "fma.rn.f32x2 q, r, yy, q;\n\t"
+      "mov.b64 {%0, %1}, q;\n\t}"
+      : "+f"(a), "+f"(b)
+      : "f"(y), "f"(ns));
+}
+
+// Codes of two quotients: byte 0 holds a's, byte 2 b's.
+template <bool BF16>
+__device__ __forceinline__ uint32_t codes2(float a, float b) {
+  uint32_t h, d;
+  if constexpr (BF16) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(h), "r"(0xC300C300u));  // -128
+    asm("min.bf16x2 %0, %0, %1;" : "+r"(d) : "r"(0x42FE42FEu));          // 127
+    const uint32_t ca = __float_as_uint(__fadd_rn(__uint_as_float(d << 16), 12582912.f));
+    const uint32_t cb = __float_as_uint(__fadd_rn(__uint_as_float(d & 0xFFFF0000u), 12582912.f));
+    return __byte_perm(ca, cb, 0x0400);
+  } else {
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(h), "r"(0xD800D800u));  // -128
+    asm("min.f16x2 %0, %0, %1;" : "+r"(d) : "r"(0x57F057F0u));          // 127
+    asm("add.rn.f16x2 %0, %0, %1;" : "+r"(d) : "r"(0x66006600u));       // + 1536
+    return d;
+  }
+}
+
+template <int NV, bool BF16>
+__global__ void __launch_bounds__(512) quant_rows16_kernel(const uint16_t* __restrict__ x, long long ldx, int M,
+                                                           int K, int Kp, int8_t* __restrict__ out,
+                                                           float* __restrict__ row_scale, int perm) {
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  if (!qchk(BS_PRO_X, row, M)) return;  // the whole block: row is uniform
+  const int nvec = K >> 3, nvp = Kp >> 3;
+  const uint16_t* xr = x + (long long)row * ldx;
+  uint4 v[NV];
+  uint32_t mx = 0u;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = threadIdx.x + i * blockDim.x;
+    v[i] = (j < nvec) ? __ldcs(reinterpret_cast<const uint4*>(xr) + j) : make_uint4(0u, 0u, 0u, 0u);
+    mx = max2_bits<BF16>(mx, v[i].x & 0x7FFF7FFFu);
+    mx = max2_bits<BF16>(mx, v[i].y & 0x7FFF7FFFu);
+    mx = max2_bits<BF16>(mx, v[i].z & 0x7FFF7FFFu);
+    mx = max2_bits<BF16>(mx, v[i].w & 0x7FFF7FFFu);
+  }
+  const float amax = block_max(fmaxf(bits_lo_f32<BF16>(mx), bits_hi_f32<BF16>(mx)), red);
+  const float scale = fmaxf(__fdiv_rn(amax, 127.f), 1e-30f);
+  float s = BF16 ? __bfloat162float(__float2bfloat16_rn(scale)) : __half2float(__float2half_rn(scale));
+  if (s == 0.f) s = BF16 ? 1.17549435e-38f : 6.103515625e-05f;
+  if (threadIdx.x == 0) row_scale[row] = scale;
+  const bool fast = s <= 1e37f;
+  const float y = __frcp_rn(s), ns = -s;
+  int8_t* o = out + (long long)row * Kp;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = threadIdx.x + i * blockDim.x;
+    if (j < nvp) {
+      const uint32_t in[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      uint32_t w[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        float a = bits_lo_f32<BF16>(in[p]), b = bits_hi_f32<BF16>(in[p]);
+        if (fast) {
+          div2_markstein(a, b, y, ns);
+        } else {
+          a = __fdiv_rn(a, s);
+          b = __fdiv_rn(b, s);
+        }
+        w[p] = codes2<BF16>(a, b);
+      }
+      uint32_t lo, hi;
+      if (perm) {  // even columns first within the group of 8
+        const uint32_t e = __byte_perm(w[0], w[1], 0x6240), f = __byte_perm(w[2], w[3], 0x6240);
+        lo = __byte_perm(e, f, 0x5410);
+        hi = __byte_perm(e, f, 0x7632);
+      } else {
+        lo = __byte_perm(w[0], w[1], 0x6420);
+        hi = __byte_perm(w[2], w[3], 0x6420);
+      }
+      if (qchk_span(BS_PRO_OUT, (long long)row * Kp + 8 * j, 8, (long long)M * Kp))
+        *reinterpret_cast<uint2*>(o + 8 * j) = make_uint2(lo, hi);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // GGUF decode-only: one thread per 4 consecutive values of the flat tensor (blocks are indexed
 // by flat element, so rows may straddle blocks).  fp32 results are bit-exact with gguf-py.
 // ---------------------------------------------------------------------------------------------
@@ -1355,6 +1487,30 @@ int launch_prologue(const void* x, int x_dtype, long long ldx, int M, int K, int
       case 256: E = 8; kind = 1; break;
       default: return -1;
     }
+  }
+  // Unrotated int8 codes of fp16 / bf16 rows: the packed quantizer when the rows are 16-byte
+  // vectors and one CTA of at most 512 threads holds a row in 8 vectors per thread or fewer.
+  if (mode == 1 && !rotate && (x_dtype == 1 || x_dtype == 2) && K % 8 == 0 && Kp % 8 == 0 && Kp <= 32768 &&
+      ((reinterpret_cast<uintptr_t>(x) | (uintptr_t)(ldx * 2)) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 7) == 0) {
+    const int nvp = Kp / 8;
+    const int nv = nvp <= 512 ? 1 : nvp <= 1024 ? 2 : nvp <= 2048 ? 4 : 8;
+    const int threads = ((nvp + nv - 1) / nv + 31) / 32 * 32;
+    const uint16_t* xs = reinterpret_cast<const uint16_t*>(x);
+    int8_t* o = reinterpret_cast<int8_t*>(out);
+#define QLIN_Q16(NV)                                                                                  \
+  do {                                                                                                \
+    if (x_dtype == 2) quant_rows16_kernel<NV, true><<<M, threads, 0, stream>>>(xs, ldx, M, K, Kp, o, row_scale, perm); \
+    else quant_rows16_kernel<NV, false><<<M, threads, 0, stream>>>(xs, ldx, M, K, Kp, o, row_scale, perm); \
+  } while (0)
+    switch (nv) {
+      case 1: QLIN_Q16(1); break;
+      case 2: QLIN_Q16(2); break;
+      case 4: QLIN_Q16(4); break;
+      default: QLIN_Q16(8); break;
+    }
+#undef QLIN_Q16
+    return 0;
   }
   // Tuning knob: QLIN_FWHT_PROLOGUE=1 keeps the shuffle-butterfly rotation for comparisons.
   static const bool fwht_only = getenv("QLIN_FWHT_PROLOGUE") != nullptr;

@@ -277,6 +277,62 @@ def test_quantize_rows_int8_bit_exact(qlin, x_dtype):
     assert np.array_equal(qp.cpu().numpy()[:, :k], want)
 
 
+def _quant_edge_rows(x_dtype, k, seed):
+    """Rows that probe the quantizer's rounding: exact ties and their neighbours, scales in the
+    subnormal range and below it (the divisor replaced by the smallest normal), the dtype's
+    extremes, zeros, and random rows over eleven decades; plus one row with +inf and one with a NaN."""
+    g = torch.Generator().manual_seed(seed)
+    m = 24
+    x = torch.randn(m, k, generator=g) * torch.logspace(-5, 5, m)[:, None]
+    x[0] = 0
+    # quotients exactly n + 0.5: s = 0.125 (row maximum 127 / 8), values (2n + 1) / 16
+    ties = (torch.arange(-127, 127).float() + 0.5) * 0.125
+    x[1] = ties[torch.arange(k) % ties.numel()]
+    x[1, k // 2] = 15.875
+    xt = x[1].to(x_dtype)
+    nxt = (xt.view(torch.int16) + 1).view(x_dtype)  # the neighbour one unit further from zero
+    x[2] = torch.where(torch.arange(k) % 2 == 0, nxt.float(), xt.float())
+    x[2, k // 2] = 15.875
+    tiny = 1e-5 if x_dtype == torch.float16 else 1e-34
+    x[3] = torch.randn(k, generator=g) * tiny  # divisor in the fp16 subnormal range / near bf16's floor
+    x[4] = torch.randn(k, generator=g) * tiny * 0.01  # fp16: divisor rounds to zero -> smallest normal
+    big = 65504.0 if x_dtype == torch.float16 else 3.3e38
+    x[5] = torch.randn(k, generator=g).clamp(-1, 1) * big
+    x[5, 3] = big
+    x = x.to(x_dtype)
+    x[6, 5] = float("inf")
+    x[7, 9 % k] = float("nan")
+    return x
+
+
+@pytest.mark.parametrize("x_dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("k", [8, 1004, 1536, 5120, 12288, 13824, 32768, 40000])
+def test_quantize_rows_int8_edge_rows(qlin, x_dtype, k):
+    """Packed quantizer (K a multiple of 8 up to 32768) and the general one (other K), both perms,
+    contiguous and strided rows: codes and scales equal to the oracle's.  Rows holding inf or NaN
+    follow fmaxf: the row maximum ignores a NaN, an element that is NaN or inf / inf gets -128."""
+    x = _quant_edge_rows(x_dtype, k, seed=k)
+    m = x.shape[0]
+    # the row maximum ignores a NaN; a NaN element, and inf / inf in a row whose maximum is inf
+    # (fp16 rows scaled past 65504 hold several), get -128
+    q_ref, s_ref = O.quantize_int8_rowwise(torch.nan_to_num(x, nan=0.0, posinf=float("inf"), neginf=float("-inf")))
+    q_ref = q_ref.numpy().copy()
+    s_ref = s_ref.numpy().copy()
+    q_ref[~torch.isfinite(x).numpy()] = -128
+    wide = torch.zeros(m, k + 16, dtype=x_dtype)
+    wide[:, 8:8 + k] = x
+    for xd in (x.cuda(), wide.cuda()[:, 8:8 + k]):  # contiguous; rows 16-byte aligned with ldx = k + 16
+        q, s = qlin.quantize_int8_rowwise(xd)
+        assert np.array_equal(q.cpu().numpy(), q_ref)
+        assert np.array_equal(s.cpu().numpy(), s_ref)
+        qp, _ = qlin.quantize_int8_rowwise(xd, perm=True)
+        if k % 8 == 0:
+            perm = np.array([0, 2, 4, 6, 1, 3, 5, 7])
+            want = q_ref.reshape(m, -1, 8)[:, :, perm].reshape(m, -1)
+            assert np.array_equal(qp.cpu().numpy()[:, :k], want)
+    _check_status(qlin)
+
+
 def test_int8_linear_streamed_from_host_memory(qlin):
     """Host activations in, host outputs out, copies overlapped in chunks: the same rows as the
     device path (per-row prologue, no K split at this shape)."""
