@@ -1349,12 +1349,62 @@ __global__ void kitchen_grid_kernel(const uint8_t* __restrict__ q, const uint8_t
   *reinterpret_cast<uint4*>(out + (long long)row * K + c0) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Uniform levels, two values at a time in fp16, exactly: the codes go under the fp16 magic exponent
+// (0x64XX is 1024 + XX), lose their offset (1024 + 8 or 1024 + 32), are multiplied by the e4m3
+// scale and clamped to [-127, 127]; every product is exact in fp16 (a level of at most 6 bits times
+// a 4-bit significand, |v| <= 14336, nonzero |v| >= 2^-9), so this equals the fp32 product of the
+// reference.  Adding 1.5 * 2^10 then rounds half-to-even to an integer (fp16 spacing 1 on
+// [1024, 2048)) and leaves the two's-complement code in the low byte of each half.
+// p: two codes as (1024 + code) fp16 pairs; s: the scale as an fp16 pair.
+template <int BITS>
+__device__ __forceinline__ uint32_t kitchen_uniform2(uint32_t p, uint32_t s) {
+  constexpr uint32_t kOff = BITS == 4 ? 0x64086408u : 0x64206420u;  // 1024 + 8 / 1024 + 32
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(p), "r"(kOff));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(d) : "r"(s));
+  asm("max.f16x2 %0, %0, %1;" : "+r"(d) : "r"(0xD7F0D7F0u));  // -127
+  asm("min.f16x2 %0, %0, %1;" : "+r"(d) : "r"(0x57F057F0u));  // 127
+  asm("add.rn.f16x2 %0, %0, %1;" : "+r"(d) : "r"(0x66006600u));  // + 1536
+  return d;
+}
+
+// Packed fp32 (a.x * s, a.y * s) and (a.x + c, a.y + c), each correctly rounded.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float s) {
+  asm("{\n\t.reg .b64 x, y;\n\t"
+      "mov.b64 x, {%0, %1};\n\t"
+      "mov.b64 y, {%2, %2};\n\t"
+      "mul.rn.f32x2 x, x, y;\n\t"
+      "mov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a.x), "+f"(a.y)
+      : "f"(s));
+  return a;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float c) {
+  asm("{\n\t.reg .b64 x, y;\n\t"
+      "mov.b64 x, {%0, %1};\n\t"
+      "mov.b64 y, {%2, %2};\n\t"
+      "add.rn.f32x2 x, x, y;\n\t"
+      "mov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a.x), "+f"(a.y)
+      : "f"(c));
+  return a;
+}
+
+// 2-bit fields at bits 4k..4k+1 (k = 0..3) of the low 16 bits of h -> bits 8k+4..8k+5: the high
+// planes of four 6-bit codes moved above their nibbles.
+__device__ __forceinline__ uint32_t kitchen_spread_hi(uint32_t h) {
+  const uint32_t y = __byte_perm(h, 0u, 0x4140);  // bytes [h0, 0, h1, 0]
+  return ((y & 0x00030003u) | (((y >> 4) & 0x00030003u) << 8)) << 4;
+}
+
 // The same grid for K a multiple of 32 (8-byte aligned code rows), 32 values of a row per thread:
 // 16 code bytes, 8 high-plane bytes for 6 bits and one or two scale bytes in, two 16-byte stores
-// out.  rint + clamp become one round-to-nearest-even float -> int conversion of the clamped
-// product (clamping first gives the same integers: both give +-127 whenever |x| >= 127.5).  Uniform
-// levels (no codebook) are computed, not looked up.  (Two 32-value chunks per thread, with the
-// loads of both issued first, measured ~10 % slower.)
+// out.  Uniform levels take the packed fp16 form above (about four instructions per value, no
+// conversions); codebook levels are looked up and multiplied in fp32 (packed pairs), clamped, and
+// rounded half-to-even by adding 1.5 * 2^23 (the code is then the low byte of the sum).  Clamping
+// before rounding gives the same integers as rounding first: both give +-127 whenever
+// |x| >= 127.5.  (Two 32-value chunks per thread, with the loads of both issued first, measured
+// ~10 % slower.)
 template <int BITS, bool CB>
 __global__ void __launch_bounds__(256) kitchen_grid32_kernel(const uint8_t* __restrict__ q,
                                                              const uint8_t* __restrict__ s_rel,
@@ -1364,10 +1414,12 @@ __global__ void __launch_bounds__(256) kitchen_grid32_kernel(const uint8_t* __re
   __shared__ float levels[kLevels];
   if (CB && threadIdx.x < kLevels) levels[threadIdx.x] = codebook[threadIdx.x];
   if (CB) __syncthreads();
-  const int gpr = K / 32;
-  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= (long long)N * gpr) return;
-  const int row = (int)(t / gpr), c0 = (int)(t - (long long)row * gpr) * 32;
+  // 32-bit unit index (the launcher keeps N * K / 32 below 2^31): a 64-bit division per thread
+  // is a visible share of this short pass
+  const unsigned gpr = (unsigned)K / 32u;
+  const unsigned t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (unsigned)N * gpr) return;
+  const int row = (int)(t / gpr), c0 = (int)(t - (unsigned)row * gpr) * 32;
   const long long pitch = (long long)K * BITS / 8;
   const uint8_t* qr = q + row * pitch;
   if (!qchk_span(BS_KITCHEN, row * pitch + c0 / 2, 16, (long long)N * pitch) ||
@@ -1385,15 +1437,49 @@ __global__ void __launch_bounds__(256) kitchen_grid32_kernel(const uint8_t* __re
   const float sc0 = e4m3_to_float(s_rel[sbase]);
   const float sc1 = group == 16 ? e4m3_to_float(s_rel[sbase + 1]) : sc0;
   uint32_t w[8];
+  if constexpr (!CB) {
+    const __half h0 = __float2half_rn(sc0), h1 = __float2half_rn(sc1);  // exact: e4m3 values are fp16 values
+    const uint32_t s0 = (uint32_t)__half_as_ushort(h0) * 0x10001u, s1 = (uint32_t)__half_as_ushort(h1) * 0x10001u;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) w[j] = 0u;
+    for (int t = 0; t < 4; ++t) {  // word t: values 8t .. 8t+7 (value 8t+2b in the low nibble of byte b)
+      uint32_t a = lw[t] & 0x0F0F0F0Fu, b = (lw[t] >> 4) & 0x0F0F0F0Fu;  // even / odd values, one per byte
+      if (BITS == 6) {
+        const uint32_t hw = ((t < 2 ? hi.x : hi.y) >> (16 * (t & 1))) & 0xFFFFu;  // value 8t+i at bits 2i..2i+1
+        a |= kitchen_spread_hi(hw);
+        b |= kitchen_spread_hi(hw >> 2);
+      }
+      const uint32_t s = t < 2 ? s0 : s1;
+      const uint32_t ca0 = kitchen_uniform2<BITS>(__byte_perm(a, 0x64646464u, 0x4140), s);  // values 8t, 8t+2
+      const uint32_t ca1 = kitchen_uniform2<BITS>(__byte_perm(a, 0x64646464u, 0x4342), s);  // 8t+4, 8t+6
+      const uint32_t cb0 = kitchen_uniform2<BITS>(__byte_perm(b, 0x64646464u, 0x4140), s);  // 8t+1, 8t+3
+      const uint32_t cb1 = kitchen_uniform2<BITS>(__byte_perm(b, 0x64646464u, 0x4342), s);  // 8t+5, 8t+7
+      w[2 * t] = __byte_perm(ca0, cb0, 0x6240);
+      w[2 * t + 1] = __byte_perm(ca1, cb1, 0x6240);
+    }
+  } else {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    uint32_t code = (lw[i >> 3] >> (4 * (i & 7))) & 0xF;
-    if (BITS == 6) code |= (((i < 16 ? hi.x : hi.y) >> (2 * (i & 15))) & 3) << 4;
-    const float lv = CB ? levels[code] : (float)((int)code - kLevels / 2);
-    const float v = fminf(fmaxf(__fmul_rn(lv, i < 16 ? sc0 : sc1), -127.f), 127.f);
-    w[i >> 2] |= ((uint32_t)__float2int_rn(v) & 0xFFu) << (8 * (i & 3));
+    for (int j = 0; j < 8; ++j) {  // values 4j .. 4j+3
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * j + e;
+        uint32_t code = (lw[i >> 3] >> (4 * (i & 7))) & 0xF;
+        if (BITS == 6) code |= (((i < 16 ? hi.x : hi.y) >> (2 * (i & 15))) & 3) << 4;
+        v[e] = levels[code];
+      }
+      const float sc = j < 4 ? sc0 : sc1;
+      uint32_t c[4];
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        float2 x = mul2_rn(make_float2(v[e], v[e + 1]), sc);
+        x.x = fminf(fmaxf(x.x, -127.f), 127.f);
+        x.y = fminf(fmaxf(x.y, -127.f), 127.f);
+        x = add2_rn(x, 12582912.f);  // 1.5 * 2^23 + rint(v): the code in byte 0
+        c[e] = __float_as_uint(x.x);
+        c[e + 1] = __float_as_uint(x.y);
+      }
+      w[j] = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
+    }
   }
   uint4* o = reinterpret_cast<uint4*>(out + (long long)row * K + c0);
   o[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -1617,7 +1703,8 @@ void launch_splitk_finalize(const float* partial, int splits, int M, int N, int 
 
 void launch_kitchen_grid(const uint8_t* q, const uint8_t* s_rel, const float* codebook, int bits, int group, int N,
                          int K, int8_t* out, cudaStream_t s) {
-  if (K % 32 == 0 && (group == 16 || group % 32 == 0) && (bits == 4 || (K * 3 / 4) % 8 == 0)) {
+  if (K % 32 == 0 && (group == 16 || group % 32 == 0) && (bits == 4 || (K * 3 / 4) % 8 == 0) &&
+      (long long)N * (K / 32) < (1ll << 31)) {
     const long long threads = (long long)N * (K / 32);
     if (threads == 0) return;
     const unsigned blocks = (unsigned)((threads + 255) / 256);
