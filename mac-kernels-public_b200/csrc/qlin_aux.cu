@@ -1391,10 +1391,10 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float c) {
 }
 
 // 2-bit fields at bits 4k..4k+1 (k = 0..3) of the low 16 bits of h -> bits 8k+4..8k+5: the high
-// planes of four 6-bit codes moved above their nibbles.
+// planes of four 6-bit codes moved above their nibbles.  With each field alone in its nibble the
+// fields are byte selectors (0..3) into the table {0x00, 0x10, 0x20, 0x30}: one byte permute.
 __device__ __forceinline__ uint32_t kitchen_spread_hi(uint32_t h) {
-  const uint32_t y = __byte_perm(h, 0u, 0x4140);  // bytes [h0, 0, h1, 0]
-  return ((y & 0x00030003u) | (((y >> 4) & 0x00030003u) << 8)) << 4;
+  return __byte_perm(0x30201000u, 0u, h & 0x3333u);
 }
 
 // The same grid for K a multiple of 32 (8-byte aligned code rows), 32 values of a row per thread:
